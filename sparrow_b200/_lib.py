@@ -1,0 +1,76 @@
+"""ctypes binding of include/vmlm_cuda.h (the library's C ABI)."""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(HERE, "lib", "libvmlm_cuda.so")
+
+STATUS = {
+    0: "VMLM_OK",
+    1: "VMLM_ERR_ARG",
+    2: "VMLM_ERR_SHAPE",
+    3: "VMLM_ERR_CUDA",
+    4: "VMLM_ERR_NO_DEVICE",
+    5: "VMLM_ERR_STATE",
+    6: "VMLM_ERR_OOM",
+    7: "VMLM_ERR_DEVICE_TIMEOUT",
+}
+
+P, S, I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+
+# name -> (restype, argtypes); must list every symbol the header declares.
+SIGNATURES = {
+    "vmlm_version": (I, []),
+    "vmlm_init": (I, [I]),
+    "vmlm_shutdown": (I, []),
+    "vmlm_last_error": (ctypes.c_char_p, []),
+    "vmlm_register_weight": (I, [P, S]),
+    "vmlm_unregister_weight": (I, [P]),
+    "vmlm_unregister_all": (I, []),
+    "vmlm_gemm_nt_int8": (I, [P, P, P, P, S, S, S]),
+    "vmlm_gemm_nt_bf16": (I, [P, P, P, S, S, S]),
+    "vmlm_gemm_i8i8": (I, [P, P, P, P, P, S, S, S]),
+    "vmlm_gemm_nt_int8_dev": (I, [P, P, P, P, S, S, S, P]),
+    "vmlm_gemm_nt_bf16_dev": (I, [P, P, P, S, S, S, P]),
+    "vmlm_gemm_i8i8_dev": (I, [P, P, P, P, P, S, S, S, P]),
+    "vmlm_sync": (I, [P]),
+    "vmlm_launch_count": (ctypes.c_uint64, []),
+}
+
+
+class VmlmError(RuntimeError):
+    """A non-zero status from the C ABI (the reference VM prints and exits 9)."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+
+
+_lib = None
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise ImportError(
+                f"{_LIB_PATH} is missing: build it with `python -m sparrow_b200.build` "
+                "(there is no CPU fallback)")
+        L = ctypes.CDLL(_LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        msg = lib().vmlm_last_error()
+        raise VmlmError(status, msg.decode() if msg else "")

@@ -1,0 +1,564 @@
+// tc_gemm.cuh -- the tcgen05 GEMM used by every fast path of the library.
+//
+// One persistent, warp-specialised kernel computes D = A[rows,K] . B[cols,K]^T
+// with both operands K-major in HBM, staged by TMA (128-byte swizzle, no
+// multicast) through an mbarrier ring, multiplied by tcgen05.mma into a
+// double-buffered TMEM accumulator, and finished by an epilogue that depends
+// on the mode:
+//
+//   kQ8Swap    A = int8 weight rows W[n,:], B = int8 digit planes of the f32
+//              activations (row 3t+p is plane p of token t). kind::i8, s32
+//              accumulators. Epilogue recombines the three planes exactly in
+//              int64, applies the token's power-of-two exponent and scale[n]:
+//              C[t][n] = f32(f64(sum_p 256^p acc_p) * 2^-e_t) * scale[n].
+//   kBf16Swap  A = bf16 weight rows, B = bf16 split terms of the f32
+//              activations (row 3t+j is term j of token t). kind::f16 with f32
+//              accumulators; the epilogue adds the three terms.
+//   kBf16Norm  A = bf16 split terms of the activations laid out term-major
+//              along K (K' = T*K, T read on the device), B = bf16 weight rows.
+//              C[m][n] straight from the accumulator.
+//   kI8Norm    A = int8 activations X[m,:], B = int8 weights W[n,:]:
+//              C[m][n] = f32(acc) * scale[n], and/or the raw int32 acc.
+//
+// Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
+// the MMAs, warps 2..5 are the epilogue (TMEM lanes 32*(warp%4) .. +31).
+//
+// Scheduling is static and deterministic. Units are (tile, k-block) pairs
+// ordered tile-major. With many tiles the CTAs take whole tiles round-robin;
+// otherwise each CTA takes a contiguous range of units (stream-K). A tile
+// split between CTAs is finished by whichever CTA brings the tile's counter to
+// the full k-block count: every contributor stores its raw 32-bit partial in
+// its own slot, and the finisher sums the slots in CTA order, so results do
+// not depend on arrival order (integer sums are exact in any case).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace vmlm {
+
+enum class TcMode : int { kQ8Swap = 0, kBf16Swap = 1, kBf16Norm = 2, kI8Norm = 3 };
+
+constexpr int kTileRows = 128;        // UMMA M
+constexpr int kBlockBytes = 128;      // bytes of K per stage (one 128B swizzle row)
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int kMaxSmem = 227 * 1024;
+
+struct TcParams {
+  int rows;          // extent of A rows (W rows in swap modes, tokens in normal modes)
+  int cols;          // extent of B rows (plane/term rows in swap modes, W rows in normal modes)
+  int bn;            // UMMA N per tile (multiple of 16, <= 256; multiple of 48 in swap modes)
+  int kb_per_term;   // k-blocks per pass over K
+  int max_terms;     // kBf16Norm: term passes allocated in A (1..3); 1 otherwise
+  int tiles_m, tiles_n;
+  int streamk;       // 1 = stream-K ranges, 0 = round-robin whole tiles
+  int tm_fastest;    // tile index -> (tm, tn): 1 = tm varies fastest, 0 = tn fastest
+  int stages;
+  int tmem_cols;     // allocated TMEM columns (power of two >= 2*bn)
+  int a_box_elems;   // TMA box inner extent of A/B in elements (128 int8 or 64 bf16)
+  int term_stride;   // kBf16Norm: element offset between terms along A's K
+  // epilogue
+  float* out;        // C, row-major
+  long long ldo;     // row stride of C (elements)
+  int vec_out;       // C (and acc_out) rows are 16-byte aligned: vector stores allowed
+  int32_t* acc_out;  // kI8Norm: optional raw accumulators (row stride ldo)
+  const float* scale;
+  const int* exps;        // kQ8Swap: per-token exponent e (value = v * 2^-e)
+  const int* nonfinite;   // per-token flag: row of x holds NaN/Inf
+  const int* term_flags;  // kBf16Norm: per-token OR of (1<<j) for nonzero term j
+  int n_tokens;           // tokens (swap modes: real tokens; used for bounds)
+  int tok_per_tile;       // swap modes: tokens per column tile (bn/3)
+  int n_out;              // swap modes: W rows (bounds on n)
+  // non-finite fallback (swap modes): exact f32 recompute of flagged tokens
+  const float* x;
+  long long ldx;
+  const void* w;     // int8 or bf16 weight rows (row stride k)
+  int k;
+  // split-tile fixup
+  uint32_t* slots;   // [2*grid][128][bn] 32-bit partials
+  int* counters;     // [tiles] k-blocks finished so far (self-resetting)
+  int* err;          // device error word
+};
+
+struct TcSmem {
+  uint32_t a_off, b_off, bar_off;  // offsets from the 1024-aligned base
+  uint32_t a_bytes, b_bytes, total;
+};
+
+__host__ __device__ inline TcSmem tc_smem_layout(int stages, int bn) {
+  TcSmem s;
+  s.a_bytes = kTileRows * kBlockBytes;
+  s.b_bytes = static_cast<uint32_t>(bn) * kBlockBytes;
+  s.a_off = 0;
+  s.b_off = s.a_off + stages * s.a_bytes;
+  s.bar_off = s.b_off + stages * s.b_bytes;
+  // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, tmem addr, flags
+  s.total = s.bar_off + (2 * stages + 5) * 8 + 64 + 1024;  // +1024 for base alignment
+  return s;
+}
+
+struct WorkItem {
+  int tile, kb0, kb1;  // k-blocks [kb0, kb1) of the tile (in units of the tile's KB)
+  bool partial;
+};
+
+// Units per tile depend on the number of active terms (kBf16Norm).
+struct Sched {
+  long long units;  // total units
+  int kb_tile;      // k-blocks per tile
+  int tiles;
+  int grid;
+  int streamk;
+
+  __device__ __forceinline__ long long start(int c) const { return (static_cast<long long>(c) * units) / grid; }
+
+  // i-th work item of CTA c; returns false when exhausted.
+  __device__ __forceinline__ bool item(int c, int i, long long& cursor, WorkItem& w) const {
+    if (!streamk) {
+      long long t = static_cast<long long>(c) + static_cast<long long>(i) * grid;
+      if (t >= tiles) return false;
+      w.tile = static_cast<int>(t);
+      w.kb0 = 0;
+      w.kb1 = kb_tile;
+      w.partial = false;
+      return true;
+    }
+    const long long end = start(c + 1);
+    if (i == 0) cursor = start(c);
+    if (cursor >= end) return false;
+    const long long tile = cursor / kb_tile;
+    const int kb0 = static_cast<int>(cursor - tile * kb_tile);
+    long long kb1 = kb0 + (end - cursor);
+    if (kb1 > kb_tile) kb1 = kb_tile;
+    w.tile = static_cast<int>(tile);
+    w.kb0 = kb0;
+    w.kb1 = static_cast<int>(kb1);
+    w.partial = !(kb0 == 0 && kb1 == kb_tile);
+    cursor += kb1 - kb0;
+    return true;
+  }
+
+  // CTA that owns unit u: the largest c with start(c) <= u (every range is
+  // non-empty because the host launches at most `units` CTAs).
+  __device__ __forceinline__ int owner(long long u) const {
+    long long c = (u * grid) / units;
+    if (c > grid - 1) c = grid - 1;
+    while (c > 0 && start(static_cast<int>(c)) > u) --c;
+    while (c + 1 < grid && start(static_cast<int>(c + 1)) <= u) ++c;
+    return static_cast<int>(c);
+  }
+};
+
+__device__ __forceinline__ int active_terms(const TcParams& p) {
+  if (p.max_terms <= 1) return 1;
+  int orv = 0;
+  for (int t = 0; t < p.rows; ++t) orv |= __ldg(p.term_flags + t);
+  int T = 1;
+  if (orv & 2) T = 2;
+  if (orv & 4) T = 3;
+  return T < p.max_terms ? T : p.max_terms;
+}
+
+// ------------------------------------------------------------- epilogues
+
+// Finish 16 columns [col0, col0+16) of one accumulator row in a normal mode.
+template <TcMode MODE>
+__device__ __forceinline__ void epi_norm16(const TcParams& p, int row, int col0, const uint32_t (&v)[16]) {
+  if (row >= p.rows) return;
+  float* crow = p.out ? p.out + static_cast<long long>(row) * p.ldo : nullptr;
+  const bool full = (col0 + 16 <= p.cols) && p.vec_out;
+  if constexpr (MODE == TcMode::kI8Norm) {
+    if (p.acc_out) {
+      int32_t* arow = p.acc_out + static_cast<long long>(row) * p.ldo;
+      if (full) {
+        #pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<int4*>(arow + col0 + j) =
+              make_int4(static_cast<int>(v[j]), static_cast<int>(v[j + 1]), static_cast<int>(v[j + 2]),
+                        static_cast<int>(v[j + 3]));
+      } else {
+        for (int j = 0; j < 16; ++j)
+          if (col0 + j < p.cols) arow[col0 + j] = static_cast<int>(v[j]);
+      }
+    }
+    if (crow) {
+      float f[16];
+      #pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int c = col0 + j;
+        const float s = (c < p.cols) ? __ldg(p.scale + c) : 0.f;
+        f[j] = __fmul_rn(__int2float_rn(static_cast<int>(v[j])), s);
+      }
+      if (full) {
+        #pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+      } else {
+        for (int j = 0; j < 16; ++j)
+          if (col0 + j < p.cols) crow[col0 + j] = f[j];
+      }
+    }
+  } else {
+    if (full) {
+      #pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(crow + col0 + j) =
+            make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                        __uint_as_float(v[j + 3]));
+    } else {
+      for (int j = 0; j < 16; ++j)
+        if (col0 + j < p.cols) crow[col0 + j] = __uint_as_float(v[j]);
+    }
+  }
+}
+
+// Exact f32 recompute of one output for a token whose activations hold NaN or
+// Inf (the digit-plane / split-term encodings cannot carry them). Summation is
+// sequential, which gives the same NaN/Inf classification as any order.
+template <TcMode MODE>
+__device__ float nonfinite_dot(const TcParams& p, int t, int n) {
+  const float* xr = p.x + static_cast<long long>(t) * p.ldx;
+  float s = 0.f;
+  if constexpr (MODE == TcMode::kQ8Swap) {
+    const int8_t* wr = static_cast<const int8_t*>(p.w) + static_cast<long long>(n) * p.k;
+    for (int kk = 0; kk < p.k; ++kk) s = __fadd_rn(s, __fmul_rn(xr[kk], static_cast<float>(wr[kk])));
+    return __fmul_rn(s, __ldg(p.scale + n));
+  } else {
+    const uint16_t* wr = static_cast<const uint16_t*>(p.w) + static_cast<long long>(n) * p.k;
+    for (int kk = 0; kk < p.k; ++kk)
+      s = __fadd_rn(s, __fmul_rn(xr[kk], __uint_as_float(static_cast<uint32_t>(wr[kk]) << 16)));
+    return s;
+  }
+}
+
+// Finish 16 tokens (48 accumulator columns, token-major triples) of one weight
+// row in a swap mode. tok0 is the first token of the chunk.
+template <TcMode MODE>
+__device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, const uint32_t (&v)[48]) {
+  if (n >= p.n_out) return;
+  const float sc = (MODE == TcMode::kQ8Swap) ? __ldg(p.scale + n) : 0.f;
+  #pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int t = tok0 + j;
+    if (t >= p.n_tokens) break;
+    float r;
+    if (__ldg(p.nonfinite + t)) {
+      r = nonfinite_dot<MODE>(p, t, n);
+    } else if constexpr (MODE == TcMode::kQ8Swap) {
+      const long long a0 = static_cast<int>(v[3 * j + 0]);
+      const long long a1 = static_cast<int>(v[3 * j + 1]);
+      const long long a2 = static_cast<int>(v[3 * j + 2]);
+      const long long vsum = a2 * 65536ll + a1 * 256ll + a0;
+      const double d = ldexp(static_cast<double>(vsum), -__ldg(p.exps + t));
+      r = __fmul_rn(__double2float_rn(d), sc);
+    } else {
+      const float hi = __uint_as_float(v[3 * j + 0]);
+      const float mid = __uint_as_float(v[3 * j + 1]);
+      const float lo = __uint_as_float(v[3 * j + 2]);
+      r = __fadd_rn(hi, __fadd_rn(mid, lo));
+    }
+    p.out[static_cast<long long>(t) * p.ldo + n] = r;
+  }
+}
+
+// --------------------------------------------------------------- kernel
+
+template <TcMode MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcParams p) {
+  constexpr bool kSwap = (MODE == TcMode::kQ8Swap || MODE == TcMode::kBf16Swap);
+  constexpr bool kInt = (MODE == TcMode::kQ8Swap || MODE == TcMode::kI8Norm);
+  constexpr uint32_t kMmaPerBlock = 4;  // 128 bytes of K / 32 bytes per UMMA
+  const uint32_t idesc = kInt ? umma_idesc(2, 1, kTileRows, p.bn) : umma_idesc(1, 1, kTileRows, p.bn);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  const TcSmem L = tc_smem_layout(p.stages, p.bn);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty_bar = full_bar + p.stages;
+  uint64_t* tfull_bar = empty_bar + p.stages;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full_bar + s, 1);
+      mbar_init(empty_bar + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar + b, 1);
+      mbar_init(tempty_bar + b, 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Everything below may read what the previous kernel in the stream wrote.
+  pdl_wait_prior();
+
+  const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
+  Sched sc;
+  sc.kb_tile = p.kb_per_term * T;
+  sc.tiles = p.tiles_m * p.tiles_n;
+  sc.units = static_cast<long long>(sc.tiles) * sc.kb_tile;
+  sc.grid = gridDim.x;
+  sc.streamk = p.streamk;
+  const int cta = blockIdx.x;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase = 0;  // per stage: ever issued / parity of last issue
+      long long cur = 0;
+      WorkItem w;
+      bool ok = true;
+      for (int i = 0; ok && sc.item(cta, i, cur, w); ++i) {
+        const int tm = p.tm_fastest ? w.tile % p.tiles_m : w.tile / p.tiles_n;
+        const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + L.a_off + stage * L.a_bytes;
+          uint8_t* sb = smem + L.b_off + stage * L.b_bytes;
+          mbar_arrive_expect_tx(full_bar + stage, L.a_bytes + L.b_bytes);
+          int ka, kbx;
+          if constexpr (MODE == TcMode::kBf16Norm) {
+            const int term = kb / p.kb_per_term, kin = kb % p.kb_per_term;
+            ka = term * p.term_stride + kin * p.a_box_elems;
+            kbx = kin * p.a_box_elems;
+          } else {
+            ka = kb * p.a_box_elems;
+            kbx = ka;
+          }
+          tma_load_2d(sa, &tmA, full_bar + stage, ka, tm * kTileRows, pol_a);
+          tma_load_2d(sb, &tmB, full_bar + stage, kbx, tn * p.bn, pol_b);
+          issued_mask |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Copies already issued must land before this CTA's shared memory is released.
+        for (int s = 0; s < p.stages; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(full_bar + s, (last_phase >> s) & 1u, nullptr, abort_flag, kDevTimeoutDrain, false);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long cur = 0;
+      WorkItem w;
+      bool ok = true;
+      bool issued = false;
+      for (int i = 0; ok && sc.item(cta, i, cur, w); ++i) {
+        const int buf = i & 1;
+        if (!mbar_wait(tempty_bar + buf, ((i >> 1) & 1) ^ 1, p.err, abort_flag, kDevTimeoutAccumFree)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
+          const uint32_t b_addr = smem_u32(smem + L.b_off + stage * L.b_bytes);
+          #pragma unroll
+          for (uint32_t j = 0; j < kMmaPerBlock; ++j) {
+            const uint64_t ad = umma_desc_sw128(a_addr + 32 * j);
+            const uint64_t bd = umma_desc_sw128(b_addr + 32 * j);
+            const uint32_t acc = (kb > w.kb0 || j > 0) ? 1u : 0u;
+            if constexpr (kInt)
+              umma_i8(d_tmem, ad, bd, idesc, acc);
+            else
+              umma_f16(d_tmem, ad, bd, idesc, acc);
+          }
+          issued = true;
+          umma_commit(empty_bar + stage);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar + buf);
+      }
+      if (issued && *abort_flag) {
+        // Let in-flight MMAs finish before TMEM is released.
+        umma_commit(drain_bar);
+        mbar_wait(drain_bar, 0, nullptr, abort_flag, kDevTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // accumulator row within the tile
+    const int ethread = threadIdx.x - 64;  // 0..127
+    long long cur = 0;
+    WorkItem w;
+    for (int i = 0; sc.item(cta, i, cur, w); ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
+      tc_fence_after();
+      const int tm = p.tm_fastest ? w.tile % p.tiles_m : w.tile / p.tiles_n;
+      const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
+      const int grow = tm * kTileRows + row;  // A row (W row in swap modes, token in normal modes)
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
+
+      if (!w.partial) {
+        if constexpr (kSwap) {
+          for (int c = 0; c < p.bn; c += 48) {
+            uint32_t v[48];
+            __syncwarp();
+            tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+            tmem_ld16(tbase + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+            tmem_ld16(tbase + c + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
+            tmem_ld_wait();
+            if (c + 48 >= p.bn) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(tempty_bar + buf);
+            }
+            epi_swap48<MODE>(p, grow, tn * p.tok_per_tile + c / 3, v);
+          }
+        } else {
+          for (int c = 0; c < p.bn; c += 16) {
+            uint32_t v[16];
+            __syncwarp();
+            tmem_ld16(tbase + c, v);
+            tmem_ld_wait();
+            if (c + 16 >= p.bn) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(tempty_bar + buf);
+            }
+            epi_norm16<MODE>(p, grow, tn * p.bn + c, v);
+          }
+        }
+        continue;
+      }
+
+      // Split tile: publish this CTA's partial, then let the last contributor finish.
+      const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
+      const int which = (sc.start(cta) >= tile_u0) ? 0 : 1;
+      uint32_t* myslot = p.slots + (static_cast<long long>(2 * cta + which) * kTileRows + row) * p.bn;
+      for (int c = 0; c < p.bn; c += 16) {
+        uint32_t v[16];
+        __syncwarp();
+        tmem_ld16(tbase + c, v);
+        tmem_ld_wait();
+        #pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          __stcg(reinterpret_cast<uint4*>(myslot + c + j), make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar + buf);
+      __threadfence();
+      named_bar_sync(1, kEpiThreads);
+      if (ethread == 0) {
+        const int done = atomicAdd(p.counters + w.tile, w.kb1 - w.kb0) + (w.kb1 - w.kb0);
+        const int last = (done == sc.kb_tile);
+        if (last) p.counters[w.tile] = 0;  // ready for the next call
+        *bcast = last;
+      }
+      named_bar_sync(1, kEpiThreads);
+      const int last = *bcast;
+      named_bar_sync(1, kEpiThreads);
+      if (!last) continue;
+      __threadfence();
+      const int c_first = sc.owner(tile_u0);
+      const int c_last = sc.owner(tile_u0 + sc.kb_tile - 1);
+      if constexpr (kSwap) {
+        for (int c = 0; c < p.bn; c += 48) {
+          uint32_t v[48];
+          #pragma unroll
+          for (int j = 0; j < 48; ++j) v[j] = 0;
+          for (int q = c_first; q <= c_last; ++q) {
+            const int wq = (sc.start(q) >= tile_u0) ? 0 : 1;
+            const uint32_t* s = p.slots + (static_cast<long long>(2 * q + wq) * kTileRows + row) * p.bn + c;
+            #pragma unroll
+            for (int j = 0; j < 48; j += 4) {
+              const uint4 u = __ldcg(reinterpret_cast<const uint4*>(s + j));
+              if constexpr (kInt) {
+                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
+              } else {
+                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(u.x)));
+                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), __uint_as_float(u.y)));
+                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), __uint_as_float(u.z)));
+                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), __uint_as_float(u.w)));
+              }
+            }
+          }
+          epi_swap48<MODE>(p, grow, tn * p.tok_per_tile + c / 3, v);
+        }
+      } else {
+        for (int c = 0; c < p.bn; c += 16) {
+          uint32_t v[16];
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0;
+          for (int q = c_first; q <= c_last; ++q) {
+            const int wq = (sc.start(q) >= tile_u0) ? 0 : 1;
+            const uint32_t* s = p.slots + (static_cast<long long>(2 * q + wq) * kTileRows + row) * p.bn + c;
+            #pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const uint4 u = __ldcg(reinterpret_cast<const uint4*>(s + j));
+              if constexpr (kInt) {
+                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
+              } else {
+                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(u.x)));
+                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), __uint_as_float(u.y)));
+                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), __uint_as_float(u.z)));
+                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), __uint_as_float(u.w)));
+              }
+            }
+          }
+          epi_norm16<MODE>(p, grow, tn * p.bn + c, v);
+        }
+      }
+    }
+  }
+
+  // Teardown: every role has left its loop (normally or on abort).
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    __syncwarp();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+}  // namespace vmlm

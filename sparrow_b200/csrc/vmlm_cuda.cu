@@ -1,0 +1,628 @@
+// vmlm_cuda.cu -- host side of the C ABI declared in include/vmlm_cuda.h:
+// device contexts, workspace, the weight registry, argument checks, kernel
+// selection and launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "../../include/vmlm_cuda.h"
+#include "prep.cuh"
+#include "tc_gemm.cuh"
+
+using namespace vmlm;
+
+namespace {
+
+thread_local std::string g_err;
+std::recursive_mutex g_mu;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define VMLM_CUDA(x)                                                                                    \
+  do {                                                                                                  \
+    cudaError_t e_ = (x);                                                                               \
+    if (e_ != cudaSuccess)                                                                              \
+      return fail(e_ == cudaErrorMemoryAllocation ? VMLM_ERR_OOM : VMLM_ERR_CUDA, "%s: %s (%s:%d)", #x, \
+                  cudaGetErrorString(e_), __FILE__, __LINE__);                                          \
+  } while (0)
+
+#define VMLM_TRY(x)              \
+  do {                           \
+    int r_ = (x);                \
+    if (r_ != VMLM_OK) return r_; \
+  } while (0)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+// Grow-only device buffer. Growing frees the old buffer (cudaFree waits for
+// the device), so a call that needs more workspace than any earlier call
+// cannot be captured into a CUDA graph.
+int ensure(DevBuf& b, size_t bytes, bool zero = false) {
+  if (bytes == 0) bytes = 16;
+  if (b.bytes >= bytes) return VMLM_OK;
+  size_t nb = b.bytes * 2 > bytes ? b.bytes * 2 : bytes;
+  nb = (nb + 255) & ~static_cast<size_t>(255);
+  if (b.p) VMLM_CUDA(cudaFree(b.p));
+  b.p = nullptr;
+  b.bytes = 0;
+  VMLM_CUDA(cudaMalloc(&b.p, nb));
+  if (zero) VMLM_CUDA(cudaMemset(b.p, 0, nb));
+  b.bytes = nb;
+  return VMLM_OK;
+}
+
+struct Ctx {
+  int dev = -1;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  DevBuf act;       // digit planes / split terms
+  DevBuf small;     // exps | nonfinite | term_flags, each [M] int
+  DevBuf slots;     // split-tile partials
+  DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
+  int* err = nullptr;       // device error word
+  int* err_host = nullptr;  // pinned copy read after host-API calls
+  DevBuf h_a, h_c, h_w, h_s, h_acc;  // host-API staging
+  bool attrs_set = false;
+};
+
+std::map<int, Ctx*> g_ctx;
+int g_host_dev = -1;
+
+struct Reg {
+  size_t bytes;
+  void* dptr;
+  int dev;
+};
+std::map<uintptr_t, Reg> g_reg;
+
+int load_encoder() {
+  if (g_encode) return VMLM_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  VMLM_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (q != cudaDriverEntryPointSuccess || !fn) return fail(VMLM_ERR_CUDA, "cuTensorMapEncodeTiled not available");
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return VMLM_OK;
+}
+
+template <TcMode M>
+int set_smem_attr() {
+  VMLM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  return VMLM_OK;
+}
+
+int get_ctx(int dev, Ctx** out) {
+  auto it = g_ctx.find(dev);
+  if (it != g_ctx.end()) {
+    *out = it->second;
+    return VMLM_OK;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(VMLM_ERR_NO_DEVICE, "no CUDA device");
+  if (dev < 0 || dev >= ndev) return fail(VMLM_ERR_ARG, "device %d out of range (%d devices)", dev, ndev);
+  cudaDeviceProp prop;
+  VMLM_CUDA(cudaGetDeviceProperties(&prop, dev));
+  if (prop.major != 10)
+    return fail(VMLM_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, prop.major,
+                prop.minor);
+  int prev = -1;
+  VMLM_CUDA(cudaGetDevice(&prev));
+  VMLM_CUDA(cudaSetDevice(dev));
+  VMLM_TRY(load_encoder());
+  Ctx* c = new Ctx();
+  c->dev = dev;
+  c->sms = prop.multiProcessorCount;
+  VMLM_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  VMLM_CUDA(cudaMalloc(&c->err, sizeof(int)));
+  VMLM_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+  VMLM_CUDA(cudaHostAlloc(&c->err_host, sizeof(int), cudaHostAllocDefault));
+  *c->err_host = 0;
+  VMLM_TRY(set_smem_attr<TcMode::kQ8Swap>());
+  VMLM_TRY(set_smem_attr<TcMode::kBf16Swap>());
+  VMLM_TRY(set_smem_attr<TcMode::kBf16Norm>());
+  VMLM_TRY(set_smem_attr<TcMode::kI8Norm>());
+  g_ctx[dev] = c;
+  if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+  *out = c;
+  return VMLM_OK;
+}
+
+int current_ctx(Ctx** out) {
+  int dev = -1;
+  VMLM_CUDA(cudaGetDevice(&dev));
+  return get_ctx(dev, out);
+}
+
+int host_ctx(Ctx** out) {
+  if (g_host_dev < 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    g_host_dev = dev;
+  }
+  VMLM_CUDA(cudaSetDevice(g_host_dev));
+  return get_ctx(g_host_dev, out);
+}
+
+// ------------------------------------------------------------- launches
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  VMLM_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return VMLM_OK;
+}
+
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows) {
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(VMLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, pitch %llu, box %u x %u",
+                static_cast<int>(r), static_cast<unsigned long long>(inner), static_cast<unsigned long long>(rows),
+                static_cast<unsigned long long>(row_bytes), box_inner, box_rows);
+  return VMLM_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+inline int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// Plan and launch the tcgen05 kernel. units_min = tiles * k-blocks with one term.
+template <TcMode MODE>
+int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool streamk,
+           bool pdl) {
+  const int stage_bytes = kTileRows * kBlockBytes + p.bn * kBlockBytes;
+  const int avail = kMaxSmem - 2048;
+  int stages = avail / stage_bytes;
+  if (stages > 16) stages = 16;
+  if (stages < 2) return fail(VMLM_ERR_SHAPE, "tile too large for shared memory");
+  p.stages = stages;
+  p.tmem_cols = pow2_at_least(2 * p.bn);
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long units_min = tiles * p.kb_per_term;
+  long long grid = streamk ? (units_min < c->sms ? units_min : c->sms) : (tiles < c->sms ? tiles : c->sms);
+  if (grid < 1) grid = 1;
+  p.streamk = streamk ? 1 : 0;
+  if (streamk) {
+    VMLM_TRY(ensure(c->slots, static_cast<size_t>(2 * grid) * kTileRows * p.bn * 4));
+    VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
+  }
+  p.slots = static_cast<uint32_t*>(c->slots.p);
+  p.counters = static_cast<int*>(c->counters.p);
+  p.err = c->err;
+  const TcSmem L = tc_smem_layout(stages, p.bn);
+  return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma, mb,
+                p);
+}
+
+int check_dims(size_t m, size_t n, size_t k) {
+  const size_t lim = static_cast<size_t>(1) << 31;
+  if (m >= lim || n >= lim || k >= lim) return fail(VMLM_ERR_SHAPE, "m, n, k must each be < 2^31");
+  return VMLM_OK;
+}
+
+// ------------------------------------------------------------- Q8 path
+
+int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
+           cudaStream_t st) {
+  const int kp = static_cast<int>(cdiv(K, 16) * 16);
+  VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * (kp ? kp : 16)));
+  VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));
+  int8_t* planes = static_cast<int8_t*>(c->act.p);
+  int* exps = static_cast<int*>(c->small.p);
+  int* nonf = exps + M;
+  VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+                  kp, planes, exps, nonf));
+  const bool tc_ok = K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
+  if (!tc_ok) {
+    const long long warps = static_cast<long long>(M) * N;
+    return launch(q8_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, true, q,
+                  scale, static_cast<const int8_t*>(planes), kp, static_cast<const int*>(exps),
+                  static_cast<const int*>(nonf), a, static_cast<long long>(K), out, static_cast<long long>(N), M, N,
+                  K);
+  }
+  const int tok = static_cast<int>(cdiv(M < 80 ? M : 80, 16) * 16);
+  TcParams p = {};
+  p.rows = N;
+  p.cols = 3 * M;
+  p.bn = 3 * tok;
+  p.kb_per_term = static_cast<int>(cdiv(K, 128));
+  p.max_terms = 1;
+  p.tiles_m = static_cast<int>(cdiv(N, kTileRows));
+  p.tiles_n = static_cast<int>(cdiv(M, tok));
+  p.tm_fastest = 0;
+  p.a_box_elems = 128;
+  p.out = out;
+  p.ldo = N;
+  p.vec_out = 0;
+  p.scale = scale;
+  p.exps = exps;
+  p.nonfinite = nonf;
+  p.n_tokens = M;
+  p.tok_per_tile = tok;
+  p.n_out = N;
+  p.x = a;
+  p.ldx = K;
+  p.w = q;
+  p.k = K;
+  CUtensorMap ma, mb;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn));
+  return run_tc<TcMode::kQ8Swap>(c, st, ma, mb, p, true, true);
+}
+
+// ------------------------------------------------------------ bf16 path
+
+int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, cudaStream_t st) {
+  const bool tc_ok = K > 0 && K % 8 == 0 && aligned16(b);
+  if (!tc_ok) {
+    const long long warps = static_cast<long long>(M) * N;
+    return launch(bf16_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, false,
+                  b, a, static_cast<long long>(K), out, static_cast<long long>(N), M, N, K);
+  }
+  const int kp = static_cast<int>(cdiv(K, 8) * 8);
+  VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * kp * 2));
+  VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));
+  uint16_t* terms = static_cast<uint16_t*>(c->act.p);
+  int* flags = static_cast<int*>(c->small.p) + 2 * M;
+  int* nonf = static_cast<int*>(c->small.p) + M;
+  const bool swap = M <= 80;
+  VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+                  kp, swap ? 0 : 1, terms, flags, nonf));
+  TcParams p = {};
+  p.max_terms = 1;
+  p.a_box_elems = 64;
+  p.kb_per_term = static_cast<int>(cdiv(K, 64));
+  p.out = out;
+  p.ldo = N;
+  p.nonfinite = nonf;
+  p.term_flags = flags;
+  p.x = a;
+  p.ldx = K;
+  p.w = b;
+  p.k = K;
+  CUtensorMap ma, mb;
+  if (swap) {
+    const int tok = static_cast<int>(cdiv(M, 16) * 16);
+    p.rows = N;
+    p.cols = 3 * M;
+    p.bn = 3 * tok;
+    p.tiles_m = static_cast<int>(cdiv(N, kTileRows));
+    p.tiles_n = 1;
+    p.tm_fastest = 0;
+    p.vec_out = 0;
+    p.n_tokens = M;
+    p.tok_per_tile = tok;
+    p.n_out = N;
+    VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, kTileRows));
+    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, K, 3ull * M, 2ull * kp, 64, p.bn));
+    return run_tc<TcMode::kBf16Swap>(c, st, ma, mb, p, true, true);
+  }
+  p.rows = M;
+  p.cols = N;
+  p.bn = 256;
+  p.max_terms = 3;
+  p.term_stride = kp;
+  p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
+  p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+  p.tm_fastest = 1;
+  p.vec_out = (N % 4 == 0) && aligned16(out);
+  p.n_tokens = M;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, tiles < 4ll * c->sms, true);
+}
+
+// ---------------------------------------------------------- int8 x int8
+
+int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float* out, int32_t* acc, int M, int N,
+             int K, cudaStream_t st) {
+  const bool tc_ok = K > 0 && K % 16 == 0 && aligned16(x) && aligned16(w);
+  if (!tc_ok) {
+    const long long warps = static_cast<long long>(M) * N;
+    return launch(i8i8_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, false,
+                  x, w, scale, out, acc, M, N, K);
+  }
+  TcParams p = {};
+  p.rows = M;
+  p.cols = N;
+  p.bn = 256;
+  p.kb_per_term = static_cast<int>(cdiv(K, 128));
+  p.max_terms = 1;
+  p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
+  p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+  p.tm_fastest = 1;
+  p.a_box_elems = 128;
+  p.out = out;
+  p.acc_out = acc;
+  p.ldo = N;
+  p.vec_out = (N % 4 == 0) && (!out || aligned16(out)) && (!acc || aligned16(acc));
+  p.scale = scale;
+  p.n_tokens = M;
+  CUtensorMap ma, mb;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, tiles < 4ll * c->sms, false);
+}
+
+// ------------------------------------------------------------ host API
+
+// Device address for a host range: registered copy, or a staged upload.
+int resolve(Ctx* c, const void* host, size_t bytes, DevBuf& stage, cudaStream_t st, const void** dptr) {
+  auto it = g_reg.upper_bound(reinterpret_cast<uintptr_t>(host));
+  if (it != g_reg.begin()) {
+    --it;
+    const uintptr_t h = reinterpret_cast<uintptr_t>(host);
+    if (it->second.dev == c->dev && h >= it->first && h + bytes <= it->first + it->second.bytes) {
+      *dptr = static_cast<const char*>(it->second.dptr) + (h - it->first);
+      return VMLM_OK;
+    }
+  }
+  VMLM_TRY(ensure(stage, bytes));
+  VMLM_CUDA(cudaMemcpyAsync(stage.p, host, bytes, cudaMemcpyHostToDevice, st));
+  *dptr = stage.p;
+  return VMLM_OK;
+}
+
+int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, size_t acc_bytes) {
+  if (host_c) VMLM_CUDA(cudaMemcpyAsync(host_c, c->h_c.p, c_bytes, cudaMemcpyDeviceToHost, c->stream));
+  if (host_acc) VMLM_CUDA(cudaMemcpyAsync(host_acc, c->h_acc.p, acc_bytes, cudaMemcpyDeviceToHost, c->stream));
+  VMLM_CUDA(cudaMemcpyAsync(c->err_host, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  VMLM_CUDA(cudaStreamSynchronize(c->stream));
+  if (*c->err_host != 0) {
+    const int code = *c->err_host;
+    cudaMemset(c->err, 0, sizeof(int));
+    if (c->counters.p) cudaMemset(c->counters.p, 0, c->counters.bytes);
+    *c->err_host = 0;
+    return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
+  }
+  return VMLM_OK;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+
+extern "C" {
+
+int vmlm_version(void) { return 100; }
+
+const char* vmlm_last_error(void) { return g_err.c_str(); }
+
+uint64_t vmlm_launch_count(void) { return g_launches.load(); }
+
+int vmlm_init(int device) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (device < 0) {
+    int d = 0;
+    VMLM_CUDA(cudaGetDevice(&d));
+    device = d;
+  }
+  Ctx* c = nullptr;
+  VMLM_TRY(get_ctx(device, &c));
+  g_host_dev = device;
+  VMLM_CUDA(cudaSetDevice(device));
+  return VMLM_OK;
+}
+
+int vmlm_unregister_all(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  for (auto& kv : g_reg) {
+    cudaSetDevice(kv.second.dev);
+    cudaFree(kv.second.dptr);
+  }
+  g_reg.clear();
+  return VMLM_OK;
+}
+
+int vmlm_shutdown(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  vmlm_unregister_all();
+  for (auto& kv : g_ctx) {
+    Ctx* c = kv.second;
+    cudaSetDevice(c->dev);
+    cudaStreamSynchronize(c->stream);
+    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
+      if (b->p) cudaFree(b->p);
+    cudaFree(c->err);
+    cudaFreeHost(c->err_host);
+    cudaStreamDestroy(c->stream);
+    delete c;
+  }
+  g_ctx.clear();
+  g_host_dev = -1;
+  return VMLM_OK;
+}
+
+int vmlm_register_weight(const void* host_ptr, size_t bytes) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!host_ptr || bytes == 0) return fail(VMLM_ERR_ARG, "register: null pointer or zero size");
+  Ctx* c = nullptr;
+  VMLM_TRY(host_ctx(&c));
+  const uintptr_t h = reinterpret_cast<uintptr_t>(host_ptr);
+  auto it = g_reg.lower_bound(h);
+  if (it != g_reg.end() && it->first < h + bytes && it->second.dev == c->dev)
+    return fail(VMLM_ERR_ARG, "register: range overlaps an existing registration");
+  if (it != g_reg.begin()) {
+    auto pv = std::prev(it);
+    if (pv->first + pv->second.bytes > h && pv->second.dev == c->dev)
+      return fail(VMLM_ERR_ARG, "register: range overlaps an existing registration");
+  }
+  void* d = nullptr;
+  VMLM_CUDA(cudaMalloc(&d, bytes));
+  cudaError_t e = cudaMemcpy(d, host_ptr, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return fail(VMLM_ERR_CUDA, "register: upload failed: %s", cudaGetErrorString(e));
+  }
+  g_reg[h] = Reg{bytes, d, c->dev};
+  return VMLM_OK;
+}
+
+int vmlm_unregister_weight(const void* host_ptr) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto it = g_reg.find(reinterpret_cast<uintptr_t>(host_ptr));
+  if (it == g_reg.end()) return fail(VMLM_ERR_ARG, "unregister: pointer was not registered");
+  cudaSetDevice(it->second.dev);
+  cudaFree(it->second.dptr);
+  g_reg.erase(it);
+  return VMLM_OK;
+}
+
+int vmlm_gemm_nt_int8(const float* a, const int8_t* q, const float* scale, float* c, size_t m, size_t n,
+                      size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || !scale || (k > 0 && (!a || !q))) return fail(VMLM_ERR_ARG, "gemm_nt_int8: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *dq = nullptr, *ds = nullptr;
+  VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+  VMLM_TRY(resolve(ctx, q, n * k, ctx->h_w, ctx->stream, &dq));
+  VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  VMLM_TRY(run_q8(ctx, static_cast<const float*>(da), static_cast<const int8_t*>(dq), static_cast<const float*>(ds),
+                  static_cast<float*>(ctx->h_c.p), static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                  ctx->stream));
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int vmlm_gemm_nt_bf16(const float* a, const uint16_t* b, float* c, size_t m, size_t n, size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "gemm_nt_bf16: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *db = nullptr;
+  VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+  VMLM_TRY(resolve(ctx, b, n * k * 2, ctx->h_w, ctx->stream, &db));
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  VMLM_TRY(run_bf16(ctx, static_cast<const float*>(da), static_cast<const uint16_t*>(db),
+                    static_cast<float*>(ctx->h_c.p), static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                    ctx->stream));
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int vmlm_gemm_i8i8(const int8_t* x, const int8_t* w, const float* scale, float* c, int32_t* acc, size_t m, size_t n,
+                   size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (k > 131072) return fail(VMLM_ERR_SHAPE, "gemm_i8i8: k > 131072 can overflow the int32 accumulator");
+  if (m == 0 || n == 0 || (!c && !acc)) return VMLM_OK;
+  if ((c && !scale) || (k > 0 && (!x || !w))) return fail(VMLM_ERR_ARG, "gemm_i8i8: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *dx = nullptr, *dw = nullptr, *ds = nullptr;
+  VMLM_TRY(resolve(ctx, x, m * k, ctx->h_a, ctx->stream, &dx));
+  VMLM_TRY(resolve(ctx, w, n * k, ctx->h_w, ctx->stream, &dw));
+  if (c) VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+  if (c) VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  if (acc) VMLM_TRY(ensure(ctx->h_acc, m * n * 4));
+  VMLM_TRY(run_i8i8(ctx, static_cast<const int8_t*>(dx), static_cast<const int8_t*>(dw),
+                    static_cast<const float*>(ds), c ? static_cast<float*>(ctx->h_c.p) : nullptr,
+                    acc ? static_cast<int32_t*>(ctx->h_acc.p) : nullptr, static_cast<int>(m), static_cast<int>(n),
+                    static_cast<int>(k), ctx->stream));
+  return finish_host_call(ctx, c, m * n * 4, acc, m * n * 4);
+}
+
+int vmlm_gemm_nt_int8_dev(const float* a, const int8_t* q, const float* scale, float* c, size_t m, size_t n,
+                          size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || !scale || (k > 0 && (!a || !q))) return fail(VMLM_ERR_ARG, "gemm_nt_int8_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_q8(ctx, a, q, scale, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_gemm_nt_bf16_dev(const float* a, const uint16_t* b, float* c, size_t m, size_t n, size_t k,
+                          void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "gemm_nt_bf16_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_bf16(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_gemm_i8i8_dev(const int8_t* x, const int8_t* w, const float* scale, float* c, int32_t* acc, size_t m,
+                       size_t n, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (k > 131072) return fail(VMLM_ERR_SHAPE, "gemm_i8i8: k > 131072 can overflow the int32 accumulator");
+  if (m == 0 || n == 0 || (!c && !acc)) return VMLM_OK;
+  if ((c && !scale) || (k > 0 && (!x || !w))) return fail(VMLM_ERR_ARG, "gemm_i8i8_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_i8i8(ctx, x, w, scale, c, acc, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_sync(void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  VMLM_CUDA(cudaStreamSynchronize(st));
+  int code = 0;
+  VMLM_CUDA(cudaMemcpy(&code, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    cudaMemset(ctx->err, 0, sizeof(int));
+    if (ctx->counters.p) cudaMemset(ctx->counters.p, 0, ctx->counters.bytes);
+    return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
+  }
+  return VMLM_OK;
+}
+
+}  // extern "C"

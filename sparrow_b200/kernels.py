@@ -1,0 +1,165 @@
+"""Python mirror of `vmlm_ops::kernels` for the quantised-linear path.
+
+Same operator names, argument order and meaning as the reference
+(ops/src/kernels.rs in the shouzugzs-AI/Sparrow tree):
+
+    gemm_nt_int8(a, q, scale, c, m, n, k)   ops/src/kernels.rs:1256-1287
+    gemm_nt_bf16(a, b, c, m, n, k)          ops/src/kernels.rs:1199-1227
+
+`a`, `q`/`b`, `scale` and `c` are host buffers (numpy arrays, contiguous, of
+the stated element type and at least the stated length); `c` is overwritten.
+The reference kernels check nothing and the VM calls exit(9) on misuse
+(core/src/interp.rs:752-806); here a bad argument raises VmlmError (or
+ValueError for a Python-side type or size mismatch) before any GPU work.
+
+The `_dev` variants take device buffers: torch CUDA tensors (or raw device
+addresses as ints) and an optional CUDA stream, and return without waiting.
+"""
+import ctypes
+
+import numpy as np
+
+from ._lib import check, lib
+
+
+def _host_ptr(x, dtype, count, name):
+    if not isinstance(x, np.ndarray):
+        raise ValueError(f"{name}: expected a numpy array, got {type(x).__name__}")
+    if x.dtype != dtype:
+        raise ValueError(f"{name}: expected {np.dtype(dtype).name}, got {x.dtype.name}")
+    if not x.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"{name}: must be C-contiguous")
+    if x.size < count:
+        raise ValueError(f"{name}: needs {count} elements, has {x.size}")
+    return ctypes.c_void_p(x.ctypes.data) if x.size else None
+
+
+def _dev_ptr(x, dtype_name, count, name):
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return ctypes.c_void_p(x)
+    if not getattr(x, "is_cuda", False):
+        raise ValueError(f"{name}: expected a CUDA tensor or a device address")
+    if str(x.dtype) != f"torch.{dtype_name}":
+        raise ValueError(f"{name}: expected torch.{dtype_name}, got {x.dtype}")
+    if not x.is_contiguous():
+        raise ValueError(f"{name}: must be contiguous")
+    if x.numel() < count:
+        raise ValueError(f"{name}: needs {count} elements, has {x.numel()}")
+    return ctypes.c_void_p(x.data_ptr())
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return ctypes.c_void_p(stream)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+# ------------------------------------------------------------------ setup
+
+def init(device: int = 0) -> None:
+    """Select the device for the host-pointer entry points (creates its context)."""
+    check(lib().vmlm_init(device))
+
+
+def shutdown() -> None:
+    check(lib().vmlm_shutdown())
+
+
+def register_weight(w: np.ndarray) -> None:
+    """Keep a device copy of an immutable host weight (or scale) array."""
+    if not isinstance(w, np.ndarray) or not w.flags["C_CONTIGUOUS"]:
+        raise ValueError("register_weight: expected a C-contiguous numpy array")
+    check(lib().vmlm_register_weight(ctypes.c_void_p(w.ctypes.data), w.nbytes))
+
+
+def unregister_weight(w: np.ndarray) -> None:
+    check(lib().vmlm_unregister_weight(ctypes.c_void_p(w.ctypes.data)))
+
+
+def unregister_all() -> None:
+    check(lib().vmlm_unregister_all())
+
+
+def sync(stream=None) -> None:
+    check(lib().vmlm_sync(_stream_ptr(stream)))
+
+
+def launch_count() -> int:
+    return int(lib().vmlm_launch_count())
+
+
+# ------------------------------------------------------- reference operators
+
+def gemm_nt_int8(a, q, scale, c, m, n, k) -> None:
+    """C[M,N] = (A[M,K] . f32(q[N,K])^T) * scale[N]  (ops/src/kernels.rs:1256-1287)."""
+    check(lib().vmlm_gemm_nt_int8(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(q, np.int8, n * k, "q"),
+        _host_ptr(scale, np.float32, n, "scale"), _host_ptr(c, np.float32, m * n, "c"), m, n, k))
+
+
+def gemm_nt_bf16(a, b, c, m, n, k) -> None:
+    """C[M,N] = A[M,K] . widen(B_bf16[N,K])^T  (ops/src/kernels.rs:1199-1227); b holds bf16 bits as uint16."""
+    check(lib().vmlm_gemm_nt_bf16(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(b, np.uint16, n * k, "b"),
+        _host_ptr(c, np.float32, m * n, "c"), m, n, k))
+
+
+def gemm_i8i8(x, w, scale, c, acc, m, n, k) -> None:
+    """int8 x int8 -> exact int32 acc[M,N]; C = f32(acc) * scale[N]. c or acc may be None."""
+    check(lib().vmlm_gemm_i8i8(
+        _host_ptr(x, np.int8, m * k, "x"), _host_ptr(w, np.int8, n * k, "w"),
+        _host_ptr(scale, np.float32, n, "scale") if c is not None else None,
+        _host_ptr(c, np.float32, m * n, "c") if c is not None else None,
+        _host_ptr(acc, np.int32, m * n, "acc") if acc is not None else None, m, n, k))
+
+
+# ----------------------------------------------------------- device variants
+
+def gemm_nt_int8_dev(a, q, scale, c, m, n, k, stream=None) -> None:
+    check(lib().vmlm_gemm_nt_int8_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(q, "int8", n * k, "q"),
+        _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"), m, n, k,
+        _stream_ptr(stream)))
+
+
+def gemm_nt_bf16_dev(a, b, c, m, n, k, stream=None) -> None:
+    """b: a bfloat16 (or int16/uint16 bit-pattern) CUDA tensor [n, k]."""
+    if b is not None and not isinstance(b, int) and str(b.dtype) in ("torch.int16", "torch.uint16"):
+        bptr = _dev_ptr(b, str(b.dtype)[6:], n * k, "b")
+    else:
+        bptr = _dev_ptr(b, "bfloat16", n * k, "b")
+    check(lib().vmlm_gemm_nt_bf16_dev(
+        _dev_ptr(a, "float32", m * k, "a"), bptr, _dev_ptr(c, "float32", m * n, "c"), m, n, k,
+        _stream_ptr(stream)))
+
+
+def gemm_i8i8_dev(x, w, scale, c, acc, m, n, k, stream=None) -> None:
+    check(lib().vmlm_gemm_i8i8_dev(
+        _dev_ptr(x, "int8", m * k, "x"), _dev_ptr(w, "int8", n * k, "w"),
+        _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"),
+        _dev_ptr(acc, "int32", m * n, "acc"), m, n, k, _stream_ptr(stream)))
+
+
+# ---------------------------------------------------------- conveniences
+
+def q8_linear(x: np.ndarray, q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """x[M,K] f32, q[N,K] int8, scale[N] f32 -> C[M,N] f32 through gemm_nt_int8."""
+    m, k = x.shape
+    n = q.shape[0]
+    c = np.empty((m, n), np.float32)
+    gemm_nt_int8(np.ascontiguousarray(x, np.float32), np.ascontiguousarray(q, np.int8),
+                 np.ascontiguousarray(scale, np.float32), c, m, n, k)
+    return c
+
+
+def bf16_linear(x: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """x[M,K] f32, b_bits[N,K] uint16 (bf16 bits) -> C[M,N] f32 through gemm_nt_bf16."""
+    m, k = x.shape
+    n = b_bits.shape[0]
+    c = np.empty((m, n), np.float32)
+    gemm_nt_bf16(np.ascontiguousarray(x, np.float32), np.ascontiguousarray(b_bits, np.uint16), c, m, n, k)
+    return c

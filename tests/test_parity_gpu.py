@@ -1,0 +1,309 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle.
+
+Tolerances: int8 x int8 -> int32 accumulators and their
+scaled outputs bit-exact; f32 outputs within 1e-3 max relative error
+(max|gpu-ref| / max|ref|). The kernels are tighter than that: Q8 results carry
+~2^-22 relative rounding of the activations and bf16 results ~f32 accumulation
+error, so the tests also assert the tighter bounds TIGHT_Q8 / TIGHT_BF16.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from test_oracle import EDGE_SHAPES, edge_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3        # BASELINE: fp32 outputs within 1e-3 max relative error
+TIGHT_Q8 = 2e-5
+TIGHT_BF16 = 1e-4
+NT = os.cpu_count() or 1
+
+
+def q8_case(O, m, n, k, seed=0):
+    x = O.fill_normal(m * k, seed, 1.0).reshape(m, k)
+    q, s = O.quant_int8(O.fill_normal(n * k, seed + 1, 0.02).reshape(n, k))
+    return x, q, s
+
+
+def check_q8(K, O, x, q, s, tight=TIGHT_Q8):
+    got = K.q8_linear(x, q, s)
+    ref = O.gemm_nt_int8(x, q, s, nt=NT)
+    err = O.max_rel_err(got, ref)
+    assert err <= TOL and err <= tight, err
+    return got, ref
+
+
+# ----------------------------------------------------------- golden fixtures
+
+def _f32(p, shape=None):
+    a = np.fromfile(os.path.join(GOLDEN, p), "<f4")
+    return a.reshape(shape) if shape else a
+
+
+def _i8(p, shape):
+    return np.fromfile(os.path.join(GOLDEN, p), "i1").reshape(shape)
+
+
+def test_golden_p13_q8_exact(kernels):
+    a = _f32("p13/q8_a.f32", (1, 4))
+    w = _i8("p13/q8_w.i8", (2, 4))
+    s = _f32("p13/q8_scale.f32")
+    assert kernels.q8_linear(a, w, s).ravel().tolist() == [-1.0, -1.0]
+
+
+def test_golden_int8_bins_through_gpu(kernels, oracle):
+    def lin(d, tag, x, kin):
+        q = _i8(f"{d}/{tag}_Wq.bin", (4, kin))
+        return kernels.q8_linear(x, q, _f32(f"{d}/{tag}_scale.bin")) + _f32(f"{d}/{tag}_b.bin")
+
+    def lin_f32(d, tag, x, kin):
+        return oracle.gemm_naive_f32(x, _f32(f"{d}/{tag}_W.bin", (4, kin))) + _f32(f"{d}/{tag}_b.bin")
+
+    x1 = _f32("int8_bins/i8o_in.bin", (1, 1))
+    assert oracle.print_f32(lin("int8_bins", "o", x1, 1)) == "0.881869 -0.907158 -0.010653 2.102990"
+    x4 = _f32("int8_bins/i8t_in.bin", (1, 4))
+    two = lambda d, f: f(d, "b", f(d, "a", x4, 4), 4)  # noqa: E731
+    exact = two("int8_bins", lin_f32)
+    assert np.abs(two("int8_bins", lin) - exact).max() <= 1e-4
+    assert abs(np.abs(two("int8_bad_bins", lin) - exact).max() - 0.607249) < 1e-5
+    xn = _f32("int8_naive_bins/i8t_in.bin", (1, 4))
+    d4 = np.abs(lin("int8_naive_bins", "b", lin("int8_naive_bins", "a", xn, 4), 4)
+                - lin_f32("int8_naive_bins", "b", lin_f32("int8_naive_bins", "a", xn, 4), 4)).max()
+    assert abs(d4 - 0.009791) < 1e-5
+
+
+# ------------------------------------------------------------- Q8 configs
+
+def test_c1_q8_gemv_full(kernels, oracle):
+    x, q, s = q8_case(oracle, 1, 5760, 2304)
+    check_q8(kernels, oracle, x, q, s)
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+def test_c3_q8_layer_set(kernels, oracle, m):
+    shapes = [(2304, 2304)] * 4 + [(5760, 2304)] * 2 + [(2304, 5760)]
+    for i, (n, k) in enumerate(shapes):
+        x, q, s = q8_case(oracle, m, n, k, seed=10 * i)
+        check_q8(kernels, oracle, x, q, s)
+
+
+@pytest.mark.parametrize("m", [1, 64])
+def test_c4_q8_lm_head(kernels, oracle, m):
+    n, k = 122753, 2304
+    x, q, s = q8_case(oracle, m, n, k, seed=40)
+    got = kernels.q8_linear(x, q, s)
+    rows = np.unique(np.concatenate([np.arange(256), np.arange(n - 256, n),
+                                     np.random.default_rng(0).integers(0, n, 4096)]))
+    ref = oracle.gemm_nt_int8(x, np.ascontiguousarray(q[rows]), np.ascontiguousarray(s[rows]), nt=NT)
+    err = oracle.max_rel_err(np.ascontiguousarray(got[:, rows]), ref)
+    assert err <= TOL and err <= TIGHT_Q8, err
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 2304, 2304), (3, 1000, 4096), (17, 130, 2304), (80, 384, 1024),
+                                   (81, 640, 768), (100, 257, 512), (200, 96, 256), (64, 128, 8192)])
+def test_q8_shapes_streamk_and_token_chunks(kernels, oracle, m, n, k):
+    x, q, s = q8_case(oracle, m, n, k, seed=m + n)
+    check_q8(kernels, oracle, x, q, s)
+
+
+@pytest.mark.parametrize("m,n,k", EDGE_SHAPES)
+def test_q8_edge_shapes(kernels, oracle, m, n, k):
+    a, b = edge_inputs(m, n, k)
+    q, s = oracle.quant_int8(b)
+    check_q8(kernels, oracle, a, q, s)
+
+
+def test_q8_nonfinite_rows_match_reference(kernels, oracle):
+    m, n, k = 4, 300, 512
+    x, q, s = q8_case(oracle, m, n, k, seed=3)
+    x[1, 7] = np.inf
+    x[2, 100] = np.nan
+    x[3, 5] = -np.inf
+    x[3, 6] = np.inf
+    got = kernels.q8_linear(x, q, s)
+    ref = oracle.gemm_nt_int8(x, q, s)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.sign(got[np.isinf(ref)]), np.sign(ref[np.isinf(ref)]))
+    assert oracle.max_rel_err(np.ascontiguousarray(got[fin]), np.ascontiguousarray(ref[fin])) <= TIGHT_Q8
+
+
+def test_q8_zero_rows_and_extreme_scales(kernels, oracle):
+    m, n, k = 3, 200, 256
+    x, q, s = q8_case(oracle, m, n, k, seed=9)
+    x[0] = 0.0
+    x[1] *= np.float32(1e-30)
+    x[2] *= np.float32(1e30)
+    got = kernels.q8_linear(x, q, s)
+    ref = oracle.gemm_nt_int8(x, q, s)
+    assert np.all(got[0] == 0.0)
+    for r in (1, 2):
+        assert oracle.max_rel_err(got[r:r + 1], ref[r:r + 1]) <= TIGHT_Q8
+
+
+def test_q8_deterministic(kernels, oracle):
+    x, q, s = q8_case(oracle, 8, 2304, 2304, seed=5)
+    a = kernels.q8_linear(x, q, s)
+    b = kernels.q8_linear(x, q, s)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_registered_weights_and_layer_offsets(kernels, oracle):
+    # OP_LAYERB hands the kernel pointers into the middle of one constant
+    # (core/src/interp.rs:438-475): register the whole stack, call on a slice.
+    layers, n, k = 3, 384, 1024
+    x, q, s = q8_case(oracle, 2, layers * n, k, seed=21)
+    kernels.register_weight(q)
+    kernels.register_weight(s)
+    try:
+        for l in range(layers):
+            ql, sl = q[l * n:(l + 1) * n], s[l * n:(l + 1) * n]
+            got = kernels.q8_linear(x, ql, sl)
+            assert oracle.max_rel_err(got, oracle.gemm_nt_int8(x, ql, sl)) <= TIGHT_Q8
+    finally:
+        kernels.unregister_all()
+
+
+# ------------------------------------------------------------- bf16 configs
+
+def bf16_case(O, m, n, k, seed=0, exact_x=True):
+    x = O.fill_normal(m * k, seed, 1.0)
+    if exact_x:
+        x = O.bf16_to_f32(O.f32_to_bf16(x))
+    w = O.f32_to_bf16(O.fill_normal(n * k, seed + 1, 0.02)).reshape(n, k)
+    return x.reshape(m, k), w
+
+
+def check_bf16(K, O, x, w, tight=TIGHT_BF16):
+    got = K.bf16_linear(x, w)
+    ref = O.gemm_nt_bf16(x, w, nt=NT)
+    err = O.max_rel_err(got, ref)
+    assert err <= TOL and err <= tight, err
+    return got, ref
+
+
+def test_c2_bf16_prefill_full(kernels, oracle):
+    x, w = bf16_case(oracle, 512, 2304, 2304)
+    check_bf16(kernels, oracle, x, w)
+
+
+def test_c2_shape_general_f32_activations(kernels, oracle):
+    # activations that are not bf16 values: three split terms are active
+    x, w = bf16_case(oracle, 512, 2304, 2304, seed=7, exact_x=False)
+    check_bf16(kernels, oracle, x, w)
+
+
+@pytest.mark.parametrize("m", [1, 8, 32, 80])
+def test_bf16_decode_shapes(kernels, oracle, m):
+    x, w = bf16_case(oracle, m, 5760, 2304, seed=m, exact_x=False)
+    check_bf16(kernels, oracle, x, w)
+
+
+@pytest.mark.parametrize("m,n,k", [(81, 300, 512), (129, 257, 1000), (300, 2304, 64), (1000, 520, 2048)])
+def test_bf16_ragged_tiles(kernels, oracle, m, n, k):
+    x, w = bf16_case(oracle, m, n, k, seed=m, exact_x=False)
+    check_bf16(kernels, oracle, x, w)
+
+
+@pytest.mark.parametrize("m,n,k", EDGE_SHAPES)
+def test_bf16_edge_shapes(kernels, oracle, m, n, k):
+    a, b = edge_inputs(m, n, k)
+    check_bf16(kernels, oracle, a, oracle.f32_to_bf16(b))
+
+
+def test_bf16_nonfinite(kernels, oracle):
+    x, w = bf16_case(oracle, 3, 200, 256, seed=2, exact_x=False)
+    x[0, 3] = np.inf
+    x[1, 9] = np.nan
+    got = kernels.bf16_linear(x, w)
+    ref = oracle.gemm_nt_bf16(x, w)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+
+
+# ------------------------------------------------------------- int8 x int8
+
+def i8_case(O, m, n, k, seed=0):
+    x = O.fill_int8(m * k, seed).reshape(m, k)
+    w = O.fill_int8(n * k, seed + 1).reshape(n, k)
+    s = np.abs(O.fill_normal(n, seed + 2, 0.02)) + np.float32(1e-3)
+    return x, w, s
+
+
+def run_i8(K, x, w, s):
+    m, k = x.shape
+    n = w.shape[0]
+    c = np.empty((m, n), np.float32)
+    acc = np.empty((m, n), np.int32)
+    K.gemm_i8i8(x, w, s, c, acc, m, n, k)
+    return c, acc
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 2048, 8192), (128, 256, 128), (300, 1000, 4096), (4096, 512, 1024)])
+def test_i8i8_bit_exact(kernels, oracle, m, n, k):
+    x, w, s = i8_case(oracle, m, n, k, seed=m)
+    c, acc = run_i8(kernels, x, w, s)
+    rc, racc = oracle.gemm_i8i8(x, w, s, nt=NT)
+    assert np.array_equal(acc, racc)
+    assert np.array_equal(c.view(np.uint32), rc.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k", EDGE_SHAPES)
+def test_i8i8_edge_shapes(kernels, oracle, m, n, k):
+    x, w, s = i8_case(oracle, m, n, k, seed=1)
+    c, acc = run_i8(kernels, x, w, s)
+    rc, racc = oracle.gemm_i8i8(x, w, s)
+    assert np.array_equal(acc, racc) and np.array_equal(c.view(np.uint32), rc.view(np.uint32))
+
+
+def test_c5_full_size_checksums_and_blocks(kernels, oracle):
+    """C5 at full size: exact row/column checksums (int64) plus exact random blocks."""
+    import torch
+    m, n, k = 4096, 28672, 8192
+    x, w, s = i8_case(oracle, m, n, k, seed=55)
+    dx, dw, ds = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda()
+    dacc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    dc = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    kernels.gemm_i8i8_dev(dx, dw, ds, dc, dacc, m, n, k)
+    kernels.sync()
+    # column sums: sum_m acc[m][n] = (sum_m x[m,:]) . w[n,:]
+    colsum = dacc.to(torch.int64).sum(0).cpu().numpy()
+    xs = x.astype(np.int64).sum(0)
+    ref_col = (w.astype(np.int64) @ xs)
+    assert np.array_equal(colsum, ref_col)
+    rowsum = dacc.to(torch.int64).sum(1).cpu().numpy()
+    ref_row = x.astype(np.int64) @ w.astype(np.int64).sum(0)
+    assert np.array_equal(rowsum, ref_row)
+    rng = np.random.default_rng(1)
+    for _ in range(3):
+        r0, c0 = int(rng.integers(0, m - 64)), int(rng.integers(0, n - 256))
+        blk_c, blk_a = oracle.gemm_i8i8(np.ascontiguousarray(x[r0:r0 + 64]), np.ascontiguousarray(w[c0:c0 + 256]),
+                                        np.ascontiguousarray(s[c0:c0 + 256]), nt=NT)
+        assert np.array_equal(dacc[r0:r0 + 64, c0:c0 + 256].cpu().numpy(), blk_a)
+        assert np.array_equal(dc[r0:r0 + 64, c0:c0 + 256].cpu().numpy().view(np.uint32), blk_c.view(np.uint32))
+
+
+# ------------------------------------------------------- device entry points
+
+def test_device_entry_points_match_host_ones(kernels, oracle):
+    import torch
+    x, q, s = q8_case(oracle, 8, 5760, 2304, seed=77)
+    host = kernels.q8_linear(x, q, s)
+    dx, dq, ds = torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    dc = torch.empty((8, 5760), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    kernels.gemm_nt_int8_dev(dx, dq, ds, dc, 8, 5760, 2304, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(dc.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    xb, wb = bf16_case(oracle, 64, 1024, 2304, seed=3, exact_x=False)
+    hb = kernels.bf16_linear(xb, wb)
+    dxb = torch.from_numpy(xb).cuda()
+    dwb = torch.from_numpy(wb.view(np.int16)).cuda()
+    dcb = torch.empty((64, 1024), dtype=torch.float32, device="cuda")
+    kernels.gemm_nt_bf16_dev(dxb, dwb, dcb, 64, 1024, 2304, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(dcb.cpu().numpy().view(np.uint32), hb.view(np.uint32))
