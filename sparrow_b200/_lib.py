@@ -35,6 +35,8 @@ SIGNATURES = {
     "vmlm_gemm_i8i8_dev": (I, [P, P, P, P, P, S, S, S, P]),
     "vmlm_sync": (I, [P]),
     "vmlm_launch_count": (ctypes.c_uint64, []),
+    "vmlm_profile_enable": (I, [I]),
+    "vmlm_profile_take": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 

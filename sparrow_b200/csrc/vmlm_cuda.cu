@@ -11,6 +11,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/vmlm_cuda.h"
 #include "prep.cuh"
@@ -91,6 +92,15 @@ struct Ctx {
 
 std::map<int, Ctx*> g_ctx;
 int g_host_dev = -1;
+
+// Optional timing of the tensor-core GEMM launches (diagnostics): a CUDA event
+// pair on the launch stream around each launch, summed by vmlm_profile_take.
+bool g_profile = false;
+struct ProfPair {
+  cudaEvent_t a, b;
+  int dev;
+};
+std::vector<ProfPair> g_prof_live, g_prof_free;
 
 struct Reg {
   size_t bytes;
@@ -234,8 +244,24 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   p.counters = static_cast<int*>(c->counters.p);
   p.err = c->err;
   const TcSmem L = tc_smem_layout(stages, p.bn);
-  return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma, mb,
-                p);
+  if (!g_profile)
+    return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma,
+                  mb, p);
+  ProfPair pp;
+  if (!g_prof_free.empty() && g_prof_free.back().dev == c->dev) {
+    pp = g_prof_free.back();
+    g_prof_free.pop_back();
+  } else {
+    VMLM_CUDA(cudaEventCreate(&pp.a));
+    VMLM_CUDA(cudaEventCreate(&pp.b));
+    pp.dev = c->dev;
+  }
+  VMLM_CUDA(cudaEventRecord(pp.a, st));
+  VMLM_TRY(launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false, ma,
+                  mb, p));
+  VMLM_CUDA(cudaEventRecord(pp.b, st));
+  g_prof_live.push_back(pp);
+  return VMLM_OK;
 }
 
 int check_dims(size_t m, size_t n, size_t k) {
@@ -607,6 +633,30 @@ int vmlm_gemm_i8i8_dev(const int8_t* x, const int8_t* w, const float* scale, flo
   VMLM_TRY(current_ctx(&ctx));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_i8i8(ctx, x, w, scale, c, acc, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_profile_enable(int on) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  g_profile = on != 0;
+  return VMLM_OK;
+}
+
+int vmlm_profile_take(double* gemm_ms, uint64_t* launches) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  double total = 0.0;
+  uint64_t n = 0;
+  for (ProfPair& pp : g_prof_live) {
+    VMLM_CUDA(cudaEventSynchronize(pp.b));
+    float ms = 0.f;
+    VMLM_CUDA(cudaEventElapsedTime(&ms, pp.a, pp.b));
+    total += ms;
+    ++n;
+    g_prof_free.push_back(pp);
+  }
+  g_prof_live.clear();
+  if (gemm_ms) *gemm_ms = total;
+  if (launches) *launches = n;
+  return VMLM_OK;
 }
 
 int vmlm_sync(void* stream) {

@@ -92,6 +92,19 @@ def launch_count() -> int:
     return int(lib().vmlm_launch_count())
 
 
+def profile_enable(on: bool) -> None:
+    """Bracket each tensor-core GEMM launch with CUDA events (diagnostics)."""
+    check(lib().vmlm_profile_enable(1 if on else 0))
+
+
+def profile_take():
+    """(summed device ms, launches) of the GEMM launches recorded since the last take."""
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_uint64(0)
+    check(lib().vmlm_profile_take(ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value
+
+
 # ------------------------------------------------------- reference operators
 
 def gemm_nt_int8(a, q, scale, c, m, n, k) -> None:
