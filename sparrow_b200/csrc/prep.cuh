@@ -116,14 +116,18 @@ __device__ __forceinline__ float bf16_val(uint16_t h) { return __uint_as_float(s
 
 // One CTA per token. Layout 0 (swap): out[(3t+j)*kp + k]. Layout 1 (normal):
 // out[t*3*kp + j*kp + k]. Columns [K, kp) are 0. term_flags[t] |= 1<<j for
-// every term j that is non-zero somewhere in the row.
+// every term j that is non-zero somewhere in the row. The last CTA to finish
+// (counted on done[0], which it resets) ORs all rows into done[1], so a
+// consumer reads one word instead of M.
 __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* __restrict__ x, long long ldx, int M,
                                                                   int K, int kp, int layout,
                                                                   uint16_t* __restrict__ out,
                                                                   int* __restrict__ term_flags,
-                                                                  int* __restrict__ nonfinite) {
+                                                                  int* __restrict__ nonfinite,
+                                                                  unsigned* __restrict__ done) {
   pdl_launch_dependents();
   __shared__ int redi[32];
+  __shared__ int is_last;
   const int t = blockIdx.x;
   if (t >= M) return;
   const float* xr = x + static_cast<long long>(t) * ldx;
@@ -158,6 +162,19 @@ __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* _
   if (threadIdx.x == 0) {
     term_flags[t] = flags | 1;
     nonfinite[t] = bad;
+    __threadfence();
+    is_last = (atomicAdd(done, 1u) == static_cast<unsigned>(M - 1));
+  }
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    int orv = 0;
+    for (int i = threadIdx.x; i < M; i += blockDim.x) orv |= __ldcg(term_flags + i);
+    orv = block_or(orv, redi);
+    if (threadIdx.x == 0) {
+      done[1] = static_cast<unsigned>(orv);
+      done[0] = 0u;
+    }
   }
 }
 

@@ -69,7 +69,7 @@ struct TcParams {
   const float* scale;
   const int* exps;        // kQ8Swap: per-token exponent e (value = v * 2^-e)
   const int* nonfinite;   // per-token flag: row of x holds NaN/Inf
-  const int* term_flags;  // kBf16Norm: per-token OR of (1<<j) for nonzero term j
+  const int* term_flags;  // kBf16Norm: OR over tokens of (1<<j) for every non-zero term j
   int n_tokens;           // tokens (swap modes: real tokens; used for bounds)
   int tok_per_tile;       // swap modes: tokens per column tile (bn/3)
   int n_out;              // swap modes: W rows (bounds on n)
@@ -153,10 +153,11 @@ struct Sched {
   }
 };
 
+// Number of split terms with any non-zero value (term_flags points at the OR of
+// all tokens' flags, written by the prep kernel).
 __device__ __forceinline__ int active_terms(const TcParams& p) {
   if (p.max_terms <= 1) return 1;
-  int orv = 0;
-  for (int t = 0; t < p.rows; ++t) orv |= __ldg(p.term_flags + t);
+  const int orv = __ldcg(p.term_flags);
   int T = 1;
   if (orv & 2) T = 2;
   if (orv & 4) T = 3;

@@ -84,6 +84,7 @@ struct Ctx {
   DevBuf small;     // exps | nonfinite | term_flags, each [M] int
   DevBuf slots;     // split-tile partials
   DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
+  DevBuf sync;      // prep completion counter and term-flag OR (zeroed once, self-resetting)
   int* err = nullptr;       // device error word
   int* err_host = nullptr;  // pinned copy read after host-API calls
   DevBuf h_a, h_c, h_w, h_s, h_acc;  // host-API staging
@@ -335,9 +336,11 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   uint16_t* terms = static_cast<uint16_t*>(c->act.p);
   int* flags = static_cast<int*>(c->small.p) + 2 * M;
   int* nonf = static_cast<int*>(c->small.p) + M;
+  VMLM_TRY(ensure(c->sync, 64, true));
+  unsigned* done = static_cast<unsigned*>(c->sync.p);
   const bool swap = M <= 80;
   VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
-                  kp, swap ? 0 : 1, terms, flags, nonf));
+                  kp, swap ? 0 : 1, terms, flags, nonf, done));
   TcParams p = {};
   p.max_terms = 1;
   p.a_box_elems = 64;
@@ -345,7 +348,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   p.out = out;
   p.ldo = N;
   p.nonfinite = nonf;
-  p.term_flags = flags;
+  p.term_flags = reinterpret_cast<const int*>(done + 1);
   p.x = a;
   p.ldx = K;
   p.w = b;
@@ -444,6 +447,7 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
     const int code = *c->err_host;
     cudaMemset(c->err, 0, sizeof(int));
     if (c->counters.p) cudaMemset(c->counters.p, 0, c->counters.bytes);
+    if (c->sync.p) cudaMemset(c->sync.p, 0, c->sync.bytes);
     *c->err_host = 0;
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
@@ -493,7 +497,7 @@ int vmlm_shutdown(void) {
     Ctx* c = kv.second;
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
-    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
+    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->sync, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
@@ -670,6 +674,7 @@ int vmlm_sync(void* stream) {
   if (code != 0) {
     cudaMemset(ctx->err, 0, sizeof(int));
     if (ctx->counters.p) cudaMemset(ctx->counters.p, 0, ctx->counters.bytes);
+    if (ctx->sync.p) cudaMemset(ctx->sync.p, 0, ctx->sync.bytes);
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
   return VMLM_OK;

@@ -50,12 +50,17 @@ def _dev_ptr(x, dtype_name, count, name):
     return ctypes.c_void_p(x.data_ptr())
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream
+
+
 def _stream_ptr(stream):
+    """None -> the library's own stream. A torch stream whose handle is 0 is the
+    legacy default stream, which the C ABI must receive as cudaStreamLegacy
+    (a NULL handle there selects the library stream)."""
     if stream is None:
         return None
-    if isinstance(stream, int):
-        return ctypes.c_void_p(stream)
-    return ctypes.c_void_p(stream.cuda_stream)
+    h = stream if isinstance(stream, int) else stream.cuda_stream
+    return ctypes.c_void_p(h if h else CUDA_STREAM_LEGACY)
 
 
 # ------------------------------------------------------------------ setup
