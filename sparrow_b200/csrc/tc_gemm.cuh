@@ -23,13 +23,14 @@
 // Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
 // the MMAs, warps 2..5 are the epilogue (TMEM lanes 32*(warp%4) .. +31).
 //
-// Scheduling is static and deterministic. Units are (tile, k-block) pairs
-// ordered tile-major. With many tiles the CTAs take whole tiles round-robin;
-// otherwise each CTA takes a contiguous range of units (stream-K). A tile
-// split between CTAs is finished by whichever CTA brings the tile's counter to
-// the full k-block count: every contributor stores its raw 32-bit partial in
-// its own slot, and the finisher sums the slots in CTA order, so results do
-// not depend on arrival order (integer sums are exact in any case).
+// Scheduling is static. Units are (tile, k-block) pairs ordered tile-major.
+// Either every CTA takes whole tiles round-robin, or each CTA takes a
+// contiguous range of units (stream-K). A tile split between CTAs is
+// accumulated with atomics into one slot (owned by the CTA that holds the
+// tile's last unit); the CTA that brings the tile's counter to the full
+// k-block count reads the slot, writes the output and clears the slot. Integer
+// accumulators (kQ8Swap, kI8Norm) are exact in any order; f32 partials
+// (bf16 modes) are order-dependent in the last bit.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -47,6 +48,7 @@ constexpr int kBlockBytes = 128;      // bytes of K per stage (one 128B swizzle 
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
 constexpr int kMaxSmem = 227 * 1024;
+constexpr int kMaxTokPerTile = 128;   // swap modes: tokens per column tile (bn/3 <= 85)
 
 struct TcParams {
   int rows;          // extent of A rows (W rows in swap modes, tokens in normal modes)
@@ -79,13 +81,13 @@ struct TcParams {
   const void* w;     // int8 or bf16 weight rows (row stride k)
   int k;
   // split-tile fixup
-  uint32_t* slots;   // [2*grid][128][bn] 32-bit partials
+  uint32_t* slots;   // [grid][128][bn] 32-bit accumulators, all zero between calls
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int* err;          // device error word
 };
 
 struct TcSmem {
-  uint32_t a_off, b_off, bar_off;  // offsets from the 1024-aligned base
+  uint32_t a_off, b_off, bar_off, meta_off;  // offsets from the 1024-aligned base
   uint32_t a_bytes, b_bytes, total;
 };
 
@@ -96,8 +98,10 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, int bn) {
   s.a_off = 0;
   s.b_off = s.a_off + stages * s.a_bytes;
   s.bar_off = s.b_off + stages * s.b_bytes;
-  // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, tmem addr, flags
-  s.total = s.bar_off + (2 * stages + 5) * 8 + 64 + 1024;  // +1024 for base alignment
+  // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, then 64 bytes of words
+  s.meta_off = s.bar_off + (2 * stages + 5) * 8 + 64;
+  // per-tile token table: exps[kMaxTokPerTile], nonfinite[kMaxTokPerTile]; +1024 for base alignment
+  s.total = s.meta_off + 2 * kMaxTokPerTile * 4 + 1024;
   return s;
 }
 
@@ -237,24 +241,26 @@ __device__ float nonfinite_dot(const TcParams& p, int t, int n) {
 }
 
 // Finish 16 tokens (48 accumulator columns, token-major triples) of one weight
-// row in a swap mode. tok0 is the first token of the chunk.
+// row in a swap mode. lt0 is the chunk's first token within the tile, tok0 the
+// tile's first token; s_exp / s_bad hold the tile's per-token metadata.
 template <TcMode MODE>
-__device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, const uint32_t (&v)[48]) {
+__device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, int lt0, float sc, const int* s_exp,
+                                           const int* s_bad, const uint32_t (&v)[48]) {
   if (n >= p.n_out) return;
-  const float sc = (MODE == TcMode::kQ8Swap) ? __ldg(p.scale + n) : 0.f;
   #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const int t = tok0 + j;
+    const int lt = lt0 + j;
+    const int t = tok0 + lt;
     if (t >= p.n_tokens) break;
     float r;
-    if (__ldg(p.nonfinite + t)) {
+    if (s_bad[lt]) {
       r = nonfinite_dot<MODE>(p, t, n);
     } else if constexpr (MODE == TcMode::kQ8Swap) {
       const long long a0 = static_cast<int>(v[3 * j + 0]);
       const long long a1 = static_cast<int>(v[3 * j + 1]);
       const long long a2 = static_cast<int>(v[3 * j + 2]);
       const long long vsum = a2 * 65536ll + a1 * 256ll + a0;
-      const double d = ldexp(static_cast<double>(vsum), -__ldg(p.exps + t));
+      const double d = ldexp(static_cast<double>(vsum), -s_exp[lt]);
       r = __fmul_rn(__double2float_rn(d), sc);
     } else {
       const float hi = __uint_as_float(v[3 * j + 0]);
@@ -263,6 +269,19 @@ __device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, c
       r = __fadd_rn(hi, __fadd_rn(mid, lo));
     }
     p.out[static_cast<long long>(t) * p.ldo + n] = r;
+  }
+}
+
+// Add 16 accumulator values into a fixup slot (integer or f32 atomics; the
+// return values are unused, so these compile to reductions).
+template <bool kInt>
+__device__ __forceinline__ void slot_add16(uint32_t* s, const uint32_t (&v)[16]) {
+  #pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (kInt)
+      atomicAdd(reinterpret_cast<int*>(s + j), static_cast<int>(v[j]));
+    else
+      atomicAdd(reinterpret_cast<float*>(s + j), __uint_as_float(v[j]));
   }
 }
 
@@ -289,6 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  int* s_exp = reinterpret_cast<int*>(smem + L.meta_off);
+  int* s_bad = s_exp + kMaxTokPerTile;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -425,17 +446,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // accumulator row within the tile
+    const int row = quarter * 32 + lane;   // accumulator row within the tile
     const int ethread = threadIdx.x - 64;  // 0..127
     long long cur = 0;
     WorkItem w;
     for (int i = 0; sc.item(cta, i, cur, w); ++i) {
       const int buf = i & 1;
-      if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
-      tc_fence_after();
       const int tm = p.tm_fastest ? w.tile % p.tiles_m : w.tile / p.tiles_n;
       const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
       const int grow = tm * kTileRows + row;  // A row (W row in swap modes, token in normal modes)
+      const int tok0 = tn * p.tok_per_tile;
+      float scale_n = 0.f;
+      if constexpr (kSwap) {
+        // Stage the tile's per-token metadata once (one load per thread) while
+        // the accumulator is still being computed.
+        named_bar_sync(1, kEpiThreads);
+        if (ethread < p.tok_per_tile) {
+          const int t = tok0 + ethread;
+          s_exp[ethread] = (MODE == TcMode::kQ8Swap && t < p.n_tokens) ? __ldg(p.exps + t) : 0;
+          s_bad[ethread] = (t < p.n_tokens) ? __ldg(p.nonfinite + t) : 0;
+        }
+        if (MODE == TcMode::kQ8Swap && grow < p.n_out) scale_n = __ldg(p.scale + grow);
+        named_bar_sync(1, kEpiThreads);
+      }
+      if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
 
       if (!w.partial) {
@@ -452,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(tempty_bar + buf);
             }
-            epi_swap48<MODE>(p, grow, tn * p.tok_per_tile + c / 3, v);
+            epi_swap48<MODE>(p, grow, tok0, c / 3, scale_n, s_exp, s_bad, v);
           }
         } else {
           for (int c = 0; c < p.bn; c += 16) {
@@ -471,18 +506,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      // Split tile: publish this CTA's partial, then let the last contributor finish.
+      // Split tile: add this CTA's partial into the tile's slot; the CTA that
+      // completes the tile's k-block count finishes it and clears the slot.
       const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
-      const int which = (sc.start(cta) >= tile_u0) ? 0 : 1;
-      uint32_t* myslot = p.slots + (static_cast<long long>(2 * cta + which) * kTileRows + row) * p.bn;
+      const int slot = sc.owner(tile_u0 + sc.kb_tile - 1);
+      uint32_t* srow = p.slots + (static_cast<long long>(slot) * kTileRows + row) * p.bn;
       for (int c = 0; c < p.bn; c += 16) {
         uint32_t v[16];
         __syncwarp();
         tmem_ld16(tbase + c, v);
         tmem_ld_wait();
-        #pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          __stcg(reinterpret_cast<uint4*>(myslot + c + j), make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        slot_add16<kInt>(srow + c, v);
       }
       tc_fence_before();
       __syncwarp();
@@ -497,55 +531,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_bar_sync(1, kEpiThreads);
       const int last = *bcast;
-      named_bar_sync(1, kEpiThreads);
       if (!last) continue;
       __threadfence();
-      const int c_first = sc.owner(tile_u0);
-      const int c_last = sc.owner(tile_u0 + sc.kb_tile - 1);
       if constexpr (kSwap) {
         for (int c = 0; c < p.bn; c += 48) {
           uint32_t v[48];
           #pragma unroll
-          for (int j = 0; j < 48; ++j) v[j] = 0;
-          for (int q = c_first; q <= c_last; ++q) {
-            const int wq = (sc.start(q) >= tile_u0) ? 0 : 1;
-            const uint32_t* s = p.slots + (static_cast<long long>(2 * q + wq) * kTileRows + row) * p.bn + c;
-            #pragma unroll
-            for (int j = 0; j < 48; j += 4) {
-              const uint4 u = __ldcg(reinterpret_cast<const uint4*>(s + j));
-              if constexpr (kInt) {
-                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
-              } else {
-                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(u.x)));
-                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), __uint_as_float(u.y)));
-                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), __uint_as_float(u.z)));
-                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), __uint_as_float(u.w)));
-              }
-            }
+          for (int j = 0; j < 48; j += 4) {
+            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(srow + c + j));
+            v[j] = u.x;
+            v[j + 1] = u.y;
+            v[j + 2] = u.z;
+            v[j + 3] = u.w;
           }
-          epi_swap48<MODE>(p, grow, tn * p.tok_per_tile + c / 3, v);
+          #pragma unroll
+          for (int j = 0; j < 48; j += 4) __stcg(reinterpret_cast<uint4*>(srow + c + j), make_uint4(0, 0, 0, 0));
+          epi_swap48<MODE>(p, grow, tok0, c / 3, scale_n, s_exp, s_bad, v);
         }
       } else {
         for (int c = 0; c < p.bn; c += 16) {
           uint32_t v[16];
           #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0;
-          for (int q = c_first; q <= c_last; ++q) {
-            const int wq = (sc.start(q) >= tile_u0) ? 0 : 1;
-            const uint32_t* s = p.slots + (static_cast<long long>(2 * q + wq) * kTileRows + row) * p.bn + c;
-            #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const uint4 u = __ldcg(reinterpret_cast<const uint4*>(s + j));
-              if constexpr (kInt) {
-                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
-              } else {
-                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(u.x)));
-                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), __uint_as_float(u.y)));
-                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), __uint_as_float(u.z)));
-                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), __uint_as_float(u.w)));
-              }
-            }
+          for (int j = 0; j < 16; j += 4) {
+            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(srow + c + j));
+            v[j] = u.x;
+            v[j + 1] = u.y;
+            v[j + 2] = u.z;
+            v[j + 3] = u.w;
           }
+          #pragma unroll
+          for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<uint4*>(srow + c + j), make_uint4(0, 0, 0, 0));
           epi_norm16<MODE>(p, grow, tn * p.bn + c, v);
         }
       }

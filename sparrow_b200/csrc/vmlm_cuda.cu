@@ -221,14 +221,33 @@ inline int pow2_at_least(int v) {
   return p;
 }
 
+// Tile width for a normal-mode GEMM (rows x N output, 128-row tiles, whole
+// tiles round-robin over the SMs): the narrowest widths fill more SMs but run
+// the tensor cores less efficiently, so pick the width with the least
+// estimated time, waves x per-tile cost.
+int pick_bn(int rows, int N, int sms) {
+  const int cand[3] = {256, 128, 64};
+  const double eff[3] = {1.0, 0.92, 0.75};
+  int best = 256;
+  double best_cost = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    const long long tiles = cdiv(rows, kTileRows) * cdiv(N, cand[i]);
+    const long long waves = cdiv(tiles, sms);
+    const double cost = static_cast<double>(waves) * cand[i] / eff[i];
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = cand[i];
+    }
+  }
+  return best;
+}
+
 // Plan and launch the tcgen05 kernel. units_min = tiles * k-blocks with one term.
 template <TcMode MODE>
 int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool streamk,
            bool pdl) {
-  const int stage_bytes = kTileRows * kBlockBytes + p.bn * kBlockBytes;
-  const int avail = kMaxSmem - 2048;
-  int stages = avail / stage_bytes;
-  if (stages > 16) stages = 16;
+  int stages = 16;
+  while (stages >= 2 && tc_smem_layout(stages, p.bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   if (stages < 2) return fail(VMLM_ERR_SHAPE, "tile too large for shared memory");
   p.stages = stages;
   p.tmem_cols = pow2_at_least(2 * p.bn);
@@ -238,7 +257,7 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   if (grid < 1) grid = 1;
   p.streamk = streamk ? 1 : 0;
   if (streamk) {
-    VMLM_TRY(ensure(c->slots, static_cast<size_t>(2 * grid) * kTileRows * p.bn * 4));
+    VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
     VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
   }
   p.slots = static_cast<uint32_t*>(c->slots.p);
@@ -372,7 +391,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   }
   p.rows = M;
   p.cols = N;
-  p.bn = 256;
+  p.bn = pick_bn(M, N, c->sms);
   p.max_terms = 3;
   p.term_stride = kp;
   p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
@@ -382,8 +401,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   p.n_tokens = M;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, tiles < 4ll * c->sms, true);
+  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true);
 }
 
 // ---------------------------------------------------------- int8 x int8
@@ -399,7 +417,7 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   TcParams p = {};
   p.rows = M;
   p.cols = N;
-  p.bn = 256;
+  p.bn = pick_bn(M, N, c->sms);
   p.kb_per_term = static_cast<int>(cdiv(K, 128));
   p.max_terms = 1;
   p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
@@ -415,8 +433,7 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, tiles < 4ll * c->sms, false);
+  return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false);
 }
 
 // ------------------------------------------------------------ host API
@@ -448,6 +465,7 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
     cudaMemset(c->err, 0, sizeof(int));
     if (c->counters.p) cudaMemset(c->counters.p, 0, c->counters.bytes);
     if (c->sync.p) cudaMemset(c->sync.p, 0, c->sync.bytes);
+    if (c->slots.p) cudaMemset(c->slots.p, 0, c->slots.bytes);
     *c->err_host = 0;
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
@@ -675,6 +693,7 @@ int vmlm_sync(void* stream) {
     cudaMemset(ctx->err, 0, sizeof(int));
     if (ctx->counters.p) cudaMemset(ctx->counters.p, 0, ctx->counters.bytes);
     if (ctx->sync.p) cudaMemset(ctx->sync.p, 0, ctx->sync.bytes);
+    if (ctx->slots.p) cudaMemset(ctx->slots.p, 0, ctx->slots.bytes);
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
   return VMLM_OK;
