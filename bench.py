@@ -69,7 +69,62 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration section")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="run only this workload, --steps times (for profilers); prints device ms/step")
+    ap.add_argument("--trace", action="store_true", help="with --case: per-CTA phase timestamps of one launch")
     return ap.parse_args()
+
+
+# Single workloads for profiling: name -> (kind, m, n, k)
+CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf16f", M2, N2, K2),
+         "c3q_m8": ("q8", 8, 2304, 2304), "c4m1": ("q8", 1, 122753, 2304), "c4m64": ("q8", 64, 122753, 2304),
+         "c5": ("i8", 4096, 28672, 8192), "c5small": ("i8", 1024, 4096, 8192)}
+
+
+def run_case(args):
+    """One workload through the device entry point, L2 flushed between steps."""
+    import torch
+    import sparrow_b200.kernels as K
+    torch.cuda.set_device(0)
+    K.init(0)
+    kind, m, n, k = CASES[args.case]
+    st = torch.cuda.current_stream()
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    if kind == "q8":
+        x = gen((m, k), 0, 1.0)
+        q, s = quantise_rows(gen((n, k), 1, 0.02))
+        step = lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)  # noqa: E731
+    elif kind in ("bf16", "bf16f"):
+        x = gen((m, k), 0, 1.0)
+        if kind == "bf16":
+            x = x.to(torch.bfloat16).float().contiguous()
+        w = gen((n, k), 1, 0.02).to(torch.bfloat16)
+        step = lambda: K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)  # noqa: E731
+    else:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5)
+        x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
+        w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+        s = gen((n,), 2, 0.02).abs() + 1e-3
+        step = lambda: K.gemm_i8i8_dev(x, w, s, c, None, m, n, k, stream=st)  # noqa: E731
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    t = time_steps(step, args.steps, args.warmup, flush)
+    out = {"case": args.case, "shape": [m, n, k], "ms_per_step": t}
+    if args.trace:
+        # phase stamps of one more launch, relative to the earliest CTA start (us)
+        K.trace_enable(1024)
+        flush_l2(flush)
+        step()
+        torch.cuda.synchronize()
+        tr = K.trace_take(1024).astype(np.float64)
+        K.trace_enable(0)
+        tr = tr[tr[:, 0] > 0]
+        t0 = tr[:, 0].min()
+        names = ["start", "prologue", "tma_issued", "first_stage", "last_commit", "first_accum", "epi_done", "end"]
+        out["trace_us"] = {nm: [round(float(np.min(v)), 2), round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
+                           for nm, v in zip(names, ((tr[:, j] - t0) / 1e3 for j in range(8)))}
+        out["trace_ctas"] = int(tr.shape[0])
+    print(json.dumps(out), flush=True)
 
 
 # ------------------------------------------------------------------ clocks
@@ -179,6 +234,14 @@ def gen(shape, seed, sigma):
     return torch.randn(shape, generator=g, device="cuda", dtype=torch.float32) * sigma
 
 
+def flush_l2(buf):
+    """Evict L2 before a timed step: write a buffer larger than L2, then read it
+    back, so the step starts with none of its data in L2 and no dirty lines
+    left for it to write back."""
+    buf.zero_()
+    buf.sum()
+
+
 def time_steps(step, k, warmup, flush, dist=None):
     """Device time of k steps (CUDA events on the current stream around each
     step, L2 flushed before each, outside the events), max over ranks; ms/step."""
@@ -189,7 +252,7 @@ def time_steps(step, k, warmup, flush, dist=None):
     st = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
     for a, b in evs:
-        flush.zero_()
+        flush_l2(flush)
         a.record(st)
         step()
         b.record(st)
@@ -206,7 +269,7 @@ def gemm_only(K, step, reps, flush, dist):
     K.profile_enable(True)
     K.profile_take()
     for _ in range(reps):
-        flush.zero_()
+        flush_l2(flush)
         step()
     torch.cuda.synchronize()
     ms, n = K.profile_take()
@@ -399,7 +462,7 @@ def run_ours(args):
     n0 = K.launch_count()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for a, b in evs:
-        flush.zero_()
+        flush_l2(flush)
         a.record(st)
         step()
         b.record(st)
@@ -433,7 +496,7 @@ def run_ours(args):
         K.gemm_nt_bf16(a_np, w_h, c_np, M2, N2, K2)
     e2e_t = []
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2(flush)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         K.gemm_nt_bf16(a_np, w_h, c_np, M2, N2, K2)
@@ -473,7 +536,9 @@ def run_ours(args):
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

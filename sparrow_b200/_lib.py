@@ -37,6 +37,8 @@ SIGNATURES = {
     "vmlm_launch_count": (ctypes.c_uint64, []),
     "vmlm_profile_enable": (I, [I]),
     "vmlm_profile_take": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
+    "vmlm_trace_enable": (I, [I]),
+    "vmlm_trace_take": (I, [P, S]),
 }
 
 

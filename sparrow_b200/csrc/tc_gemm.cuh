@@ -84,7 +84,13 @@ struct TcParams {
   uint32_t* slots;   // [grid][128][bn] 32-bit accumulators, all zero between calls
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int* err;          // device error word
+  unsigned long long* trace;  // optional: kTraceSlots globaltimer stamps per CTA (diagnostics)
 };
+
+// Trace slots (per CTA): kernel start, after prologue, producer done issuing,
+// first stage consumed by the MMA warp, last accumulator committed, first
+// accumulator seen by the epilogue, epilogue done, kernel end.
+constexpr int kTraceSlots = 8;
 
 struct TcSmem {
   uint32_t a_off, b_off, bar_off, meta_off;  // offsets from the 1024-aligned base
@@ -313,6 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  unsigned long long* trace = p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceSlots : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = globaltimer();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -337,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Everything below may read what the previous kernel in the stream wrote.
   pdl_wait_prior();
+  if (trace && threadIdx.x == 0) trace[1] = globaltimer();
 
   const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
   Sched sc;
@@ -388,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (trace) trace[2] = globaltimer();
       if (*abort_flag) {
         // Copies already issued must land before this CTA's shared memory is released.
         for (int s = 0; s < p.stages; ++s)
@@ -415,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (trace && !issued) trace[3] = globaltimer();
           const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
           const uint32_t b_addr = smem_u32(smem + L.b_off + stage * L.b_bytes);
           #pragma unroll
@@ -437,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         umma_commit(tfull_bar + buf);
       }
+      if (trace) trace[4] = globaltimer();
       if (issued && *abort_flag) {
         // Let in-flight MMAs finish before TMEM is released.
         umma_commit(drain_bar);
@@ -471,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
       tc_fence_after();
+      if (trace && ethread == 0 && i == 0) trace[5] = globaltimer();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
 
       if (!w.partial) {
@@ -568,8 +581,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // Teardown: every role has left its loop (normally or on abort).
+  if (trace && threadIdx.x == 64) trace[6] = globaltimer();
   tc_fence_before();
   __syncthreads();
+  if (trace && threadIdx.x == 0) trace[7] = globaltimer();
   if (warp == 1) {
     tc_fence_after();
     __syncwarp();

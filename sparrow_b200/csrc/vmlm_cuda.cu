@@ -97,6 +97,10 @@ int g_host_dev = -1;
 // Optional timing of the tensor-core GEMM launches (diagnostics): a CUDA event
 // pair on the launch stream around each launch, summed by vmlm_profile_take.
 bool g_profile = false;
+// Optional per-CTA phase timestamps of the tensor-core GEMM (diagnostics).
+unsigned long long* g_trace = nullptr;
+size_t g_trace_ctas = 0;
+int g_trace_dev = -1;
 struct ProfPair {
   cudaEvent_t a, b;
   int dev;
@@ -263,6 +267,7 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   p.slots = static_cast<uint32_t*>(c->slots.p);
   p.counters = static_cast<int*>(c->counters.p);
   p.err = c->err;
+  p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
   const TcSmem L = tc_smem_layout(stages, p.bn);
   if (!g_profile)
     return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma,
@@ -655,6 +660,35 @@ int vmlm_gemm_i8i8_dev(const int8_t* x, const int8_t* w, const float* scale, flo
   VMLM_TRY(current_ctx(&ctx));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_i8i8(ctx, x, w, scale, c, acc, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_trace_enable(int max_ctas) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_trace) {
+    cudaSetDevice(g_trace_dev);
+    cudaFree(g_trace);
+    g_trace = nullptr;
+    g_trace_ctas = 0;
+  }
+  if (max_ctas <= 0) return VMLM_OK;
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  const size_t bytes = static_cast<size_t>(max_ctas) * kTraceSlots * sizeof(unsigned long long);
+  VMLM_CUDA(cudaMalloc(&g_trace, bytes));
+  VMLM_CUDA(cudaMemset(g_trace, 0, bytes));
+  g_trace_ctas = static_cast<size_t>(max_ctas);
+  g_trace_dev = ctx->dev;
+  return VMLM_OK;
+}
+
+int vmlm_trace_take(uint64_t* host, size_t n_values) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!g_trace) return fail(VMLM_ERR_STATE, "trace: not enabled");
+  const size_t have = g_trace_ctas * kTraceSlots;
+  if (!host || n_values > have) return fail(VMLM_ERR_ARG, "trace: buffer larger than the trace");
+  VMLM_CUDA(cudaDeviceSynchronize());
+  VMLM_CUDA(cudaMemcpy(host, g_trace, n_values * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+  return VMLM_OK;
 }
 
 int vmlm_profile_enable(int on) {

@@ -102,6 +102,18 @@ def profile_enable(on: bool) -> None:
     check(lib().vmlm_profile_enable(1 if on else 0))
 
 
+def trace_enable(max_ctas: int) -> None:
+    """Record per-CTA phase timestamps of each GEMM launch (0 disables)."""
+    check(lib().vmlm_trace_enable(max_ctas))
+
+
+def trace_take(n_ctas: int) -> np.ndarray:
+    """The last traced launch: [n_ctas, 8] globaltimer stamps in ns."""
+    out = np.zeros((n_ctas, 8), np.uint64)
+    check(lib().vmlm_trace_take(ctypes.c_void_p(out.ctypes.data), out.size))
+    return out
+
+
 def profile_take():
     """(summed device ms, launches) of the GEMM launches recorded since the last take."""
     ms = ctypes.c_double(0.0)

@@ -306,4 +306,5 @@ def test_device_entry_points_match_host_ones(kernels, oracle):
     dcb = torch.empty((64, 1024), dtype=torch.float32, device="cuda")
     kernels.gemm_nt_bf16_dev(dxb, dwb, dcb, 64, 1024, 2304, stream=st)
     kernels.sync(st)
-    assert np.array_equal(dcb.cpu().numpy().view(np.uint32), hb.view(np.uint32))
+    # bf16 tiles split between CTAs are summed with f32 atomics: equal up to the last bits
+    assert oracle.max_rel_err(dcb.cpu().numpy(), hb) <= 1e-6
