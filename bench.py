@@ -120,9 +120,11 @@ def run_case(args):
         K.trace_enable(0)
         tr = tr[tr[:, 0] > 0]
         t0 = tr[:, 0].min()
-        names = ["start", "prologue", "tma_issued", "first_stage", "last_commit", "first_accum", "epi_done", "end"]
+        names = ["start", "prologue", "tma_issued", "first_stage", "last_commit", "first_accum", "epi_done", "end",
+                 "wait_empty", "wait_full", "wait_accum_free", "epi_wait"]
+        cols = [(tr[:, j] - t0) / 1e3 for j in range(8)] + [tr[:, j] / 1e3 for j in range(8, 12)]
         out["trace_us"] = {nm: [round(float(np.min(v)), 2), round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
-                           for nm, v in zip(names, ((tr[:, j] - t0) / 1e3 for j in range(8)))}
+                           for nm, v in zip(names, cols)}
         out["trace_ctas"] = int(tr.shape[0])
     print(json.dumps(out), flush=True)
 
@@ -240,6 +242,14 @@ def flush_l2(buf):
     left for it to write back."""
     buf.zero_()
     buf.sum()
+    # keep the GPU busy while the host enqueues the step, so the timed events
+    # measure device execution rather than host launch overhead
+    torch_sleep(100_000)
+
+
+def torch_sleep(cycles):
+    import torch
+    torch.cuda._sleep(cycles)
 
 
 def time_steps(step, k, warmup, flush, dist=None):

@@ -3,7 +3,7 @@
 //
 // Q8 activations are encoded as three signed 8-bit digit planes per token:
 //   e   = 22 - E  where max|x_t| = f * 2^E, f in [0.5, 1)   (e = 0 for a zero row)
-//   X   = rint(x * 2^e)              |X| <= 2^22, exact scaling in f64
+//   X   = rint(x * 2^e)              |X| <= 2^22; the power-of-two scaling is exact
 //   X   = d0 + 256*d1 + 65536*d2     d0, d1 in [-128,127], d2 in [-64,64]
 // so sum_k x_k*q_k = 2^-e * sum_p 256^p * (sum_k d_p,k * q_k) up to the
 // 2^-23*max|x| rounding of X; the three int32 sums are exact.
@@ -11,6 +11,10 @@
 // bf16 activations (f32 in, bf16 weights) are split into three bf16 terms
 //   hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
 // (each difference is exact in f32), which carry 24 significant bits.
+//
+// Both kernels run one CTA per token and keep the row in registers (up to
+// kPrepThreads * kPrepVec elements; longer rows are read twice), with one
+// block reduction for the row's flags.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -20,43 +24,68 @@
 
 namespace vmlm {
 
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 512;
+constexpr int kPrepVec = 16;  // elements per thread kept in registers (4 float4)
 
-__device__ __forceinline__ float block_max(float v, float* red) {
+__device__ __forceinline__ float warp_max(float v) {
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_or(int v) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide max of a float and OR of an int in one pass (two shared arrays).
+__device__ __forceinline__ void block_max_or(float& m, int& o, float* redf, int* redi) {
+  m = warp_max(m);
+  o = warp_or(o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = (l < (blockDim.x >> 5)) ? red[l] : 0.f;
-    #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (l == 0) red[0] = v;
+  if (l == 0) {
+    redf[w] = m;
+    redi[w] = o;
   }
   __syncthreads();
-  return red[0];
+  const int nw = blockDim.x >> 5;
+  m = (l < nw) ? redf[l] : 0.f;
+  o = (l < nw) ? redi[l] : 0;
+  m = warp_max(m);
+  o = warp_or(o);
 }
 
 __device__ __forceinline__ int block_or(int v, int* red) {
-  #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+  v = warp_or(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   __syncthreads();
   if (l == 0) red[w] = v;
   __syncthreads();
-  if (w == 0) {
-    v = (l < (blockDim.x >> 5)) ? red[l] : 0;
-    #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
-    if (l == 0) red[0] = v;
-  }
-  __syncthreads();
-  return red[0];
+  v = (l < static_cast<int>(blockDim.x >> 5)) ? red[l] : 0;
+  return warp_or(v);
+}
+
+// x * 2^e exactly (power-of-two scaling), for any e the encoder produces.
+__device__ __forceinline__ float scale_pow2(float x, int e) {
+  if (e >= -126 && e <= 127) return __fmul_rn(x, __int_as_float((127 + e) << 23));
+  return scalbnf(x, e);
+}
+
+__device__ __forceinline__ void q8_digits(float x, int e, int& d0, int& d1, int& d2) {
+  const int X = __float2int_rn(scale_pow2(x, e));
+  d0 = ((X + 128) & 255) - 128;
+  const int X1 = (X - d0) >> 8;
+  d1 = ((X1 + 128) & 255) - 128;
+  d2 = (X1 - d1) >> 8;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 255u) | ((static_cast<uint32_t>(b) & 255u) << 8) |
+         ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
 }
 
 // One CTA per token. planes: [3*M][kp] int8, row 3t+p. Columns [K, kp) are 0.
+// Requires kp % 16 == 0.
 __global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __restrict__ x, long long ldx, int M,
                                                                  int K, int kp, int8_t* __restrict__ planes,
                                                                  int* __restrict__ exps, int* __restrict__ nonfinite) {
@@ -66,36 +95,73 @@ __global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __
   const int t = blockIdx.x;
   if (t >= M) return;
   const float* xr = x + static_cast<long long>(t) * ldx;
+  const bool vec = ((K & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
+  const int nchunk = (kp + 3) >> 2;  // 4-element chunks covering [0, kp)
+  float4 reg[kPrepVec / 4];
   float amax = 0.f;
   int bad = 0;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    const float v = xr[k];
-    if (!isfinite(v))
-      bad = 1;
-    else
-      amax = fmaxf(amax, fabsf(v));
+  #pragma unroll
+  for (int i = 0; i < kPrepVec / 4; ++i) {
+    const int ch = threadIdx.x + i * blockDim.x;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ch < nchunk) {
+      const int k = ch * 4;
+      if (vec && k + 3 < K) {
+        v = *reinterpret_cast<const float4*>(xr + k);
+      } else {
+        v.x = k < K ? xr[k] : 0.f;
+        v.y = k + 1 < K ? xr[k + 1] : 0.f;
+        v.z = k + 2 < K ? xr[k + 2] : 0.f;
+        v.w = k + 3 < K ? xr[k + 3] : 0.f;
+      }
+    }
+    reg[i] = v;
+    bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
-  amax = block_max(amax, redf);
-  bad = block_or(bad, redi);
+  for (int ch = threadIdx.x + kPrepVec / 4 * blockDim.x; ch < nchunk; ch += blockDim.x) {
+    for (int j = 0; j < 4; ++j) {
+      const int k = ch * 4 + j;
+      const float v = k < K ? xr[k] : 0.f;
+      bad |= !isfinite(v);
+      amax = fmaxf(amax, fabsf(v));
+    }
+  }
+  block_max_or(amax, bad, redf, redi);
   int e = 0;
   if (!bad && amax > 0.f) {
     int E;
     frexpf(amax, &E);
     e = 22 - E;
   }
-  int8_t* p0 = planes + static_cast<long long>(3 * t) * kp;
-  int8_t* p1 = p0 + kp;
-  int8_t* p2 = p1 + kp;
-  for (int k = threadIdx.x; k < kp; k += blockDim.x) {
-    int X = 0;
-    if (k < K && !bad) X = __double2int_rn(ldexp(static_cast<double>(xr[k]), e));
-    const int d0 = ((X + 128) & 255) - 128;
-    const int X1 = (X - d0) >> 8;
-    const int d1 = ((X1 + 128) & 255) - 128;
-    const int d2 = (X1 - d1) >> 8;
-    p0[k] = static_cast<int8_t>(d0);
-    p1[k] = static_cast<int8_t>(d1);
-    p2[k] = static_cast<int8_t>(d2);
+  uint32_t* p0 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t) * kp);
+  uint32_t* p1 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t + 1) * kp);
+  uint32_t* p2 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t + 2) * kp);
+  #pragma unroll
+  for (int i = 0; i < kPrepVec / 4; ++i) {
+    const int ch = threadIdx.x + i * blockDim.x;
+    if (ch < nchunk) {
+      int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
+      const float4 v = bad ? make_float4(0.f, 0.f, 0.f, 0.f) : reg[i];
+      q8_digits(v.x, e, a0, a1, a2);
+      q8_digits(v.y, e, b0, b1, b2);
+      q8_digits(v.z, e, c0, c1, c2);
+      q8_digits(v.w, e, f0, f1, f2);
+      p0[ch] = pack4(a0, b0, c0, f0);
+      p1[ch] = pack4(a1, b1, c1, f1);
+      p2[ch] = pack4(a2, b2, c2, f2);
+    }
+  }
+  for (int ch = threadIdx.x + kPrepVec / 4 * blockDim.x; ch < nchunk; ch += blockDim.x) {
+    int d[3][4];
+    for (int j = 0; j < 4; ++j) {
+      const int k = ch * 4 + j;
+      const float v = (k < K && !bad) ? xr[k] : 0.f;
+      q8_digits(v, e, d[0][j], d[1][j], d[2][j]);
+    }
+    p0[ch] = pack4(d[0][0], d[0][1], d[0][2], d[0][3]);
+    p1[ch] = pack4(d[1][0], d[1][1], d[1][2], d[1][3]);
+    p2[ch] = pack4(d[2][0], d[2][1], d[2][2], d[2][3]);
   }
   if (threadIdx.x == 0) {
     exps[t] = e;
@@ -114,11 +180,30 @@ __device__ __forceinline__ uint16_t bf16_rn_bits(float v) {
 
 __device__ __forceinline__ float bf16_val(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
 
+// Three bf16 terms of one value; flags |= 2 / 4 for a non-zero mid / lo term,
+// 256 for a non-finite value (which keeps only hi: NaN or +-Inf).
+__device__ __forceinline__ void bf16_split(float v, uint16_t& h, uint16_t& m, uint16_t& l, int& flags) {
+  if (!isfinite(v)) {
+    flags |= 256;
+    h = (v != v) ? 0x7fc0u : static_cast<uint16_t>(__float_as_uint(v) >> 16);
+    m = 0;
+    l = 0;
+    return;
+  }
+  h = bf16_rn_bits(v);
+  const float r1 = __fsub_rn(v, bf16_val(h));
+  m = bf16_rn_bits(r1);
+  const float r2 = __fsub_rn(r1, bf16_val(m));
+  l = bf16_rn_bits(r2);
+  if (m & 0x7fffu) flags |= 2;
+  if (l & 0x7fffu) flags |= 4;
+}
+
 // One CTA per token. Layout 0 (swap): out[(3t+j)*kp + k]. Layout 1 (normal):
-// out[t*3*kp + j*kp + k]. Columns [K, kp) are 0. term_flags[t] |= 1<<j for
-// every term j that is non-zero somewhere in the row. The last CTA to finish
-// (counted on done[0], which it resets) ORs all rows into done[1], so a
-// consumer reads one word instead of M.
+// out[t*3*kp + j*kp + k]. Columns [K, kp) are 0; kp % 8 == 0. term_flags[t]
+// gets 1 | (2 if a mid term is non-zero) | (4 if a lo term is non-zero). The
+// last CTA to finish (counted on done[0], which it resets) ORs all rows into
+// done[1], so a consumer reads one word instead of M.
 __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* __restrict__ x, long long ldx, int M,
                                                                   int K, int kp, int layout,
                                                                   uint16_t* __restrict__ out,
@@ -131,37 +216,39 @@ __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* _
   const int t = blockIdx.x;
   if (t >= M) return;
   const float* xr = x + static_cast<long long>(t) * ldx;
+  const bool vec = ((K & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
   uint16_t* o0 = layout == 0 ? out + static_cast<long long>(3 * t) * kp : out + static_cast<long long>(t) * 3 * kp;
   uint16_t* o1 = o0 + kp;
   uint16_t* o2 = o1 + kp;
-  int flags = 0, bad = 0;
-  for (int k = threadIdx.x; k < kp; k += blockDim.x) {
-    uint16_t h = 0, m = 0, l = 0;
-    if (k < K) {
-      const float v = xr[k];
-      if (!isfinite(v)) {
-        bad = 1;
-        h = static_cast<uint16_t>(__float_as_uint(v) >> 16);
-        if (v != v) h = 0x7fc0u;
-      } else {
-        h = bf16_rn_bits(v);
-        const float r1 = __fsub_rn(v, bf16_val(h));
-        m = bf16_rn_bits(r1);
-        const float r2 = __fsub_rn(r1, bf16_val(m));
-        l = bf16_rn_bits(r2);
-      }
+  const int nchunk = kp >> 2;  // kp % 8 == 0
+  int flags = 0;
+  for (int ch = threadIdx.x; ch < nchunk; ch += blockDim.x) {
+    const int k = ch * 4;
+    float4 v;
+    if (vec && k + 3 < K) {
+      v = *reinterpret_cast<const float4*>(xr + k);
+    } else {
+      v.x = k < K ? xr[k] : 0.f;
+      v.y = k + 1 < K ? xr[k + 1] : 0.f;
+      v.z = k + 2 < K ? xr[k + 2] : 0.f;
+      v.w = k + 3 < K ? xr[k + 3] : 0.f;
     }
-    o0[k] = h;
-    o1[k] = m;
-    o2[k] = l;
-    if (m & 0x7fffu) flags |= 2;
-    if (l & 0x7fffu) flags |= 4;
+    uint16_t h[4], m[4], l[4];
+    bf16_split(v.x, h[0], m[0], l[0], flags);
+    bf16_split(v.y, h[1], m[1], l[1], flags);
+    bf16_split(v.z, h[2], m[2], l[2], flags);
+    bf16_split(v.w, h[3], m[3], l[3], flags);
+    reinterpret_cast<uint2*>(o0)[ch] = make_uint2(h[0] | (static_cast<uint32_t>(h[1]) << 16),
+                                                  h[2] | (static_cast<uint32_t>(h[3]) << 16));
+    reinterpret_cast<uint2*>(o1)[ch] = make_uint2(m[0] | (static_cast<uint32_t>(m[1]) << 16),
+                                                  m[2] | (static_cast<uint32_t>(m[3]) << 16));
+    reinterpret_cast<uint2*>(o2)[ch] = make_uint2(l[0] | (static_cast<uint32_t>(l[1]) << 16),
+                                                  l[2] | (static_cast<uint32_t>(l[3]) << 16));
   }
   flags = block_or(flags, redi);
-  bad = block_or(bad, redi);
   if (threadIdx.x == 0) {
-    term_flags[t] = flags | 1;
-    nonfinite[t] = bad;
+    term_flags[t] = (flags & 6) | 1;
+    nonfinite[t] = (flags >> 8) & 1;
     __threadfence();
     is_last = (atomicAdd(done, 1u) == static_cast<unsigned>(M - 1));
   }
@@ -204,7 +291,7 @@ __global__ void q8_generic_kernel(const int8_t* __restrict__ q, const float* __r
     out = __fmul_rn(s, scale[n]);
   } else {
     const int8_t* p0 = planes + static_cast<long long>(3 * t) * kp;
-    int a0 = 0, a1 = 0, a2 = 0;
+    long long a0 = 0, a1 = 0, a2 = 0;
     for (int k = lane; k < K; k += 32) {
       const int w = qr[k];
       a0 += w * p0[k];
@@ -217,7 +304,7 @@ __global__ void q8_generic_kernel(const int8_t* __restrict__ q, const float* __r
       a1 += __shfl_xor_sync(0xffffffffu, a1, o);
       a2 += __shfl_xor_sync(0xffffffffu, a2, o);
     }
-    const long long v = static_cast<long long>(a2) * 65536ll + static_cast<long long>(a1) * 256ll + a0;
+    const long long v = a2 * 65536ll + a1 * 256ll + a0;
     out = __fmul_rn(__double2float_rn(ldexp(static_cast<double>(v), -exps[t])), scale[n]);
   }
   if (lane == 0) c[static_cast<long long>(t) * ldc + n] = out;

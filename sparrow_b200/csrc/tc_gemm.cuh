@@ -36,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 
@@ -87,10 +88,13 @@ struct TcParams {
   unsigned long long* trace;  // optional: kTraceSlots globaltimer stamps per CTA (diagnostics)
 };
 
-// Trace slots (per CTA): kernel start, after prologue, producer done issuing,
-// first stage consumed by the MMA warp, last accumulator committed, first
-// accumulator seen by the epilogue, epilogue done, kernel end.
-constexpr int kTraceSlots = 8;
+// Trace slots (per CTA): [0] kernel start, [1] producer past the wait for the
+// previous kernel, [2] producer done issuing, [3] first stage consumed by the
+// MMA warp, [4] last accumulator committed, [5] first accumulator seen by the
+// epilogue, [6] epilogue done, [7] TMEM released; then summed waits (ns):
+// [8] producer for free stages, [9] MMA for loaded stages, [10] MMA for a free
+// accumulator, [11] epilogue for a finished accumulator.
+constexpr int kTraceSlots = 12;
 
 struct TcSmem {
   uint32_t a_off, b_off, bar_off, meta_off;  // offsets from the 1024-aligned base
@@ -104,8 +108,8 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, int bn) {
   s.a_off = 0;
   s.b_off = s.a_off + stages * s.a_bytes;
   s.bar_off = s.b_off + stages * s.b_bytes;
-  // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, then 64 bytes of words
-  s.meta_off = s.bar_off + (2 * stages + 5) * 8 + 64;
+  // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, done, then 64 bytes of words
+  s.meta_off = s.bar_off + (2 * stages + 6) * 8 + 64;
   // per-tile token table: exps[kMaxTokPerTile], nonfinite[kMaxTokPerTile]; +1024 for base alignment
   s.total = s.meta_off + 2 * kMaxTokPerTile * 4 + 1024;
   return s;
@@ -246,9 +250,52 @@ __device__ float nonfinite_dot(const TcParams& p, int t, int n) {
   }
 }
 
-// Finish 16 tokens (48 accumulator columns, token-major triples) of one weight
-// row in a swap mode. lt0 is the chunk's first token within the tile, tok0 the
-// tile's first token; s_exp / s_bad hold the tile's per-token metadata.
+// Swap modes combine one token's three accumulator columns (token-major
+// triples) into one value: the exact int64 digit-plane sum for Q8, the f32 sum
+// of the three split terms for bf16. Split tiles reduce these combined values.
+template <TcMode MODE>
+struct SwapVal {
+  using T = typename std::conditional<MODE == TcMode::kQ8Swap, unsigned long long, float>::type;
+};
+
+template <TcMode MODE>
+__device__ __forceinline__ typename SwapVal<MODE>::T swap_combine(const uint32_t* v3) {
+  if constexpr (MODE == TcMode::kQ8Swap) {
+    const long long a0 = static_cast<int>(v3[0]);
+    const long long a1 = static_cast<int>(v3[1]);
+    const long long a2 = static_cast<int>(v3[2]);
+    return static_cast<unsigned long long>(a2 * 65536ll + a1 * 256ll + a0);
+  } else {
+    return __fadd_rn(__uint_as_float(v3[0]), __fadd_rn(__uint_as_float(v3[1]), __uint_as_float(v3[2])));
+  }
+}
+
+// Final value of output (t, n) from a token's combined accumulator. Q8:
+// C = f32(v * 2^-e) * scale[n]. When v * 2^-e is a normal float (|e| in the
+// checked range, v an integer), rounding v to f32 and then scaling by the exact
+// power of two gives the same bits as the f64 route used otherwise.
+template <TcMode MODE>
+__device__ __forceinline__ void swap_finish(const TcParams& p, int n, int t, int lt, typename SwapVal<MODE>::T val,
+                                            float sc, const int* s_exp, const int* s_bad) {
+  float r;
+  if (s_bad[lt]) {
+    r = nonfinite_dot<MODE>(p, t, n);
+  } else if constexpr (MODE == TcMode::kQ8Swap) {
+    const long long v = static_cast<long long>(val);
+    const int e = s_exp[lt];
+    if (e >= -70 && e <= 100) {
+      r = __fmul_rn(__fmul_rn(__ll2float_rn(v), __int_as_float((127 - e) << 23)), sc);
+    } else {
+      r = __fmul_rn(__double2float_rn(ldexp(static_cast<double>(v), -e)), sc);
+    }
+  } else {
+    r = val;
+  }
+  p.out[static_cast<long long>(t) * p.ldo + n] = r;
+}
+
+// Finish 16 tokens (48 accumulator columns) of one weight row of a whole tile.
+// lt0 is the chunk's first token within the tile, tok0 the tile's first token.
 template <TcMode MODE>
 __device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, int lt0, float sc, const int* s_exp,
                                            const int* s_bad, const uint32_t (&v)[48]) {
@@ -257,24 +304,7 @@ __device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, i
   for (int j = 0; j < 16; ++j) {
     const int lt = lt0 + j;
     const int t = tok0 + lt;
-    if (t >= p.n_tokens) break;
-    float r;
-    if (s_bad[lt]) {
-      r = nonfinite_dot<MODE>(p, t, n);
-    } else if constexpr (MODE == TcMode::kQ8Swap) {
-      const long long a0 = static_cast<int>(v[3 * j + 0]);
-      const long long a1 = static_cast<int>(v[3 * j + 1]);
-      const long long a2 = static_cast<int>(v[3 * j + 2]);
-      const long long vsum = a2 * 65536ll + a1 * 256ll + a0;
-      const double d = ldexp(static_cast<double>(vsum), -s_exp[lt]);
-      r = __fmul_rn(__double2float_rn(d), sc);
-    } else {
-      const float hi = __uint_as_float(v[3 * j + 0]);
-      const float mid = __uint_as_float(v[3 * j + 1]);
-      const float lo = __uint_as_float(v[3 * j + 2]);
-      r = __fadd_rn(hi, __fadd_rn(mid, lo));
-    }
-    p.out[static_cast<long long>(t) * p.ldo + n] = r;
+    if (t < p.n_tokens) swap_finish<MODE>(p, n, t, lt, swap_combine<MODE>(v + 3 * j), sc, s_exp, s_bad);
   }
 }
 
@@ -311,7 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull_bar = empty_bar + p.stages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* done_bar = drain_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 2);
   int* s_exp = reinterpret_cast<int*>(smem + L.meta_off);
@@ -332,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty_bar + b, 4);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(done_bar, 4);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -343,27 +375,57 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Everything below may read what the previous kernel in the stream wrote.
-  pdl_wait_prior();
-  if (trace && threadIdx.x == 0) trace[1] = globaltimer();
-
-  const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
-  Sched sc;
-  sc.kb_tile = p.kb_per_term * T;
-  sc.tiles = p.tiles_m * p.tiles_n;
-  sc.units = static_cast<long long>(sc.tiles) * sc.kb_tile;
-  sc.grid = gridDim.x;
-  sc.streamk = p.streamk;
   const int cta = blockIdx.x;
+  // Schedule with T active terms (T only differs from 1 in kBf16Norm).
+  auto make_sched = [&](int T) {
+    Sched s;
+    s.kb_tile = p.kb_per_term * T;
+    s.tiles = p.tiles_m * p.tiles_n;
+    s.units = static_cast<long long>(s.tiles) * s.kb_tile;
+    s.grid = gridDim.x;
+    s.streamk = p.streamk;
+    return s;
+  };
+  // The weights (A in swap modes, B in normal modes) do not depend on the
+  // previous kernel in the stream; the activations do. The producer issues the
+  // weight half of its first stages before waiting for that kernel, so the
+  // weight stream overlaps the activation preparation.
+  constexpr bool kWeightIsA = kSwap;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
+      int npre = 0;  // stages of item 0 whose weight half is already in flight
+      {
+        // Item 0 and its first term-0 k-blocks are the same for every T (the
+        // normal-mode schedule used with term passes is round-robin).
+        const Sched s1 = make_sched(1);
+        long long cur0 = 0;
+        WorkItem w0;
+        const bool pre_ok = (MODE != TcMode::kBf16Norm) || !p.streamk;
+        if (pre_ok && s1.item(cta, 0, cur0, w0)) {
+          const int tm0 = p.tm_fastest ? w0.tile % p.tiles_m : w0.tile / p.tiles_n;
+          const int tn0 = p.tm_fastest ? w0.tile / p.tiles_m : w0.tile % p.tiles_n;
+          npre = min(p.stages, min(w0.kb1, p.kb_per_term) - w0.kb0);
+          for (int s = 0; s < npre; ++s) {
+            const int kx = (w0.kb0 + s) * p.a_box_elems;
+            mbar_arrive_expect_tx(full_bar + s, L.a_bytes + L.b_bytes);
+            if (kWeightIsA)
+              tma_load_2d(smem + L.a_off + s * L.a_bytes, &tmA, full_bar + s, kx, tm0 * kTileRows, pol_a);
+            else
+              tma_load_2d(smem + L.b_off + s * L.b_bytes, &tmB, full_bar + s, kx, tn0 * p.bn, pol_b);
+          }
+        }
+      }
+      pdl_wait_prior();
+      if (trace) trace[1] = globaltimer();
+      const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, last_phase = 0;  // per stage: ever issued / parity of last issue
+      unsigned long long wait_empty = 0;         // trace: time waiting for free stages
       long long cur = 0;
       WorkItem w;
       bool ok = true;
@@ -371,13 +433,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tm = p.tm_fastest ? w.tile % p.tiles_m : w.tile / p.tiles_n;
         const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
+          const bool pre = (i == 0 && kb - w.kb0 < npre);
+          const unsigned long long tw = trace ? globaltimer() : 0;
+          if (!pre && !mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
+          if (trace) wait_empty += globaltimer() - tw;
           uint8_t* sa = smem + L.a_off + stage * L.a_bytes;
           uint8_t* sb = smem + L.b_off + stage * L.b_bytes;
-          mbar_arrive_expect_tx(full_bar + stage, L.a_bytes + L.b_bytes);
+          if (!pre) mbar_arrive_expect_tx(full_bar + stage, L.a_bytes + L.b_bytes);
           int ka, kbx;
           if constexpr (MODE == TcMode::kBf16Norm) {
             const int term = kb / p.kb_per_term, kin = kb % p.kb_per_term;
@@ -387,8 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ka = kb * p.a_box_elems;
             kbx = ka;
           }
-          tma_load_2d(sa, &tmA, full_bar + stage, ka, tm * kTileRows, pol_a);
-          tma_load_2d(sb, &tmB, full_bar + stage, kbx, tn * p.bn, pol_b);
+          if (!pre || !kWeightIsA) tma_load_2d(sa, &tmA, full_bar + stage, ka, tm * kTileRows, pol_a);
+          if (!pre || kWeightIsA) tma_load_2d(sb, &tmB, full_bar + stage, kbx, tn * p.bn, pol_b);
           issued_mask |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
@@ -397,7 +462,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (trace) trace[2] = globaltimer();
+      if (trace) {
+        trace[2] = globaltimer();
+        trace[8] = wait_empty;
+      }
       if (*abort_flag) {
         // Copies already issued must land before this CTA's shared memory is released.
         for (int s = 0; s < p.stages; ++s)
@@ -408,22 +476,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
+      pdl_wait_prior();
+      const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
       int stage = 0;
       uint32_t phase = 0;
       long long cur = 0;
       WorkItem w;
       bool ok = true;
       bool issued = false;
+      unsigned long long wait_accum = 0, wait_full = 0;  // trace: time waiting for TMEM / for stages
       for (int i = 0; ok && sc.item(cta, i, cur, w); ++i) {
         const int buf = i & 1;
+        const unsigned long long tw0 = trace ? globaltimer() : 0;
         if (!mbar_wait(tempty_bar + buf, ((i >> 1) & 1) ^ 1, p.err, abort_flag, kDevTimeoutAccumFree)) break;
+        if (trace) wait_accum += globaltimer() - tw0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          const unsigned long long tw1 = trace ? globaltimer() : 0;
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
             break;
           }
+          if (trace) wait_full += globaltimer() - tw1;
           tc_fence_after();
           if (trace && !issued) trace[3] = globaltimer();
           const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
@@ -448,7 +523,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         umma_commit(tfull_bar + buf);
       }
-      if (trace) trace[4] = globaltimer();
+      if (trace) {
+        trace[4] = globaltimer();
+        trace[9] = wait_full;
+        trace[10] = wait_accum;
+      }
       if (issued && *abort_flag) {
         // Let in-flight MMAs finish before TMEM is released.
         umma_commit(drain_bar);
@@ -460,6 +539,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;   // accumulator row within the tile
     const int ethread = threadIdx.x - 64;  // 0..127
+    pdl_wait_prior();
+    const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
+    unsigned long long epi_wait = 0;  // trace: time waiting for accumulators
     long long cur = 0;
     WorkItem w;
     for (int i = 0; sc.item(cta, i, cur, w); ++i) {
@@ -481,7 +563,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (MODE == TcMode::kQ8Swap && grow < p.n_out) scale_n = __ldg(p.scale + grow);
         named_bar_sync(1, kEpiThreads);
       }
+      const unsigned long long tw = trace ? globaltimer() : 0;
       if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
+      if (trace) epi_wait += globaltimer() - tw;
       tc_fence_after();
       if (trace && ethread == 0 && i == 0) trace[5] = globaltimer();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
@@ -524,12 +608,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
       const int slot = sc.owner(tile_u0 + sc.kb_tile - 1);
       uint32_t* srow = p.slots + (static_cast<long long>(slot) * kTileRows + row) * p.bn;
-      for (int c = 0; c < p.bn; c += 16) {
-        uint32_t v[16];
-        __syncwarp();
-        tmem_ld16(tbase + c, v);
-        tmem_ld_wait();
-        slot_add16<kInt>(srow + c, v);
+      // swap modes: one combined value per real token, row-major [128][tok_per_tile]
+      using SV = typename SwapVal<MODE>::T;
+      SV* vrow = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) +
+                 static_cast<long long>(row) * p.tok_per_tile;
+      if constexpr (kSwap) {
+        for (int c = 0; c < p.bn; c += 48) {
+          uint32_t v[48];
+          __syncwarp();
+          tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+          tmem_ld16(tbase + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+          tmem_ld16(tbase + c + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
+          tmem_ld_wait();
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int lt = c / 3 + j;
+            if (tok0 + lt < p.n_tokens) atomicAdd(vrow + lt, swap_combine<MODE>(v + 3 * j));
+          }
+        }
+      } else {
+        for (int c = 0; c < p.bn; c += 16) {
+          uint32_t v[16];
+          __syncwarp();
+          tmem_ld16(tbase + c, v);
+          tmem_ld_wait();
+          slot_add16<kInt>(srow + c, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -547,19 +651,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!last) continue;
       __threadfence();
       if constexpr (kSwap) {
-        for (int c = 0; c < p.bn; c += 48) {
-          uint32_t v[48];
+        const int ntok = min(p.tok_per_tile, p.n_tokens - tok0);
+        for (int lt0 = 0; lt0 < ntok; lt0 += 8) {
+          SV vals[8];
           #pragma unroll
-          for (int j = 0; j < 48; j += 4) {
-            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(srow + c + j));
-            v[j] = u.x;
-            v[j + 1] = u.y;
-            v[j + 2] = u.z;
-            v[j + 3] = u.w;
+          for (int j = 0; j < 8; ++j) vals[j] = (lt0 + j < ntok) ? __ldcg(vrow + lt0 + j) : SV(0);
+          #pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (lt0 + j < ntok) __stcg(vrow + lt0 + j, SV(0));
+          if (grow < p.n_out) {
+            #pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (lt0 + j < ntok)
+                swap_finish<MODE>(p, grow, tok0 + lt0 + j, lt0 + j, vals[j], scale_n, s_exp, s_bad);
           }
-          #pragma unroll
-          for (int j = 0; j < 48; j += 4) __stcg(reinterpret_cast<uint4*>(srow + c + j), make_uint4(0, 0, 0, 0));
-          epi_swap48<MODE>(p, grow, tok0, c / 3, scale_n, s_exp, s_bad, v);
         }
       } else {
         for (int c = 0; c < p.bn; c += 16) {
@@ -580,15 +685,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // Teardown: every role has left its loop (normally or on abort).
-  if (trace && threadIdx.x == 64) trace[6] = globaltimer();
-  tc_fence_before();
-  __syncthreads();
-  if (trace && threadIdx.x == 0) trace[7] = globaltimer();
+  // Teardown: every role has left its loop (normally or on abort). The
+  // epilogue warps report on done_bar; the TMEM owner waits for all four
+  // before releasing TMEM (a CTA-wide barrier is not used here because warps
+  // 0 and 1 reach it from divergent single-lane loops).
+  if (warp >= 2) {
+    if (trace && threadIdx.x == 64) {
+      trace[6] = globaltimer();
+      trace[11] = epi_wait;
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(done_bar);
+  }
   if (warp == 1) {
+    __syncwarp();
+    mbar_wait(done_bar, 0, p.err, abort_flag, kDevTimeoutDrain, false);
     tc_fence_after();
     __syncwarp();
     tmem_dealloc(tmem_base, p.tmem_cols);
+    if (trace && lane == 0) trace[7] = globaltimer();
   }
 }
 

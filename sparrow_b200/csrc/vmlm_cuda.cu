@@ -225,6 +225,13 @@ inline int pow2_at_least(int v) {
   return p;
 }
 
+// Decode GEMMs with fewer tiles than a few waves split tiles between CTAs
+// (stream-K) to keep every SM streaming weights; with more tiles, whole tiles
+// round-robin lose little to the last partial wave and need no fixup.
+bool use_streamk(const TcParams& p, int sms) {
+  return static_cast<long long>(p.tiles_m) * p.tiles_n < 4ll * sms;
+}
+
 // Tile width for a normal-mode GEMM (rows x N output, 128-row tiles, whole
 // tiles round-robin over the SMs): the narrowest widths fill more SMs but run
 // the tensor cores less efficiently, so pick the width with the least
@@ -342,7 +349,7 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn));
-  return run_tc<TcMode::kQ8Swap>(c, st, ma, mb, p, true, true);
+  return run_tc<TcMode::kQ8Swap>(c, st, ma, mb, p, use_streamk(p, c->sms), true);
 }
 
 // ------------------------------------------------------------ bf16 path
@@ -392,7 +399,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
     p.n_out = N;
     VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, kTileRows));
     VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, K, 3ull * M, 2ull * kp, 64, p.bn));
-    return run_tc<TcMode::kBf16Swap>(c, st, ma, mb, p, true, true);
+    return run_tc<TcMode::kBf16Swap>(c, st, ma, mb, p, use_streamk(p, c->sms), true);
   }
   p.rows = M;
   p.cols = N;
