@@ -391,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // weight half of its first stages before waiting for that kernel, so the
   // weight stream overlaps the activation preparation.
   constexpr bool kWeightIsA = kSwap;
+  unsigned long long epi_wait = 0;  // trace: epilogue time waiting for accumulators
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -541,7 +542,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ethread = threadIdx.x - 64;  // 0..127
     pdl_wait_prior();
     const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
-    unsigned long long epi_wait = 0;  // trace: time waiting for accumulators
     long long cur = 0;
     WorkItem w;
     for (int i = 0; sc.item(cta, i, cur, w); ++i) {
