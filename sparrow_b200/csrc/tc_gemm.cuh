@@ -82,7 +82,8 @@ struct TcParams {
   const void* w;     // int8 or bf16 weight rows (row stride k)
   int k;
   // split-tile fixup
-  uint32_t* slots;   // [grid][128][bn] 32-bit accumulators, all zero between calls
+  uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
+  uint32_t* pieces;  // normal modes: [2*grid] slots of [bn][128] 32-bit partials (overwritten)
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int* err;          // device error word
   unsigned long long* trace;  // optional: kTraceSlots globaltimer stamps per CTA (diagnostics)
@@ -97,7 +98,7 @@ struct TcParams {
 constexpr int kTraceSlots = 12;
 
 struct TcSmem {
-  uint32_t a_off, b_off, bar_off, meta_off;  // offsets from the 1024-aligned base
+  uint32_t a_off, b_off, bar_off, meta_off, stg_off;  // offsets from the 1024-aligned base
   uint32_t a_bytes, b_bytes, total;
 };
 
@@ -110,8 +111,10 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, int bn) {
   s.bar_off = s.b_off + stages * s.b_bytes;
   // full[stages], empty[stages], tmem_full[2], tmem_empty[2], drain, done, then 64 bytes of words
   s.meta_off = s.bar_off + (2 * stages + 6) * 8 + 64;
-  // per-tile token table: exps[kMaxTokPerTile], nonfinite[kMaxTokPerTile]; +1024 for base alignment
-  s.total = s.meta_off + 2 * kMaxTokPerTile * 4 + 1024;
+  // per-tile token table: exps[kMaxTokPerTile], nonfinite[kMaxTokPerTile]
+  s.stg_off = s.meta_off + 2 * kMaxTokPerTile * 4;
+  // per-epilogue-warp store staging (32 rows x 17 words); +1024 for base alignment
+  s.total = s.stg_off + 4 * 32 * 17 * 4 + 1024;
   return s;
 }
 
@@ -180,54 +183,53 @@ __device__ __forceinline__ int active_terms(const TcParams& p) {
 
 // ------------------------------------------------------------- epilogues
 
-// Finish 16 columns [col0, col0+16) of one accumulator row in a normal mode.
-template <TcMode MODE>
-__device__ __forceinline__ void epi_norm16(const TcParams& p, int row, int col0, const uint32_t (&v)[16]) {
-  if (row >= p.rows) return;
-  float* crow = p.out ? p.out + static_cast<long long>(row) * p.ldo : nullptr;
-  const bool full = (col0 + 16 <= p.cols) && p.vec_out;
-  if constexpr (MODE == TcMode::kI8Norm) {
-    if (p.acc_out) {
-      int32_t* arow = p.acc_out + static_cast<long long>(row) * p.ldo;
-      if (full) {
-        #pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<int4*>(arow + col0 + j) =
-              make_int4(static_cast<int>(v[j]), static_cast<int>(v[j + 1]), static_cast<int>(v[j + 2]),
-                        static_cast<int>(v[j + 3]));
+// Store a 32-row x 16-column block held one row per lane (lane = row - row0)
+// through a per-warp shared buffer, so that each store instruction writes 8
+// rows x 64 contiguous bytes instead of 32 rows x 16 bytes.
+__device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, int row0, int nrows, int col0,
+                                                  int ncols, bool vec, uint32_t* buf, const uint32_t (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+  #pragma unroll
+  for (int j = 0; j < 16; ++j) buf[lane * 17 + j] = v[j];
+  __syncwarp();
+  #pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const int c = (lane & 3) * 4;
+    const int grow = row0 + r;
+    if (grow < nrows) {
+      uint32_t* d = dst + static_cast<long long>(grow) * ld + col0 + c;
+      const uint32_t* s = buf + r * 17 + c;
+      if (vec && col0 + c + 4 <= ncols) {
+        *reinterpret_cast<uint4*>(d) = make_uint4(s[0], s[1], s[2], s[3]);
       } else {
-        for (int j = 0; j < 16; ++j)
-          if (col0 + j < p.cols) arow[col0 + j] = static_cast<int>(v[j]);
+        for (int j = 0; j < 4; ++j)
+          if (col0 + c + j < ncols) d[j] = s[j];
       }
     }
-    if (crow) {
-      float f[16];
+  }
+  __syncwarp();
+}
+
+// Finish 16 columns [col0, col0+16) of the warp's 32 accumulator rows
+// (row0 = first row of the warp) in a normal mode. s_scale points at the
+// chunk's 16 column scales in shared memory (kI8Norm).
+template <TcMode MODE>
+__device__ __forceinline__ void epi_norm16(const TcParams& p, int row0, int col0, const uint32_t (&v)[16],
+                                           uint32_t* buf, const float* s_scale) {
+  if constexpr (MODE == TcMode::kI8Norm) {
+    if (p.acc_out)
+      store_block_32x16(reinterpret_cast<uint32_t*>(p.acc_out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf,
+                        v);
+    if (p.out) {
+      uint32_t f[16];
       #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int c = col0 + j;
-        const float s = (c < p.cols) ? __ldg(p.scale + c) : 0.f;
-        f[j] = __fmul_rn(__int2float_rn(static_cast<int>(v[j])), s);
-      }
-      if (full) {
-        #pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-      } else {
-        for (int j = 0; j < 16; ++j)
-          if (col0 + j < p.cols) crow[col0 + j] = f[j];
-      }
+      for (int j = 0; j < 16; ++j)
+        f[j] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), s_scale[j]));
+      store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, f);
     }
   } else {
-    if (full) {
-      #pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4*>(crow + col0 + j) =
-            make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                        __uint_as_float(v[j + 3]));
-    } else {
-      for (int j = 0; j < 16; ++j)
-        if (col0 + j < p.cols) crow[col0 + j] = __uint_as_float(v[j]);
-    }
+    store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, v);
   }
 }
 
@@ -312,12 +314,13 @@ __device__ __forceinline__ void epi_swap48(const TcParams& p, int n, int tok0, i
 // return values are unused, so these compile to reductions).
 template <bool kInt>
 __device__ __forceinline__ void slot_add16(uint32_t* s, const uint32_t (&v)[16]) {
+  // column-major slot: consecutive columns are kTileRows words apart
   #pragma unroll
   for (int j = 0; j < 16; ++j) {
     if constexpr (kInt)
-      atomicAdd(reinterpret_cast<int*>(s + j), static_cast<int>(v[j]));
+      atomicAdd(reinterpret_cast<int*>(s + j * kTileRows), static_cast<int>(v[j]));
     else
-      atomicAdd(reinterpret_cast<float*>(s + j), __uint_as_float(v[j]));
+      atomicAdd(reinterpret_cast<float*>(s + j * kTileRows), __uint_as_float(v[j]));
   }
 }
 
@@ -350,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  uint32_t* s_stage = reinterpret_cast<uint32_t*>(smem + L.stg_off) + (warp & 3) * 32 * 17;
   unsigned long long* trace = p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceSlots : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
 
@@ -562,6 +566,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (MODE == TcMode::kQ8Swap && grow < p.n_out) scale_n = __ldg(p.scale + grow);
         named_bar_sync(1, kEpiThreads);
+      } else if constexpr (MODE == TcMode::kI8Norm) {
+        // Stage the tile's column scales (bn <= 256 floats, in the token-table
+        // words) while the accumulator is still being computed.
+        named_bar_sync(1, kEpiThreads);
+        if (p.out) {
+          float* s_scale = reinterpret_cast<float*>(s_exp);
+          for (int j = ethread; j < p.bn; j += kEpiThreads) {
+            const int col = tn * p.bn + j;
+            s_scale[j] = col < p.cols ? __ldg(p.scale + col) : 0.f;
+          }
+        }
+        named_bar_sync(1, kEpiThreads);
       }
       const unsigned long long tw = trace ? globaltimer() : 0;
       if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
@@ -597,21 +613,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(tempty_bar + buf);
             }
-            epi_norm16<MODE>(p, grow, tn * p.bn + c, v);
+            epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
           }
         }
         continue;
       }
 
-      // Split tile: add this CTA's partial into the tile's slot; the CTA that
-      // completes the tile's k-block count finishes it and clears the slot.
+      // Split tile. Slots are column-major ([column][128 rows]) so that a
+      // warp's 32 rows of one column are contiguous.
+      //  swap modes: every contributor adds one combined value per real token
+      //    ([tok][128]) atomically into the slot of the CTA that holds the
+      //    tile's last unit; the finisher reads it and clears it.
+      //  normal modes: every contributor stores its 32-bit partial ([bn][128])
+      //    in its own slot (2*cta + 0 for the head of its range, + 1 for the
+      //    tail); the finisher sums the contributors' slots in CTA order, so
+      //    f32 results do not depend on arrival order.
       const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
-      const int slot = sc.owner(tile_u0 + sc.kb_tile - 1);
-      uint32_t* srow = p.slots + (static_cast<long long>(slot) * kTileRows + row) * p.bn;
-      // swap modes: one combined value per real token, row-major [128][tok_per_tile]
+      const int slot = kSwap ? sc.owner(tile_u0 + sc.kb_tile - 1) : 2 * cta + (sc.start(cta) >= tile_u0 ? 0 : 1);
+      uint32_t* scol = (kSwap ? p.slots : p.pieces) + static_cast<long long>(slot) * kTileRows * p.bn + row;
       using SV = typename SwapVal<MODE>::T;
-      SV* vrow = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) +
-                 static_cast<long long>(row) * p.tok_per_tile;
+      SV* vcol = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) + row;
       if constexpr (kSwap) {
         for (int c = 0; c < p.bn; c += 48) {
           uint32_t v[48];
@@ -623,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int lt = c / 3 + j;
-            if (tok0 + lt < p.n_tokens) atomicAdd(vrow + lt, swap_combine<MODE>(v + 3 * j));
+            if (tok0 + lt < p.n_tokens) atomicAdd(vcol + lt * kTileRows, swap_combine<MODE>(v + 3 * j));
           }
         }
       } else {
@@ -632,7 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           tmem_ld16(tbase + c, v);
           tmem_ld_wait();
-          slot_add16<kInt>(srow + c, v);
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(scol + (c + j) * kTileRows, v[j]);
         }
       }
       tc_fence_before();
@@ -655,10 +677,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int lt0 = 0; lt0 < ntok; lt0 += 8) {
           SV vals[8];
           #pragma unroll
-          for (int j = 0; j < 8; ++j) vals[j] = (lt0 + j < ntok) ? __ldcg(vrow + lt0 + j) : SV(0);
+          for (int j = 0; j < 8; ++j) vals[j] = (lt0 + j < ntok) ? __ldcg(vcol + (lt0 + j) * kTileRows) : SV(0);
           #pragma unroll
           for (int j = 0; j < 8; ++j)
-            if (lt0 + j < ntok) __stcg(vrow + lt0 + j, SV(0));
+            if (lt0 + j < ntok) __stcg(vcol + (lt0 + j) * kTileRows, SV(0));
           if (grow < p.n_out) {
             #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -667,19 +689,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
+        const int c_first = sc.owner(tile_u0);
+        const int c_last = sc.owner(tile_u0 + sc.kb_tile - 1);
         for (int c = 0; c < p.bn; c += 16) {
           uint32_t v[16];
           #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(srow + c + j));
-            v[j] = u.x;
-            v[j + 1] = u.y;
-            v[j + 2] = u.z;
-            v[j + 3] = u.w;
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+          for (int q = c_first; q <= c_last; q += 2) {
+            // two contributors' loads in flight at a time, summed in CTA order
+            const int wq0 = (sc.start(q) >= tile_u0) ? 0 : 1;
+            const uint32_t* s0 = p.pieces + static_cast<long long>(2 * q + wq0) * kTileRows * p.bn + row;
+            const bool has1 = q + 1 <= c_last;
+            const uint32_t* s1 = p.pieces + static_cast<long long>(2 * (q + 1)) * kTileRows * p.bn + row;
+            uint32_t a[16], b[16];
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              a[j] = __ldcg(s0 + (c + j) * kTileRows);
+              b[j] = has1 ? __ldcg(s1 + (c + j) * kTileRows) : 0u;
+            }
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if constexpr (kInt) {
+                v[j] += a[j];
+                if (has1) v[j] += b[j];
+              } else {
+                float f = __fadd_rn(__uint_as_float(v[j]), __uint_as_float(a[j]));
+                if (has1) f = __fadd_rn(f, __uint_as_float(b[j]));
+                v[j] = __float_as_uint(f);
+              }
+            }
           }
-          #pragma unroll
-          for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<uint4*>(srow + c + j), make_uint4(0, 0, 0, 0));
-          epi_norm16<MODE>(p, grow, tn * p.bn + c, v);
+          epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
         }
       }
     }

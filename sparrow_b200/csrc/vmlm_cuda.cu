@@ -82,7 +82,8 @@ struct Ctx {
   cudaStream_t stream = nullptr;
   DevBuf act;       // digit planes / split terms
   DevBuf small;     // exps | nonfinite | term_flags, each [M] int
-  DevBuf slots;     // split-tile partials
+  DevBuf slots;     // swap-mode split-tile accumulators (zeroed once, self-clearing)
+  DevBuf pieces;    // normal-mode split-tile partials (overwritten every call)
   DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
   DevBuf sync;      // prep completion counter and term-flag OR (zeroed once, self-resetting)
   int* err = nullptr;       // device error word
@@ -232,22 +233,40 @@ bool use_streamk(const TcParams& p, int sms) {
   return static_cast<long long>(p.tiles_m) * p.tiles_n < 4ll * sms;
 }
 
-// Tile width for a normal-mode GEMM (rows x N output, 128-row tiles, whole
-// tiles round-robin over the SMs): the narrowest widths fill more SMs but run
-// the tensor cores less efficiently, so pick the width with the least
-// estimated time, waves x per-tile cost.
-int pick_bn(int rows, int N, int sms) {
+// Tile width and K split for a normal-mode GEMM (rows x N output, 128-row
+// tiles). Each candidate is costed as waves x per-CTA time, the per-CTA time
+// being the larger of its operand traffic at a per-SM L2 rate and its MMA work
+// at a per-SM tensor rate derated for narrow tiles (narrow UMMA N runs the
+// tensor pipe less efficiently), plus the split-tile reduction. A split of 2
+// keeps f32 results deterministic (0 + a + b in either order); integer
+// accumulators allow wider splits.
+struct NormPlan {
+  int bn;
+  int split;
+};
+
+NormPlan plan_norm(int rows, int N, int K, int esz, bool int_acc, int sms) {
   const int cand[3] = {256, 128, 64};
-  const double eff[3] = {1.0, 0.92, 0.75};
-  int best = 256;
-  double best_cost = 1e300;
+  const double eff[3] = {1.0, 0.85, 0.5};
+  const double l2_bps = 120e9;                             // per SM
+  const double mac_ps = (int_acc ? 22e12 : 11e12) / 2.0;  // MACs per second per SM
+  NormPlan best{256, 1};
+  double best_t = 1e300;
   for (int i = 0; i < 3; ++i) {
     const long long tiles = cdiv(rows, kTileRows) * cdiv(N, cand[i]);
-    const long long waves = cdiv(tiles, sms);
-    const double cost = static_cast<double>(waves) * cand[i] / eff[i];
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = cand[i];
+    const int max_split = int_acc ? 4 : 2;
+    for (int split = 1; split <= max_split; split *= 2) {
+      if (split > 1 && tiles * split > sms) continue;  // only split to fill a single wave
+      const double kk = static_cast<double>(K) / split;
+      const double t_load = (kTileRows + cand[i]) * kk * esz / l2_bps;
+      const double t_mma = static_cast<double>(kTileRows) * cand[i] * kk / (mac_ps * eff[i]);
+      const double t_red = split > 1 ? 2.0 * kTileRows * cand[i] * 4 * (split - 1) / l2_bps : 0.0;
+      const double waves = static_cast<double>(cdiv(tiles * split, sms));
+      const double t = waves * ((t_load > t_mma ? t_load : t_mma) + t_red);
+      if (t < best_t * 0.999) {
+        best_t = t;
+        best = NormPlan{cand[i], split};
+      }
     }
   }
   return best;
@@ -256,7 +275,7 @@ int pick_bn(int rows, int N, int sms) {
 // Plan and launch the tcgen05 kernel. units_min = tiles * k-blocks with one term.
 template <TcMode MODE>
 int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool streamk,
-           bool pdl) {
+           bool pdl, int split = 0) {
   int stages = 16;
   while (stages >= 2 && tc_smem_layout(stages, p.bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   if (stages < 2) return fail(VMLM_ERR_SHAPE, "tile too large for shared memory");
@@ -265,13 +284,23 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   const long long units_min = tiles * p.kb_per_term;
   long long grid = streamk ? (units_min < c->sms ? units_min : c->sms) : (tiles < c->sms ? tiles : c->sms);
+  if (split > 1) {
+    // an explicit K split: exactly `split` CTAs per tile (stream-K with grid = tiles * split)
+    if (split > p.kb_per_term) split = p.kb_per_term;
+    grid = tiles * split;
+    streamk = split > 1;
+  }
   if (grid < 1) grid = 1;
   p.streamk = streamk ? 1 : 0;
   if (streamk) {
-    VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
+    if (MODE == TcMode::kQ8Swap || MODE == TcMode::kBf16Swap)
+      VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
+    else
+      VMLM_TRY(ensure(c->pieces, static_cast<size_t>(2 * grid) * kTileRows * p.bn * 4));
     VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
   }
   p.slots = static_cast<uint32_t*>(c->slots.p);
+  p.pieces = static_cast<uint32_t*>(c->pieces.p);
   p.counters = static_cast<int*>(c->counters.p);
   p.err = c->err;
   p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
@@ -403,7 +432,8 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   }
   p.rows = M;
   p.cols = N;
-  p.bn = pick_bn(M, N, c->sms);
+  const NormPlan plan = plan_norm(M, N, K, 2, false, c->sms);
+  p.bn = plan.bn;
   p.max_terms = 3;
   p.term_stride = kp;
   p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
@@ -413,7 +443,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   p.n_tokens = M;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
-  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true);
+  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true, plan.split);
 }
 
 // ---------------------------------------------------------- int8 x int8
@@ -429,7 +459,8 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   TcParams p = {};
   p.rows = M;
   p.cols = N;
-  p.bn = pick_bn(M, N, c->sms);
+  const NormPlan plan = plan_norm(M, N, K, 1, true, c->sms);
+  p.bn = plan.bn;
   p.kb_per_term = static_cast<int>(cdiv(K, 128));
   p.max_terms = 1;
   p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
@@ -445,7 +476,7 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
-  return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false);
+  return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false, plan.split);
 }
 
 // ------------------------------------------------------------ host API
@@ -527,7 +558,8 @@ int vmlm_shutdown(void) {
     Ctx* c = kv.second;
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
-    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->sync, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
+    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->pieces, &c->counters, &c->sync, &c->h_a, &c->h_c, &c->h_w,
+                      &c->h_s, &c->h_acc})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
