@@ -20,17 +20,18 @@
 //   kI8Norm    A = int8 activations X[m,:], B = int8 weights W[n,:]:
 //              C[m][n] = f32(acc) * scale[n], and/or the raw int32 acc.
 //
-// Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
-// the MMAs, warps 2..5 are the epilogue (TMEM lanes 32*(warp%4) .. +31).
+// Warp roles (320 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
+// the MMAs, warps 2..9 are the epilogue: warp w reads TMEM lanes
+// 32*(w%4) .. +31 and finishes every other column chunk of them.
 //
 // Scheduling is static. Units are (tile, k-block) pairs ordered tile-major.
 // Either every CTA takes whole tiles round-robin, or each CTA takes a
-// contiguous range of units (stream-K). A tile split between CTAs is
-// accumulated with atomics into one slot (owned by the CTA that holds the
-// tile's last unit); the CTA that brings the tile's counter to the full
-// k-block count reads the slot, writes the output and clears the slot. Integer
-// accumulators (kQ8Swap, kI8Norm) are exact in any order; f32 partials
-// (bf16 modes) are order-dependent in the last bit.
+// contiguous range of units (stream-K, or an explicit K split of every tile
+// over `split` CTAs). The CTA that brings a split tile's counter to the full
+// k-block count finishes the tile. Swap modes add one combined value per token
+// atomically into a self-clearing slot (exact for Q8; last-bit order
+// dependent for bf16); normal modes store per-CTA partials and sum them in CTA
+// order (deterministic).
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -46,8 +47,9 @@ enum class TcMode : int { kQ8Swap = 0, kBf16Swap = 1, kBf16Norm = 2, kI8Norm = 3
 
 constexpr int kTileRows = 128;        // UMMA M
 constexpr int kBlockBytes = 128;      // bytes of K per stage (one 128B swizzle row)
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, splitting the columns
+constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kMaxTokPerTile = 128;   // swap modes: tokens per column tile (bn/3 <= 85)
 
@@ -114,7 +116,7 @@ __host__ __device__ inline TcSmem tc_smem_layout(int stages, int bn) {
   // per-tile token table: exps[kMaxTokPerTile], nonfinite[kMaxTokPerTile]
   s.stg_off = s.meta_off + 2 * kMaxTokPerTile * 4;
   // per-epilogue-warp store staging (32 rows x 17 words); +1024 for base alignment
-  s.total = s.stg_off + 4 * 32 * 17 * 4 + 1024;
+  s.total = s.stg_off + kEpiWarps * 32 * 17 * 4 + 1024;
   return s;
 }
 
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  uint32_t* s_stage = reinterpret_cast<uint32_t*>(smem + L.stg_off) + (warp & 3) * 32 * 17;
+  uint32_t* s_stage = reinterpret_cast<uint32_t*>(smem + L.stg_off) + (warp >= 2 ? warp - 2 : 0) * 32 * 17;
   unsigned long long* trace = p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceSlots : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
 
@@ -364,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar + b, 1);
-      mbar_init(tempty_bar + b, 4);
+      mbar_init(tempty_bar + b, kEpiWarps);
     }
     mbar_init(drain_bar, 1);
-    mbar_init(done_bar, 4);
+    mbar_init(done_bar, kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -541,9 +543,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;      // which alternate column chunks this warp finishes
     const int row = quarter * 32 + lane;   // accumulator row within the tile
-    const int ethread = threadIdx.x - 64;  // 0..127
+    const int ethread = threadIdx.x - 64;  // 0..kEpiThreads-1
+    // Column chunks: 48 columns (16 tokens) in swap modes, 16 otherwise; warp
+    // pair (quarter, half) takes chunks ci with ci % 2 == half.
+    constexpr int kChunk = kSwap ? 48 : 16;
     pdl_wait_prior();
     const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
     long long cur = 0;
@@ -585,34 +591,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (trace && ethread == 0 && i == 0) trace[5] = globaltimer();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
+      const int nch = p.bn / kChunk;
+      // last chunk of this warp (largest ci < nch with ci % 2 == half), -1 if none
+      const int my_last = (nch - 1 - half) < 0 ? -1 : (nch - 1) - (((nch - 1) ^ half) & 1);
+      // this warp has read all its TMEM columns: let the MMA warp reuse the buffer
+      auto release_accum = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar + buf);
+      };
 
       if (!w.partial) {
+        if (my_last < 0) release_accum();
         if constexpr (kSwap) {
-          for (int c = 0; c < p.bn; c += 48) {
+          for (int ci = half; ci < nch; ci += 2) {
+            const int c = ci * kChunk;
             uint32_t v[48];
             __syncwarp();
             tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
             tmem_ld16(tbase + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
             tmem_ld16(tbase + c + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
             tmem_ld_wait();
-            if (c + 48 >= p.bn) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(tempty_bar + buf);
-            }
+            if (ci == my_last) release_accum();
             epi_swap48<MODE>(p, grow, tok0, c / 3, scale_n, s_exp, s_bad, v);
           }
         } else {
-          for (int c = 0; c < p.bn; c += 16) {
+          for (int ci = half; ci < nch; ci += 2) {
+            const int c = ci * kChunk;
             uint32_t v[16];
             __syncwarp();
             tmem_ld16(tbase + c, v);
             tmem_ld_wait();
-            if (c + 16 >= p.bn) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(tempty_bar + buf);
-            }
+            if (ci == my_last) release_accum();
             epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
           }
         }
@@ -634,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       using SV = typename SwapVal<MODE>::T;
       SV* vcol = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) + row;
       if constexpr (kSwap) {
-        for (int c = 0; c < p.bn; c += 48) {
+        for (int ci = half; ci < nch; ci += 2) {
+          const int c = ci * kChunk;
           uint32_t v[48];
           __syncwarp();
           tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
@@ -648,7 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        for (int c = 0; c < p.bn; c += 16) {
+        for (int ci = half; ci < nch; ci += 2) {
+          const int c = ci * kChunk;
           uint32_t v[16];
           __syncwarp();
           tmem_ld16(tbase + c, v);
@@ -657,9 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) __stcg(scol + (c + j) * kTileRows, v[j]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar + buf);
+      release_accum();
       __threadfence();
       named_bar_sync(1, kEpiThreads);
       if (ethread == 0) {
@@ -674,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       if constexpr (kSwap) {
         const int ntok = min(p.tok_per_tile, p.n_tokens - tok0);
-        for (int lt0 = 0; lt0 < ntok; lt0 += 8) {
+        for (int lt0 = half * 8; lt0 < ntok; lt0 += 16) {
           SV vals[8];
           #pragma unroll
           for (int j = 0; j < 8; ++j) vals[j] = (lt0 + j < ntok) ? __ldcg(vcol + (lt0 + j) * kTileRows) : SV(0);
@@ -691,7 +701,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const int c_first = sc.owner(tile_u0);
         const int c_last = sc.owner(tile_u0 + sc.kb_tile - 1);
-        for (int c = 0; c < p.bn; c += 16) {
+        for (int ci = half; ci < nch; ci += 2) {
+          const int c = ci * kChunk;
           uint32_t v[16];
           #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0u;
