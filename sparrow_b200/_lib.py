@@ -33,6 +33,7 @@ SIGNATURES = {
     "vmlm_gemm_nt_int8_dev": (I, [P, P, P, P, S, S, S, P]),
     "vmlm_gemm_nt_bf16_dev": (I, [P, P, P, S, S, S, P]),
     "vmlm_gemm_i8i8_dev": (I, [P, P, P, P, P, S, S, S, P]),
+    "vmlm_gemm_nt_int8_dev_noalloc": (I, [P, P, P, P, S, S, S, P]),
     "vmlm_sync": (I, [P]),
     "vmlm_launch_count": (ctypes.c_uint64, []),
     "vmlm_profile_enable": (I, [I]),

@@ -773,3 +773,152 @@ int vmlm_sync(void* stream) {
 }
 
 }  // extern "C"
+
+// ====================================================== allocation-free Q8
+//
+// vmlm_gemm_nt_int8_dev_noalloc runs the Q8 path with every byte of scratch
+// (activation digit planes, per-token exponents and flags, split-tile slots
+// and counters, the device error word) taken from one fixed array in device
+// memory that is part of the loaded library, so a call allocates nothing. It
+// serves callers that must not allocate device memory while they run: an
+// engine that sizes all of its device memory once at start-up (as VMLM sizes
+// its pools at load) cannot have a library call cudaMalloc in its per-token
+// loop, where the allocation could fail for lack of headroom and where
+// cudaMalloc/cudaFree would also stall the loop by synchronising the device.
+//
+// Limits (the array is sized for decode): m <= 16 tokens, n <= 131072 output
+// rows, k <= 16384. The array is kNaBytes (about 4.7 MB) and every GPU that
+// loads the library holds it until the process exits.
+
+namespace {
+
+constexpr int kNaMaxM = 16;
+constexpr int kNaMaxN = 131072;
+constexpr int kNaMaxK = 16384;
+constexpr int kNaMaxCtas = 160;  // grid cap; a B200 has 148 SMs
+constexpr int kNaBn = 48;        // UMMA N for up to 16 tokens (3 planes x 16)
+constexpr size_t kNaAlign(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+constexpr size_t kNaErrOff = 0;                                        // int error word
+constexpr size_t kNaCountersOff = 256;                                 // int32 per 128-row tile
+constexpr size_t kNaMetaOff = kNaAlign(kNaCountersOff + 4 * (kNaMaxN / kTileRows));  // exps[16], flags[16]
+constexpr size_t kNaSlotsOff = kNaAlign(kNaMetaOff + 2 * kNaMaxM * 4);
+constexpr size_t kNaSlotsBytes = static_cast<size_t>(kNaMaxCtas) * kTileRows * kNaBn * 4;
+constexpr size_t kNaPlanesOff = kNaAlign(kNaSlotsOff + kNaSlotsBytes);  // everything before starts at zero
+constexpr size_t kNaPlanesBytes = static_cast<size_t>(3) * kNaMaxM * kNaMaxK;
+constexpr size_t kNaBytes = kNaPlanesOff + kNaPlanesBytes;
+
+}  // namespace
+
+// The scratch itself. In host code this name is only a stand-in for the
+// symbol: the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
+
+namespace {
+
+struct NaDevice {
+  bool ready = false;
+  unsigned char* base = nullptr;  // device address of g_noalloc_scratch on this device
+  int sms = 0;
+};
+NaDevice g_na[64];
+
+// One-time set-up per device, with that device current: resolve the array's
+// device address, zero the part that must start at zero (error word,
+// counters, split-tile slots; the kernels leave them zero after every call),
+// and allow the GEMM kernel its shared memory. Allocates nothing.
+int na_setup(int dev, NaDevice** out) {
+  if (dev < 0 || dev >= 64) return fail(VMLM_ERR_ARG, "gemm_nt_int8_dev_noalloc: device %d out of range", dev);
+  NaDevice& d = g_na[dev];
+  if (!d.ready) {
+    int major = 0, sms = 0;
+    VMLM_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return fail(VMLM_ERR_NO_DEVICE, "device %d is not sm_100", dev);
+    VMLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    VMLM_TRY(load_encoder());
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(VMLM_ERR_CUDA, "gemm_nt_int8_dev_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    VMLM_CUDA(cudaMemset(ptr, 0, kNaPlanesOff));
+    VMLM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<TcMode::kQ8Swap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kMaxSmem));
+    d.base = static_cast<unsigned char*>(ptr);
+    d.sms = sms < kNaMaxCtas ? sms : kNaMaxCtas;
+    d.ready = true;
+  }
+  *out = &d;
+  return VMLM_OK;
+}
+
+}  // namespace
+
+extern "C" int vmlm_gemm_nt_int8_dev_noalloc(const float* a, const int8_t* q, const float* scale, float* c,
+                                             size_t m, size_t n, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || !scale || (k > 0 && (!a || !q))) return fail(VMLM_ERR_ARG, "gemm_nt_int8_dev_noalloc: null pointer");
+  if (m > static_cast<size_t>(kNaMaxM) || n > static_cast<size_t>(kNaMaxN) || k > static_cast<size_t>(kNaMaxK))
+    return fail(VMLM_ERR_SHAPE,
+                "gemm_nt_int8_dev_noalloc: m=%zu n=%zu k=%zu exceeds the fixed scratch limits m <= %d, n <= %d, "
+                "k <= %d; use vmlm_gemm_nt_int8_dev",
+                m, n, k, kNaMaxM, kNaMaxN, kNaMaxK);
+  int dev = -1;
+  VMLM_CUDA(cudaGetDevice(&dev));
+  NaDevice* d = nullptr;
+  VMLM_TRY(na_setup(dev, &d));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL = the CUDA default stream
+  const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
+  const int kp = K > 0 ? static_cast<int>(cdiv(K, 16) * 16) : 16;
+  int8_t* planes = reinterpret_cast<int8_t*>(d->base + kNaPlanesOff);
+  int* exps = reinterpret_cast<int*>(d->base + kNaMetaOff);
+  int* nonf = exps + kNaMaxM;
+  VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+                  kp, planes, exps, nonf));
+  const bool tc_ok = K > 0 && K % 16 == 0 && aligned16(q);
+  if (!tc_ok) {
+    const long long warps = static_cast<long long>(M) * N;
+    return launch(q8_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, true, q,
+                  scale, static_cast<const int8_t*>(planes), kp, static_cast<const int*>(exps),
+                  static_cast<const int*>(nonf), a, static_cast<long long>(K), c, static_cast<long long>(N), M, N, K);
+  }
+  TcParams p = {};
+  p.rows = N;
+  p.cols = 3 * M;
+  p.bn = kNaBn;
+  p.kb_per_term = static_cast<int>(cdiv(K, 128));
+  p.max_terms = 1;
+  p.tiles_m = static_cast<int>(cdiv(N, kTileRows));
+  p.tiles_n = 1;
+  p.tm_fastest = 0;
+  p.a_box_elems = 128;
+  p.out = c;
+  p.ldo = N;
+  p.scale = scale;
+  p.exps = exps;
+  p.nonfinite = nonf;
+  p.n_tokens = M;
+  p.tok_per_tile = kNaBn / 3;
+  p.n_out = N;
+  p.x = a;
+  p.ldx = K;
+  p.w = q;
+  p.k = K;
+  p.slots = reinterpret_cast<uint32_t*>(d->base + kNaSlotsOff);
+  p.counters = reinterpret_cast<int*>(d->base + kNaCountersOff);
+  p.err = reinterpret_cast<int*>(d->base + kNaErrOff);
+  int stages = 16;
+  while (stages >= 2 && tc_smem_layout(stages, p.bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  p.stages = stages;
+  p.tmem_cols = pow2_at_least(2 * p.bn);
+  const long long tiles = p.tiles_m;
+  p.streamk = use_streamk(p, d->sms) ? 1 : 0;
+  long long grid = p.streamk ? tiles * p.kb_per_term : tiles;
+  if (grid > d->sms) grid = d->sms;
+  CUtensorMap ma, mb;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn));
+  const TcSmem L = tc_smem_layout(stages, p.bn);
+  return launch(tc_gemm_kernel<TcMode::kQ8Swap>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, true,
+                ma, mb, p);
+}

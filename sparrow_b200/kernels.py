@@ -156,6 +156,17 @@ def gemm_nt_int8_dev(a, q, scale, c, m, n, k, stream=None) -> None:
         _stream_ptr(stream)))
 
 
+def gemm_nt_int8_dev_noalloc(a, q, scale, c, m, n, k, stream=None) -> None:
+    """gemm_nt_int8_dev without any device allocation: its scratch is a fixed
+    array inside the library (m <= 16, n <= 131072, k <= 16384). For callers
+    that reserve all device memory up front and must not allocate per call.
+    Calls that overlap on the GPU share that scratch and race."""
+    check(lib().vmlm_gemm_nt_int8_dev_noalloc(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(q, "int8", n * k, "q"),
+        _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"), m, n, k,
+        _stream_ptr(stream)))
+
+
 def gemm_nt_bf16_dev(a, b, c, m, n, k, stream=None) -> None:
     """b: a bfloat16 (or int16/uint16 bit-pattern) CUDA tensor [n, k]."""
     if b is not None and not isinstance(b, int) and str(b.dtype) in ("torch.int16", "torch.uint16"):
