@@ -118,15 +118,21 @@ def run_case(args):
         step()
         torch.cuda.synchronize()
         tr = K.trace_take(1024).astype(np.float64)
+        items = tr[:, 15]
         K.trace_enable(0)
         tr = tr[tr[:, 0] > 0]
         t0 = tr[:, 0].min()
         names = ["start", "prologue", "tma_issued", "first_stage", "last_commit", "first_accum", "epi_done", "end",
-                 "wait_empty", "wait_full", "wait_accum_free", "epi_wait"]
-        cols = [(tr[:, j] - t0) / 1e3 for j in range(8)] + [tr[:, j] / 1e3 for j in range(8, 12)]
+                 "wait_empty", "wait_full", "wait_accum_free", "epi_wait", "split_publish", "split_count",
+                 "split_finish", "items", "finished"]
+        cols = ([(tr[:, j] - t0) / 1e3 for j in range(8)] + [tr[:, j] / 1e3 for j in range(8, 15)]
+                + [np.floor(items / 65536), items % 65536])
         out["trace_us"] = {nm: [round(float(np.min(v)), 2), round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
                            for nm, v in zip(names, cols)}
         out["trace_ctas"] = int(tr.shape[0])
+        # the three CTAs that finished their epilogue last, all columns
+        slow = np.argsort(cols[6])[-3:][::-1]
+        out["slowest"] = [[round(float(v[i]), 2) for v in cols] for i in slow]
     print(json.dumps(out), flush=True)
 
 
@@ -194,6 +200,7 @@ def dist_init():
         import datetime
         import torch.distributed as dist
         local = int(os.environ.get("LOCAL_RANK", "0"))
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))

@@ -249,12 +249,11 @@ __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* _
   if (threadIdx.x == 0) {
     term_flags[t] = (flags & 6) | 1;
     nonfinite[t] = (flags >> 8) & 1;
-    __threadfence();
-    is_last = (atomicAdd(done, 1u) == static_cast<unsigned>(M - 1));
+    // release this row's flags; the last CTA's acquire sees every row's
+    is_last = (atom_add_acq_rel_gpu(done, 1u) == static_cast<unsigned>(M - 1));
   }
   __syncthreads();
   if (is_last) {
-    __threadfence();
     int orv = 0;
     for (int i = threadIdx.x; i < M; i += blockDim.x) orv |= __ldcg(term_flags + i);
     orv = block_or(orv, redi);

@@ -96,8 +96,10 @@ struct TcParams {
 // MMA warp, [4] last accumulator committed, [5] first accumulator seen by the
 // epilogue, [6] epilogue done, [7] TMEM released; then summed waits (ns):
 // [8] producer for free stages, [9] MMA for loaded stages, [10] MMA for a free
-// accumulator, [11] epilogue for a finished accumulator.
-constexpr int kTraceSlots = 12;
+// accumulator, [11] epilogue for a finished accumulator; split-tile epilogue
+// phases (ns, summed): [12] publishing partials, [13] counting arrivals, [14]
+// finishing; [15] work items * 65536 + tiles finished.
+constexpr int kTraceSlots = 16;
 
 struct TcSmem {
   uint32_t a_off, b_off, bar_off, meta_off, stg_off;  // offsets from the 1024-aligned base
@@ -125,7 +127,7 @@ struct WorkItem {
   bool partial;
 };
 
-// Units per tile depend on the number of active terms (kBf16Norm).
+// Static schedule over (tile, k-block) units of one term pass.
 struct Sched {
   long long units;  // total units
   int kb_tile;      // k-blocks per tile
@@ -382,10 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int cta = blockIdx.x;
-  // Schedule with T active terms (T only differs from 1 in kBf16Norm).
-  auto make_sched = [&](int T) {
+  // Units are k-blocks of one term pass; a kBf16Norm work item runs its
+  // k-block range once per active term, so the schedule does not depend on
+  // the term count that the previous kernel produces.
+  auto make_sched = [&]() {
     Sched s;
-    s.kb_tile = p.kb_per_term * T;
+    s.kb_tile = p.kb_per_term;
     s.tiles = p.tiles_m * p.tiles_n;
     s.units = static_cast<long long>(s.tiles) * s.kb_tile;
     s.grid = gridDim.x;
@@ -398,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // weight stream overlaps the activation preparation.
   constexpr bool kWeightIsA = kSwap;
   unsigned long long epi_wait = 0;  // trace: epilogue time waiting for accumulators
+  unsigned long long epi_pub = 0, epi_cnt = 0, epi_fin = 0, epi_items = 0;  // trace: split-tile phases
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -405,17 +410,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
       int npre = 0;  // stages of item 0 whose weight half is already in flight
+      const Sched sc = make_sched();
       {
-        // Item 0 and its first term-0 k-blocks are the same for every T (the
-        // normal-mode schedule used with term passes is round-robin).
-        const Sched s1 = make_sched(1);
+        // The first k-blocks of item 0 belong to term 0 whatever T turns out to be.
         long long cur0 = 0;
         WorkItem w0;
-        const bool pre_ok = (MODE != TcMode::kBf16Norm) || !p.streamk;
-        if (pre_ok && s1.item(cta, 0, cur0, w0)) {
+        if (sc.item(cta, 0, cur0, w0)) {
           const int tm0 = p.tm_fastest ? w0.tile % p.tiles_m : w0.tile / p.tiles_n;
           const int tn0 = p.tm_fastest ? w0.tile / p.tiles_m : w0.tile % p.tiles_n;
-          npre = min(p.stages, min(w0.kb1, p.kb_per_term) - w0.kb0);
+          npre = min(p.stages, w0.kb1 - w0.kb0);
           for (int s = 0; s < npre; ++s) {
             const int kx = (w0.kb0 + s) * p.a_box_elems;
             mbar_arrive_expect_tx(full_bar + s, L.a_bytes + L.b_bytes);
@@ -428,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait_prior();
       if (trace) trace[1] = globaltimer();
-      const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
+      const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, last_phase = 0;  // per stage: ever issued / parity of last issue
@@ -439,8 +442,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; ok && sc.item(cta, i, cur, w); ++i) {
         const int tm = p.tm_fastest ? w.tile % p.tiles_m : w.tile / p.tiles_n;
         const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          const bool pre = (i == 0 && kb - w.kb0 < npre);
+        const int nkb = w.kb1 - w.kb0;
+        for (int j = 0; j < T * nkb; ++j) {
+          const int term = j / nkb;
+          const int kin = w.kb0 + (j - term * nkb);
+          const bool pre = (i == 0 && j < npre);
           const unsigned long long tw = trace ? globaltimer() : 0;
           if (!pre && !mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
             ok = false;
@@ -450,15 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + L.a_off + stage * L.a_bytes;
           uint8_t* sb = smem + L.b_off + stage * L.b_bytes;
           if (!pre) mbar_arrive_expect_tx(full_bar + stage, L.a_bytes + L.b_bytes);
-          int ka, kbx;
-          if constexpr (MODE == TcMode::kBf16Norm) {
-            const int term = kb / p.kb_per_term, kin = kb % p.kb_per_term;
-            ka = term * p.term_stride + kin * p.a_box_elems;
-            kbx = kin * p.a_box_elems;
-          } else {
-            ka = kb * p.a_box_elems;
-            kbx = ka;
-          }
+          const int kbx = kin * p.a_box_elems;
+          const int ka = term * p.term_stride + kbx;
           if (!pre || !kWeightIsA) tma_load_2d(sa, &tmA, full_bar + stage, ka, tm * kTileRows, pol_a);
           if (!pre || kWeightIsA) tma_load_2d(sb, &tmB, full_bar + stage, kbx, tn * p.bn, pol_b);
           issued_mask |= 1u << stage;
@@ -484,7 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       pdl_wait_prior();
-      const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
+      const Sched sc = make_sched();
+      const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
       int stage = 0;
       uint32_t phase = 0;
       long long cur = 0;
@@ -499,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (trace) wait_accum += globaltimer() - tw0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        const int nblk = T * (w.kb1 - w.kb0);
+        for (int j = 0; j < nblk; ++j) {
           const unsigned long long tw1 = trace ? globaltimer() : 0;
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
@@ -511,10 +512,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
           const uint32_t b_addr = smem_u32(smem + L.b_off + stage * L.b_bytes);
           #pragma unroll
-          for (uint32_t j = 0; j < kMmaPerBlock; ++j) {
-            const uint64_t ad = umma_desc_sw128(a_addr + 32 * j);
-            const uint64_t bd = umma_desc_sw128(b_addr + 32 * j);
-            const uint32_t acc = (kb > w.kb0 || j > 0) ? 1u : 0u;
+          for (uint32_t u = 0; u < kMmaPerBlock; ++u) {
+            const uint64_t ad = umma_desc_sw128(a_addr + 32 * u);
+            const uint64_t bd = umma_desc_sw128(b_addr + 32 * u);
+            const uint32_t acc = (j > 0 || u > 0) ? 1u : 0u;
             if constexpr (kInt)
               umma_i8(d_tmem, ad, bd, idesc, acc);
             else
@@ -551,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pair (quarter, half) takes chunks ci with ci % 2 == half.
     constexpr int kChunk = kSwap ? 48 : 16;
     pdl_wait_prior();
-    const Sched sc = make_sched((MODE == TcMode::kBf16Norm) ? active_terms(p) : 1);
+    const Sched sc = make_sched();
     long long cur = 0;
     WorkItem w;
     for (int i = 0; sc.item(cta, i, cur, w); ++i) {
@@ -590,6 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (trace) epi_wait += globaltimer() - tw;
       tc_fence_after();
       if (trace && ethread == 0 && i == 0) trace[5] = globaltimer();
+      if (trace) epi_items += 65536;
+      const unsigned long long tp0 = trace ? globaltimer() : 0;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
       const int nch = p.bn / kChunk;
       // last chunk of this warp (largest ci < nch with ci % 2 == half), -1 if none
@@ -670,18 +673,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       release_accum();
-      __threadfence();
+      // The barrier orders every epilogue thread's slot writes before thread
+      // 0's release-acquire count; the finisher's acquire plus the second
+      // barrier make all contributors' writes visible to its threads.
       named_bar_sync(1, kEpiThreads);
+      const unsigned long long tp1 = trace ? globaltimer() : 0;
+      if (trace) epi_pub += tp1 - tp0;
       if (ethread == 0) {
-        const int done = atomicAdd(p.counters + w.tile, w.kb1 - w.kb0) + (w.kb1 - w.kb0);
+        const int done = atom_add_acq_rel_gpu(p.counters + w.tile, w.kb1 - w.kb0) + (w.kb1 - w.kb0);
         const int last = (done == sc.kb_tile);
         if (last) p.counters[w.tile] = 0;  // ready for the next call
         *bcast = last;
       }
       named_bar_sync(1, kEpiThreads);
+      const unsigned long long tp2 = trace ? globaltimer() : 0;
+      if (trace) epi_cnt += tp2 - tp1;
       const int last = *bcast;
       if (!last) continue;
-      __threadfence();
       if constexpr (kSwap) {
         const int ntok = min(p.tok_per_tile, p.n_tokens - tok0);
         for (int lt0 = half * 8; lt0 < ntok; lt0 += 16) {
@@ -733,6 +741,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
         }
       }
+      if (trace) {
+        epi_fin += globaltimer() - tp2;
+        epi_items += 1;
+      }
     }
   }
 
@@ -744,6 +756,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (trace && threadIdx.x == 64) {
       trace[6] = globaltimer();
       trace[11] = epi_wait;
+      trace[12] = epi_pub;
+      trace[13] = epi_cnt;
+      trace[14] = epi_fin;
+      trace[15] = epi_items;
     }
     tc_fence_before();
     __syncwarp();

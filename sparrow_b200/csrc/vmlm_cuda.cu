@@ -15,6 +15,7 @@
 
 #include "../../include/vmlm_cuda.h"
 #include "prep.cuh"
+#include "decode.cuh"
 #include "tc_gemm.cuh"
 
 using namespace vmlm;
@@ -90,6 +91,7 @@ struct Ctx {
   int* err_host = nullptr;  // pinned copy read after host-API calls
   DevBuf h_a, h_c, h_w, h_s, h_acc;  // host-API staging
   bool attrs_set = false;
+  std::map<std::pair<int, uint32_t>, int> dec_clusters;  // (cluster size, smem) -> co-resident clusters
 };
 
 std::map<int, Ctx*> g_ctx;
@@ -161,6 +163,7 @@ int get_ctx(int dev, Ctx** out) {
   VMLM_TRY(set_smem_attr<TcMode::kBf16Swap>());
   VMLM_TRY(set_smem_attr<TcMode::kBf16Norm>());
   VMLM_TRY(set_smem_attr<TcMode::kI8Norm>());
+  VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
   *out = c;
@@ -185,21 +188,40 @@ int host_ctx(Ctx** out) {
 
 // ------------------------------------------------------------- launches
 
+// Launch with optional programmatic dependent launch and an optional cluster
+// of `cluster` CTAs along x (1 = no cluster).
 template <typename... KArgs, typename... Args>
-int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, int cluster,
+              Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   VMLM_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return VMLM_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  return launch_ex(kern, grid, block, smem, st, pdl, 1, args...);
 }
 
 int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
@@ -272,6 +294,26 @@ NormPlan plan_norm(int rows, int N, int K, int esz, bool int_acc, int sms) {
   return best;
 }
 
+// Diagnostics: an event pair around one GEMM launch (vmlm_profile_enable).
+int prof_begin(Ctx* c, cudaStream_t st, ProfPair* pp) {
+  if (!g_prof_free.empty() && g_prof_free.back().dev == c->dev) {
+    *pp = g_prof_free.back();
+    g_prof_free.pop_back();
+  } else {
+    VMLM_CUDA(cudaEventCreate(&pp->a));
+    VMLM_CUDA(cudaEventCreate(&pp->b));
+    pp->dev = c->dev;
+  }
+  VMLM_CUDA(cudaEventRecord(pp->a, st));
+  return VMLM_OK;
+}
+
+int prof_end(cudaStream_t st, const ProfPair& pp) {
+  VMLM_CUDA(cudaEventRecord(pp.b, st));
+  g_prof_live.push_back(pp);
+  return VMLM_OK;
+}
+
 // Plan and launch the tcgen05 kernel. units_min = tiles * k-blocks with one term.
 template <TcMode MODE>
 int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool streamk,
@@ -309,20 +351,10 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
     return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma,
                   mb, p);
   ProfPair pp;
-  if (!g_prof_free.empty() && g_prof_free.back().dev == c->dev) {
-    pp = g_prof_free.back();
-    g_prof_free.pop_back();
-  } else {
-    VMLM_CUDA(cudaEventCreate(&pp.a));
-    VMLM_CUDA(cudaEventCreate(&pp.b));
-    pp.dev = c->dev;
-  }
-  VMLM_CUDA(cudaEventRecord(pp.a, st));
+  VMLM_TRY(prof_begin(c, st, &pp));
   VMLM_TRY(launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false, ma,
                   mb, p));
-  VMLM_CUDA(cudaEventRecord(pp.b, st));
-  g_prof_live.push_back(pp);
-  return VMLM_OK;
+  return prof_end(st, pp);
 }
 
 int check_dims(size_t m, size_t n, size_t k) {
@@ -331,10 +363,108 @@ int check_dims(size_t m, size_t n, size_t k) {
   return VMLM_OK;
 }
 
+// ------------------------------------------------------- Q8 decode path
+
+// Cluster size and stage ring for the decode kernel, or c == 0 when the call
+// does not fit it (more than 32 tokens, or more tiles than one wave of
+// clusters: the persistent kernel streams those better).
+struct DecPlan {
+  int c = 0;
+  int stages = 0;
+  int kbr = 0;
+  uint32_t smem = 0;
+};
+
+int max_active_clusters(Ctx* ctx, int cl, uint32_t smem, int* out) {
+  const auto key = std::make_pair(cl, smem);
+  auto it = ctx->dec_clusters.find(key);
+  if (it != ctx->dec_clusters.end()) {
+    *out = it->second;
+    return VMLM_OK;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cl * ctx->sms));
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  VMLM_CUDA(cudaOccupancyMaxActiveClusters(&n, q8_decode_kernel, &cfg));
+  ctx->dec_clusters[key] = n;
+  *out = n;
+  return VMLM_OK;
+}
+
+int plan_decode(Ctx* ctx, int M, int N, int K, DecPlan* plan) {
+  *plan = DecPlan{};
+  if (M < 1 || M > kDecMaxTok) return VMLM_OK;
+  const long long tiles = cdiv(N, kTileRows);
+  const int kb = static_cast<int>(cdiv(K, kBlockBytes));
+  const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
+  long long best_ctas = 0;
+  for (int c = 1; c <= kDecMaxCluster && c <= kb; ++c) {
+    const int kbr = static_cast<int>(cdiv(kb, c));
+    int stages = kbr < 16 ? kbr : 16;
+    while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+    if (stages < 1 || (stages < 2 && kbr > 1)) continue;
+    const uint32_t smem = dec_smem_layout(stages, rows_b, kbr, M, c).total;
+    int active = 0;
+    VMLM_TRY(max_active_clusters(ctx, c, smem, &active));
+    if (tiles > active) continue;  // one wave only
+    if (tiles * c > best_ctas) {
+      best_ctas = tiles * c;
+      *plan = DecPlan{c, stages, kbr, smem};
+    }
+  }
+  return VMLM_OK;
+}
+
+int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
+               cudaStream_t st, const DecPlan& plan) {
+  DecParams p = {};
+  p.n = N;
+  p.k = K;
+  p.m = M;
+  p.kb = static_cast<int>(cdiv(K, kBlockBytes));
+  p.cluster = plan.c;
+  p.rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
+  p.kbr_max = plan.kbr;
+  p.stages = plan.stages;
+  p.tmem_cols = pow2_at_least(p.rows_b);
+  p.vec_x = (K % 4 == 0) && aligned16(a);
+  p.x = a;
+  p.ldx = K;
+  p.w = q;
+  p.scale = scale;
+  p.out = out;
+  p.ldo = N;
+  p.err = ctx->err;
+  const long long grid = cdiv(N, kTileRows) * plan.c;
+  p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
+  CUtensorMap mw;
+  VMLM_TRY(make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+  ProfPair pp;
+  if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
+  VMLM_TRY(launch_ex(q8_decode_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), plan.smem, st, true,
+                     plan.c, mw, p));
+  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  return VMLM_OK;
+}
+
 // ------------------------------------------------------------- Q8 path
 
 int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
            cudaStream_t st) {
+  if (K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q)) {
+    DecPlan dp;
+    VMLM_TRY(plan_decode(c, M, N, K, &dp));
+    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp);
+  }
   const int kp = static_cast<int>(cdiv(K, 16) * 16);
   VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * (kp ? kp : 16)));
   VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));

@@ -108,8 +108,9 @@ def trace_enable(max_ctas: int) -> None:
 
 
 def trace_take(n_ctas: int) -> np.ndarray:
-    """The last traced launch: [n_ctas, 12] values in ns (8 globaltimer stamps, 4 summed waits)."""
-    out = np.zeros((n_ctas, 12), np.uint64)
+    """The last traced launch: [n_ctas, 16] values (8 globaltimer stamps, 4 summed waits and
+    3 summed split-tile phases in ns, then items * 65536 + tiles finished)."""
+    out = np.zeros((n_ctas, 16), np.uint64)
     check(lib().vmlm_trace_take(ctypes.c_void_p(out.ctypes.data), out.size))
     return out
 

@@ -145,6 +145,45 @@ def test_q8_zero_rows_and_extreme_scales(kernels, oracle):
         assert oracle.max_rel_err(got[r:r + 1], ref[r:r + 1]) <= TIGHT_Q8
 
 
+@pytest.mark.parametrize("m,n,k", [(32, 2304, 2304), (17, 5760, 2304), (16, 2304, 5760), (5, 640, 2304),
+                                   (2, 130, 1040), (1, 18944, 512), (9, 1, 128)])
+def test_q8_decode_cluster_shapes(kernels, oracle, m, n, k):
+    # decode kernel: K split over a cluster of CTAs, partial k-blocks, both
+    # token halves of the accumulator, a single row
+    x, q, s = q8_case(oracle, m, n, k, seed=m * 7 + k)
+    check_q8(kernels, oracle, x, q, s)
+
+
+def test_q8_decode_nonfinite_in_one_cta_range(kernels, oracle):
+    # the K range of each CTA sees only part of a row: a NaN/Inf anywhere must
+    # still turn the whole output row into the sequential f32 result
+    m, n, k = 3, 2304, 2304
+    x, q, s = q8_case(oracle, m, n, k, seed=31)
+    x[0, 2200] = np.inf
+    x[1, 3] = np.nan
+    got = kernels.q8_linear(x, q, s)
+    ref = oracle.gemm_nt_int8(x, q, s)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    assert np.array_equal(np.sign(got[np.isinf(ref)]), np.sign(ref[np.isinf(ref)]))
+    assert oracle.max_rel_err(got[2:3], ref[2:3]) <= TIGHT_Q8
+
+
+def test_q8_decode_unaligned_activations(kernels, oracle):
+    import torch
+    m, n, k = 4, 1000, 2304
+    x, q, s = q8_case(oracle, m, n, k, seed=77)
+    buf = torch.zeros(m * k + 1, dtype=torch.float32, device="cuda")
+    buf[1:].copy_(torch.from_numpy(x.ravel()))
+    dx = buf[1:].view(m, k)  # 4-byte aligned only
+    dq, ds = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    out = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    kernels.gemm_nt_int8_dev(dx, dq, ds, out, m, n, k)
+    torch.cuda.synchronize()
+    err = oracle.max_rel_err(out.cpu().numpy(), oracle.gemm_nt_int8(x, q, s))
+    assert err <= TIGHT_Q8, err
+
+
 def test_q8_deterministic(kernels, oracle):
     x, q, s = q8_case(oracle, 8, 2304, 2304, seed=5)
     a = kernels.q8_linear(x, q, s)
