@@ -226,6 +226,9 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void st_cluster_f64(uint32_t addr, double v) {
   asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
 }
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tcgen05.mma operand reads).
@@ -234,6 +237,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ------------------------------------------------ inter-CTA signalling
+
 // One thread publishes (release) or observes (acquire) at GPU scope; a CTA or
 // named barrier before / after it extends the ordering to the other threads.
 

@@ -87,6 +87,7 @@ struct TcParams {
   uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
   uint32_t* pieces;  // normal modes: [2*grid] slots of [bn][128] 32-bit partials (overwritten)
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
+  int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
   int* err;          // device error word
   unsigned long long* trace;  // optional: kTraceSlots globaltimer stamps per CTA (diagnostics)
 };
@@ -96,9 +97,10 @@ struct TcParams {
 // MMA warp, [4] last accumulator committed, [5] first accumulator seen by the
 // epilogue, [6] epilogue done, [7] TMEM released; then summed waits (ns):
 // [8] producer for free stages, [9] MMA for loaded stages, [10] MMA for a free
-// accumulator, [11] epilogue for a finished accumulator; split-tile epilogue
-// phases (ns, summed): [12] publishing partials, [13] counting arrivals, [14]
-// finishing; [15] work items * 65536 + tiles finished.
+// accumulator, [11] epilogue for a finished accumulator; epilogue phases (ns,
+// summed): [12] split tiles: publishing partials / whole tiles: TMEM loads,
+// [13] split tiles: counting arrivals / whole tiles: finishing and storing,
+// [14] split tiles: finishing; [15] work items * 65536 + tiles finished.
 constexpr int kTraceSlots = 16;
 
 struct TcSmem {
@@ -403,6 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kWeightIsA = kSwap;
   unsigned long long epi_wait = 0;  // trace: epilogue time waiting for accumulators
   unsigned long long epi_pub = 0, epi_cnt = 0, epi_fin = 0, epi_items = 0;  // trace: split-tile phases
+  bool epi_cluster_done = false;  // csplit: this epilogue thread took both cluster barrier steps
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -410,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
       int npre = 0;  // stages of item 0 whose weight half is already in flight
+      uint32_t issued_mask0 = 0;
       const Sched sc = make_sched();
       {
         // The first k-blocks of item 0 belong to term 0 whatever T turns out to be.
@@ -419,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tm0 = p.tm_fastest ? w0.tile % p.tiles_m : w0.tile / p.tiles_n;
           const int tn0 = p.tm_fastest ? w0.tile / p.tiles_m : w0.tile % p.tiles_n;
           npre = min(p.stages, w0.kb1 - w0.kb0);
+          issued_mask0 = npre >= 32 ? 0xffffffffu : ((1u << npre) - 1u);
           for (int s = 0; s < npre; ++s) {
             const int kx = (w0.kb0 + s) * p.a_box_elems;
             mbar_arrive_expect_tx(full_bar + s, L.a_bytes + L.b_bytes);
@@ -434,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_mask = 0, last_phase = 0;  // per stage: ever issued / parity of last issue
+      uint32_t issued_mask = issued_mask0, last_phase = 0;  // per stage: ever issued / parity of last issue
       unsigned long long wait_empty = 0;         // trace: time waiting for free stages
       long long cur = 0;
       WorkItem w;
@@ -623,13 +628,85 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int c = ci * kChunk;
             uint32_t v[16];
             __syncwarp();
+            const unsigned long long tl0 = trace ? globaltimer() : 0;
             tmem_ld16(tbase + c, v);
             tmem_ld_wait();
+            const unsigned long long tl1 = trace ? globaltimer() : 0;
             if (ci == my_last) release_accum();
             epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
+            if (trace) {
+              epi_pub += tl1 - tl0;              // whole tiles: time in TMEM loads
+              epi_cnt += globaltimer() - tl1;    // whole tiles: time finishing and storing
+            }
           }
         }
         continue;
+      }
+
+      if constexpr (!kSwap) {
+        if (p.csplit > 1) {
+          // K split over a cluster of S CTAs (one item each). CTA `rank`
+          // finishes columns [rank*slice, (rank+1)*slice) of the tile: the
+          // others send it their partials of those columns through
+          // distributed shared memory, into its stage buffers, which are idle
+          // once every CTA of the cluster has finished its MMAs. Received
+          // partials are [sender slot][column][128 rows] 32-bit words; the sum
+          // runs in rank order, so f32 results do not depend on timing.
+          const int S = p.csplit;
+          const int rank = static_cast<int>(cluster_ctarank());
+          const int slice = p.bn / S;
+          const int nsc = slice / 16;
+          const uint32_t* recv = reinterpret_cast<const uint32_t*>(smem);
+          cluster_arrive_release();
+          cluster_wait_acquire();  // A: every CTA of the cluster is past its MMAs
+          for (int q = 0; q < S; ++q) {
+            if (q == rank) continue;
+            const uint32_t base = mapa_shared(smem_u32(smem), static_cast<uint32_t>(q)) +
+                                  static_cast<uint32_t>(((rank - (rank > q ? 1 : 0)) * slice * kTileRows + row) * 4);
+            for (int ci = half; ci < nsc; ci += 2) {
+              uint32_t v[16];
+              __syncwarp();
+              tmem_ld16(tbase + q * slice + ci * 16, v);
+              tmem_ld_wait();
+              #pragma unroll
+              for (int j = 0; j < 16; ++j) st_cluster_u32(base + static_cast<uint32_t>((ci * 16 + j) * kTileRows * 4), v[j]);
+            }
+          }
+          const unsigned long long tp1 = trace ? globaltimer() : 0;
+          if (trace) epi_pub += tp1 - tp0;
+          cluster_arrive_release();
+          cluster_wait_acquire();  // B: all partials delivered
+          const unsigned long long tp2 = trace ? globaltimer() : 0;
+          if (trace) epi_cnt += tp2 - tp1;
+          for (int ci = half; ci < nsc; ci += 2) {
+            uint32_t own[16], v[16];
+            __syncwarp();
+            tmem_ld16(tbase + rank * slice + ci * 16, own);
+            tmem_ld_wait();
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0u;
+            for (int q = 0; q < S; ++q) {
+              const uint32_t* src = recv + ((q - (q > rank ? 1 : 0)) * slice + ci * 16) * kTileRows + row;
+              #pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t a = (q == rank) ? own[j] : src[j * kTileRows];
+                if constexpr (kInt)
+                  v[j] += a;
+                else
+                  v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(a)));
+              }
+            }
+            const int c = rank * slice + ci * 16;
+            epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
+          }
+          release_accum();
+          epi_cluster_done = true;
+          if (trace) {
+            epi_fin += globaltimer() - tp2;
+            epi_items += 1;
+          }
+          continue;
+        }
       }
 
       // Split tile. Slots are column-major ([column][128 rows]) so that a
@@ -745,6 +822,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         epi_fin += globaltimer() - tp2;
         epi_items += 1;
       }
+    }
+  }
+
+  // A cluster-split launch: every thread takes the two cluster barrier steps
+  // exactly once (warps 0 and 1 here; epilogue threads that gave up waiting
+  // for their accumulator too), so no CTA waits for a thread that left.
+  if (p.csplit > 1) {
+    bool todo = warp < 2;
+    if (warp >= 2) todo = !epi_cluster_done;
+    if (warp < 2) __syncwarp();
+    if (todo) {
+      cluster_arrive_release();
+      cluster_wait_acquire();
+      cluster_arrive_release();
+      cluster_wait_acquire();
     }
   }
 

@@ -255,34 +255,78 @@ bool use_streamk(const TcParams& p, int sms) {
   return static_cast<long long>(p.tiles_m) * p.tiles_n < 4ll * sms;
 }
 
+// Stage ring depth of the tcgen05 kernel for tile width bn (as many as fit).
+int tc_stages(int bn) {
+  int stages = 16;
+  while (stages >= 2 && tc_smem_layout(stages, bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  return stages;
+}
+
+// Co-resident clusters of `cl` CTAs of tc_gemm_kernel<MODE> at `smem` bytes.
+template <TcMode MODE>
+int tc_max_clusters(Ctx* ctx, int cl, uint32_t smem, int* out) {
+  const auto key = std::make_pair(1000 + 16 * static_cast<int>(MODE) + cl, smem);
+  auto it = ctx->dec_clusters.find(key);
+  if (it != ctx->dec_clusters.end()) {
+    *out = it->second;
+    return VMLM_OK;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cl * ctx->sms));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  VMLM_CUDA(cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<MODE>, &cfg));
+  ctx->dec_clusters[key] = n;
+  *out = n;
+  return VMLM_OK;
+}
+
 // Tile width and K split for a normal-mode GEMM (rows x N output, 128-row
 // tiles). Each candidate is costed as waves x per-CTA time, the per-CTA time
 // being the larger of its operand traffic at a per-SM L2 rate and its MMA work
 // at a per-SM tensor rate derated for narrow tiles (narrow UMMA N runs the
-// tensor pipe less efficiently), plus the split-tile reduction. A split of 2
-// keeps f32 results deterministic (0 + a + b in either order); integer
-// accumulators allow wider splits.
+// tensor pipe less efficiently), plus the split-tile reduction. A K split runs
+// over a thread-block cluster (partials exchanged in distributed shared memory,
+// summed in rank order), so it is used only when every cluster of the launch
+// is co-resident.
 struct NormPlan {
   int bn;
   int split;
 };
 
-NormPlan plan_norm(int rows, int N, int K, int esz, bool int_acc, int sms) {
+template <TcMode MODE>
+int plan_norm(Ctx* ctx, int rows, int N, int K, int esz, bool int_acc, NormPlan* out) {
   const int cand[3] = {256, 128, 64};
   const double eff[3] = {1.0, 0.85, 0.5};
   const double l2_bps = 120e9;                             // per SM
+  const double dsm_bps = 150e9;                            // per SM, distributed shared memory
   const double mac_ps = (int_acc ? 22e12 : 11e12) / 2.0;  // MACs per second per SM
+  const int sms = ctx->sms;
   NormPlan best{256, 1};
   double best_t = 1e300;
   for (int i = 0; i < 3; ++i) {
     const long long tiles = cdiv(rows, kTileRows) * cdiv(N, cand[i]);
-    const int max_split = int_acc ? 4 : 2;
-    for (int split = 1; split <= max_split; split *= 2) {
-      if (split > 1 && tiles * split > sms) continue;  // only split to fill a single wave
+    const long long kb = cdiv(K, 128 / esz);
+    for (int split = 1; split <= 4; split *= 2) {
+      if (split > 1) {
+        if (tiles * split > sms || split > kb) continue;
+        int active = 0;
+        VMLM_TRY(tc_max_clusters<MODE>(ctx, split, tc_smem_layout(tc_stages(cand[i]), cand[i]).total, &active));
+        if (tiles > active) continue;
+      }
       const double kk = static_cast<double>(K) / split;
       const double t_load = (kTileRows + cand[i]) * kk * esz / l2_bps;
       const double t_mma = static_cast<double>(kTileRows) * cand[i] * kk / (mac_ps * eff[i]);
-      const double t_red = split > 1 ? 2.0 * kTileRows * cand[i] * 4 * (split - 1) / l2_bps : 0.0;
+      const double t_red =
+          split > 1 ? (split - 1.0) / split * kTileRows * cand[i] * 4 / dsm_bps + 1.0e-6 : 0.0;
       const double waves = static_cast<double>(cdiv(tiles * split, sms));
       const double t = waves * ((t_load > t_mma ? t_load : t_mma) + t_red);
       if (t < best_t * 0.999) {
@@ -291,7 +335,8 @@ NormPlan plan_norm(int rows, int N, int K, int esz, bool int_acc, int sms) {
       }
     }
   }
-  return best;
+  *out = best;
+  return VMLM_OK;
 }
 
 // Diagnostics: an event pair around one GEMM launch (vmlm_profile_enable).
@@ -318,29 +363,33 @@ int prof_end(cudaStream_t st, const ProfPair& pp) {
 template <TcMode MODE>
 int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool streamk,
            bool pdl, int split = 0) {
-  int stages = 16;
-  while (stages >= 2 && tc_smem_layout(stages, p.bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  const int stages = tc_stages(p.bn);
   if (stages < 2) return fail(VMLM_ERR_SHAPE, "tile too large for shared memory");
   p.stages = stages;
   p.tmem_cols = pow2_at_least(2 * p.bn);
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   const long long units_min = tiles * p.kb_per_term;
   long long grid = streamk ? (units_min < c->sms ? units_min : c->sms) : (tiles < c->sms ? tiles : c->sms);
+  constexpr bool kSwapMode = (MODE == TcMode::kQ8Swap || MODE == TcMode::kBf16Swap);
+  p.csplit = 0;
   if (split > 1) {
-    // an explicit K split: exactly `split` CTAs per tile (stream-K with grid = tiles * split)
-    if (split > p.kb_per_term) split = p.kb_per_term;
+    // an explicit K split: exactly `split` CTAs per tile (stream-K ranges with
+    // grid = tiles * split); normal modes run it over a cluster of `split` CTAs
+    while (split > p.kb_per_term) split >>= 1;
     grid = tiles * split;
     streamk = split > 1;
+    if (!kSwapMode && split > 1) p.csplit = split;
   }
   if (grid < 1) grid = 1;
   p.streamk = streamk ? 1 : 0;
-  if (streamk) {
-    if (MODE == TcMode::kQ8Swap || MODE == TcMode::kBf16Swap)
+  if (streamk && p.csplit == 0) {
+    if (kSwapMode)
       VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
     else
       VMLM_TRY(ensure(c->pieces, static_cast<size_t>(2 * grid) * kTileRows * p.bn * 4));
     VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
   }
+  const int cluster = p.csplit > 1 ? p.csplit : 1;
   p.slots = static_cast<uint32_t*>(c->slots.p);
   p.pieces = static_cast<uint32_t*>(c->pieces.p);
   p.counters = static_cast<int*>(c->counters.p);
@@ -348,12 +397,12 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
   const TcSmem L = tc_smem_layout(stages, p.bn);
   if (!g_profile)
-    return launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl, ma,
-                  mb, p);
+    return launch_ex(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, pdl,
+                     cluster, ma, mb, p);
   ProfPair pp;
   VMLM_TRY(prof_begin(c, st, &pp));
-  VMLM_TRY(launch(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false, ma,
-                  mb, p));
+  VMLM_TRY(launch_ex(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false,
+                     cluster, ma, mb, p));
   return prof_end(st, pp);
 }
 
@@ -521,6 +570,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
                   b, a, static_cast<long long>(K), out, static_cast<long long>(N), M, N, K);
   }
   const int kp = static_cast<int>(cdiv(K, 8) * 8);
+  const bool swap = M <= 80;
   VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * kp * 2));
   VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));
   uint16_t* terms = static_cast<uint16_t*>(c->act.p);
@@ -528,7 +578,6 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   int* nonf = static_cast<int*>(c->small.p) + M;
   VMLM_TRY(ensure(c->sync, 64, true));
   unsigned* done = static_cast<unsigned*>(c->sync.p);
-  const bool swap = M <= 80;
   VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
                   kp, swap ? 0 : 1, terms, flags, nonf, done));
   TcParams p = {};
@@ -562,7 +611,8 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   }
   p.rows = M;
   p.cols = N;
-  const NormPlan plan = plan_norm(M, N, K, 2, false, c->sms);
+  NormPlan plan;
+  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &plan));
   p.bn = plan.bn;
   p.max_terms = 3;
   p.term_stride = kp;
@@ -589,7 +639,8 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   TcParams p = {};
   p.rows = M;
   p.cols = N;
-  const NormPlan plan = plan_norm(M, N, K, 1, true, c->sms);
+  NormPlan plan;
+  VMLM_TRY(plan_norm<TcMode::kI8Norm>(c, M, N, K, 1, true, &plan));
   p.bn = plan.bn;
   p.kb_per_term = static_cast<int>(cdiv(K, 128));
   p.max_terms = 1;

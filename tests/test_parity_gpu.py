@@ -236,6 +236,28 @@ def test_c2_shape_general_f32_activations(kernels, oracle):
     check_bf16(kernels, oracle, x, w)
 
 
+def test_bf16_term_planes_stay_exact_across_calls(kernels, oracle):
+    # the GEMM writes a row's mid / lo term planes only where they are needed
+    # now or were non-zero after the previous call: alternate activations with
+    # and without sub-bf16 bits, including single rows that need them
+    m, n, k = 512, 768, 1024
+    w = oracle.f32_to_bf16(oracle.fill_normal(n * k, 2, 0.02)).reshape(n, k)
+    general = oracle.fill_normal(m * k, 3, 1.0).reshape(m, k)
+    exact = oracle.bf16_to_f32(oracle.f32_to_bf16(general))
+    one = exact.copy()
+    one[5, 17] += np.float32(3e-3)
+    one[300, 1000] = np.float32(0.1)
+    for x in (general, exact, one, general, one, exact):
+        check_bf16(kernels, oracle, x, w)
+
+
+@pytest.mark.parametrize("m,n,k", [(129, 4096, 512), (2000, 256, 256), (640, 2304, 2304)])
+def test_bf16_row_block_waits(kernels, oracle, m, n, k):
+    # many CTAs converting a few rows each; blocks with a partial last block
+    x, w = bf16_case(oracle, m, n, k, seed=m + 1, exact_x=(m % 2 == 0))
+    check_bf16(kernels, oracle, x, w)
+
+
 @pytest.mark.parametrize("m", [1, 8, 32, 80])
 def test_bf16_decode_shapes(kernels, oracle, m):
     x, w = bf16_case(oracle, m, 5760, 2304, seed=m, exact_x=False)
