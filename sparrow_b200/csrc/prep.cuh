@@ -199,6 +199,107 @@ __device__ __forceinline__ void bf16_split(float v, uint16_t& h, uint16_t& m, ui
   if (l & 0x7fffu) flags |= 4;
 }
 
+// Split terms for the normal-mode GEMM, layout out[t*3*kp + j*kp + k]. One
+// CTA of kNormPrepThreads per token row. The hi plane is always written. The
+// mid / lo plane of a row is written only when the row has non-zero values
+// there now, or had them after the previous call (dirty[t] bits 2 / 4), so
+// every plane keeps holding this call's exact terms while activations that
+// are already bf16 values (the usual prefill input) cost one plane of writes.
+// Rows with a non-zero mid / lo plane OR bit 2 / 4 into *orword; CTA 0 clears
+// *orword_next for the next call (calls alternate between two words).
+constexpr int kNormPrepThreads = 128;
+constexpr int kNormPrepKeep = 8;  // float4 chunks per thread kept in registers
+
+__device__ __forceinline__ uint2 pack_bf16x4(const uint16_t (&h)[4]) {
+  return make_uint2(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16));
+}
+
+__global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
+    const float* __restrict__ x, long long ldx, int M, int K, int kp, int vec, uint16_t* __restrict__ out,
+    uint8_t* __restrict__ dirty, unsigned* __restrict__ orword, unsigned* __restrict__ orword_next) {
+  pdl_launch_dependents();
+  __shared__ int redi[32];
+  const int t = blockIdx.x;
+  if (t >= M) return;
+  if (t == 0 && threadIdx.x == 0) *orword_next = 0u;
+  const float* xr = x + static_cast<long long>(t) * ldx;
+  uint16_t* o0 = out + static_cast<long long>(t) * 3 * kp;
+  const int nchunk = kp >> 2;  // kp % 8 == 0
+  const bool kept = nchunk <= kNormPrepKeep * kNormPrepThreads;
+  const int old_dirty = dirty[t];
+  auto load = [&](int ch) -> float4 {
+    const int k = ch * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ch < nchunk && k < K) {
+      if (vec && k + 3 < K) {
+        v = *reinterpret_cast<const float4*>(xr + k);
+      } else {
+        v.x = xr[k];
+        v.y = k + 1 < K ? xr[k + 1] : 0.f;
+        v.z = k + 2 < K ? xr[k + 2] : 0.f;
+        v.w = k + 3 < K ? xr[k + 3] : 0.f;
+      }
+    }
+    return v;
+  };
+  float4 keep[kNormPrepKeep];
+  int flags = 0;
+  // pass 1: hi plane and the row's term flags
+  for (int c0 = 0; c0 < nchunk; c0 += kNormPrepKeep * kNormPrepThreads) {
+    #pragma unroll
+    for (int i = 0; i < kNormPrepKeep; ++i) keep[i] = load(c0 + threadIdx.x + i * kNormPrepThreads);
+    #pragma unroll
+    for (int i = 0; i < kNormPrepKeep; ++i) {
+      const int ch = c0 + threadIdx.x + i * kNormPrepThreads;
+      if (ch >= nchunk) break;
+      const float4 v = keep[i];
+      const uint32_t ux = __float_as_uint(v.x), uy = __float_as_uint(v.y);
+      const uint32_t uz = __float_as_uint(v.z), uw = __float_as_uint(v.w);
+      uint2 hi;
+      if (((ux | uy | uz | uw) & 0xffffu) == 0u) {
+        // already bf16 values (NaN and Inf included): hi is the top half
+        hi = make_uint2((ux >> 16) | (uy & 0xffff0000u), (uz >> 16) | (uw & 0xffff0000u));
+      } else {
+        uint16_t h[4], m[4], l[4];
+        bf16_split(v.x, h[0], m[0], l[0], flags);
+        bf16_split(v.y, h[1], m[1], l[1], flags);
+        bf16_split(v.z, h[2], m[2], l[2], flags);
+        bf16_split(v.w, h[3], m[3], l[3], flags);
+        hi = pack_bf16x4(h);
+      }
+      reinterpret_cast<uint2*>(o0)[ch] = hi;
+    }
+  }
+  flags = block_or(flags & 6, redi);
+  const int need = (flags | old_dirty) & 6;
+  // pass 2: mid / lo planes where needed
+  if (need) {
+    for (int c0 = 0; c0 < nchunk; c0 += kNormPrepKeep * kNormPrepThreads) {
+      if (!kept) {
+        #pragma unroll
+        for (int i = 0; i < kNormPrepKeep; ++i) keep[i] = load(c0 + threadIdx.x + i * kNormPrepThreads);
+      }
+      #pragma unroll
+      for (int i = 0; i < kNormPrepKeep; ++i) {
+        const int ch = c0 + threadIdx.x + i * kNormPrepThreads;
+        if (ch >= nchunk) break;
+        int f = 0;
+        uint16_t h[4], m[4], l[4];
+        bf16_split(keep[i].x, h[0], m[0], l[0], f);
+        bf16_split(keep[i].y, h[1], m[1], l[1], f);
+        bf16_split(keep[i].z, h[2], m[2], l[2], f);
+        bf16_split(keep[i].w, h[3], m[3], l[3], f);
+        if (need & 2) reinterpret_cast<uint2*>(o0 + kp)[ch] = pack_bf16x4(m);
+        if (need & 4) reinterpret_cast<uint2*>(o0 + 2 * kp)[ch] = pack_bf16x4(l);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (flags != old_dirty) dirty[t] = static_cast<uint8_t>(flags);
+    if (flags) atomicOr(orword, static_cast<unsigned>(flags));
+  }
+}
+
 // One CTA per token. Layout 0 (swap): out[(3t+j)*kp + k]. Layout 1 (normal):
 // out[t*3*kp + j*kp + k]. Columns [K, kp) are 0; kp % 8 == 0. term_flags[t]
 // gets 1 | (2 if a mid term is non-zero) | (4 if a lo term is non-zero). The

@@ -87,6 +87,11 @@ struct Ctx {
   DevBuf pieces;    // normal-mode split-tile partials (overwritten every call)
   DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
   DevBuf sync;      // prep completion counter and term-flag OR (zeroed once, self-resetting)
+  // bf16 normal mode: term planes and per-row dirty bits of their own (zeroed
+  // whenever the layout changes), and two term-flag words used by alternate calls
+  DevBuf norm_terms, norm_dirty, norm_flags;
+  int norm_m = -1, norm_kp = -1;
+  unsigned norm_parity = 0;
   int* err = nullptr;       // device error word
   int* err_host = nullptr;  // pinned copy read after host-API calls
   DevBuf h_a, h_c, h_w, h_s, h_acc;  // host-API staging
@@ -562,6 +567,58 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
 
 // ------------------------------------------------------------ bf16 path
 
+// bf16 normal mode (more than 80 tokens): split terms written by
+// bf16_terms_norm_kernel into buffers of their own, then the tcgen05 GEMM
+// with as many term passes as the activations need.
+int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, int kp,
+                  cudaStream_t st) {
+  const size_t tbytes = static_cast<size_t>(3) * M * kp * 2;
+  if (M != c->norm_m || kp != c->norm_kp) {
+    // a new layout: planes and dirty bits start over at zero
+    VMLM_TRY(ensure(c->norm_terms, tbytes));
+    VMLM_TRY(ensure(c->norm_dirty, static_cast<size_t>(M)));
+    VMLM_CUDA(cudaMemsetAsync(c->norm_terms.p, 0, tbytes, st));
+    VMLM_CUDA(cudaMemsetAsync(c->norm_dirty.p, 0, static_cast<size_t>(M), st));
+    c->norm_m = M;
+    c->norm_kp = kp;
+  }
+  VMLM_TRY(ensure(c->norm_flags, 256, true));
+  unsigned* fw = static_cast<unsigned*>(c->norm_flags.p);
+  unsigned* orword = fw + 32 * c->norm_parity;  // the two words sit on separate 128-byte lines
+  unsigned* orword_next = fw + 32 * (c->norm_parity ^ 1u);
+  c->norm_parity ^= 1u;
+  uint16_t* terms = static_cast<uint16_t*>(c->norm_terms.p);
+  VMLM_TRY(launch(bf16_terms_norm_kernel, dim3(M), dim3(kNormPrepThreads), 0, st, false, a,
+                  static_cast<long long>(K), M, K, kp, static_cast<int>((K % 4 == 0) && aligned16(a)), terms,
+                  static_cast<uint8_t*>(c->norm_dirty.p), orword, orword_next));
+  TcParams p = {};
+  p.rows = M;
+  p.cols = N;
+  NormPlan plan;
+  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &plan));
+  p.bn = plan.bn;
+  p.max_terms = 3;
+  p.a_box_elems = 64;
+  p.kb_per_term = static_cast<int>(cdiv(K, 64));
+  p.term_stride = kp;
+  p.term_flags = reinterpret_cast<const int*>(orword);
+  p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
+  p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+  p.tm_fastest = 1;
+  p.out = out;
+  p.ldo = N;
+  p.vec_out = (N % 4 == 0) && aligned16(out);
+  p.n_tokens = M;
+  p.x = a;
+  p.ldx = K;
+  p.w = b;
+  p.k = K;
+  CUtensorMap ma, mb;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
+  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true, plan.split);
+}
+
 int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, cudaStream_t st) {
   const bool tc_ok = K > 0 && K % 8 == 0 && aligned16(b);
   if (!tc_ok) {
@@ -570,7 +627,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
                   b, a, static_cast<long long>(K), out, static_cast<long long>(N), M, N, K);
   }
   const int kp = static_cast<int>(cdiv(K, 8) * 8);
-  const bool swap = M <= 80;
+  if (M > 80) return run_bf16_norm(c, a, b, out, M, N, K, kp, st);
   VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * kp * 2));
   VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));
   uint16_t* terms = static_cast<uint16_t*>(c->act.p);
@@ -579,7 +636,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   VMLM_TRY(ensure(c->sync, 64, true));
   unsigned* done = static_cast<unsigned*>(c->sync.p);
   VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
-                  kp, swap ? 0 : 1, terms, flags, nonf, done));
+                  kp, 0, terms, flags, nonf, done));
   TcParams p = {};
   p.max_terms = 1;
   p.a_box_elems = 64;
@@ -593,7 +650,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   p.w = b;
   p.k = K;
   CUtensorMap ma, mb;
-  if (swap) {
+  {
     const int tok = static_cast<int>(cdiv(M, 16) * 16);
     p.rows = N;
     p.cols = 3 * M;
@@ -609,21 +666,6 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
     VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, K, 3ull * M, 2ull * kp, 64, p.bn));
     return run_tc<TcMode::kBf16Swap>(c, st, ma, mb, p, use_streamk(p, c->sms), true);
   }
-  p.rows = M;
-  p.cols = N;
-  NormPlan plan;
-  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &plan));
-  p.bn = plan.bn;
-  p.max_terms = 3;
-  p.term_stride = kp;
-  p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
-  p.tiles_n = static_cast<int>(cdiv(N, p.bn));
-  p.tm_fastest = 1;
-  p.vec_out = (N % 4 == 0) && aligned16(out);
-  p.n_tokens = M;
-  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
-  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
-  return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true, plan.split);
 }
 
 // ---------------------------------------------------------- int8 x int8
@@ -690,6 +732,7 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
     if (c->counters.p) cudaMemset(c->counters.p, 0, c->counters.bytes);
     if (c->sync.p) cudaMemset(c->sync.p, 0, c->sync.bytes);
     if (c->slots.p) cudaMemset(c->slots.p, 0, c->slots.bytes);
+    if (c->norm_flags.p) cudaMemset(c->norm_flags.p, 0, c->norm_flags.bytes);
     *c->err_host = 0;
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
