@@ -26,12 +26,14 @@
 //
 // Scheduling is static. Units are (tile, k-block) pairs ordered tile-major.
 // Either every CTA takes whole tiles round-robin, or each CTA takes a
-// contiguous range of units (stream-K, or an explicit K split of every tile
-// over `split` CTAs). The CTA that brings a split tile's counter to the full
-// k-block count finishes the tile. Swap modes add one combined value per token
-// atomically into a self-clearing slot (exact for Q8; last-bit order
-// dependent for bf16); normal modes store per-CTA partials and sum them in CTA
-// order (deterministic).
+// contiguous range of units:
+//   swap modes (stream-K): the CTA that brings a split tile's counter to the
+//     full k-block count finishes it; contributors add one combined value per
+//     token atomically into a self-clearing slot (exact for Q8; last-bit order
+//     dependent for bf16);
+//   normal modes (explicit K split over a thread-block cluster of csplit
+//     CTAs): partial tiles are exchanged through distributed shared memory and
+//     each CTA finishes a column slice, summing in rank order (deterministic).
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -85,7 +87,6 @@ struct TcParams {
   int k;
   // split-tile fixup
   uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
-  uint32_t* pieces;  // normal modes: [2*grid] slots of [bn][128] 32-bit partials (overwritten)
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
   int* err;          // device error word
@@ -709,21 +710,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 
-      // Split tile. Slots are column-major ([column][128 rows]) so that a
-      // warp's 32 rows of one column are contiguous.
-      //  swap modes: every contributor adds one combined value per real token
-      //    ([tok][128]) atomically into the slot of the CTA that holds the
-      //    tile's last unit; the finisher reads it and clears it.
-      //  normal modes: every contributor stores its 32-bit partial ([bn][128])
-      //    in its own slot (2*cta + 0 for the head of its range, + 1 for the
-      //    tail); the finisher sums the contributors' slots in CTA order, so
-      //    f32 results do not depend on arrival order.
-      const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
-      const int slot = kSwap ? sc.owner(tile_u0 + sc.kb_tile - 1) : 2 * cta + (sc.start(cta) >= tile_u0 ? 0 : 1);
-      uint32_t* scol = (kSwap ? p.slots : p.pieces) + static_cast<long long>(slot) * kTileRows * p.bn + row;
-      using SV = typename SwapVal<MODE>::T;
-      SV* vcol = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) + row;
+      // Split tile of a swap mode (stream-K). The slot is column-major
+      // ([tok][128 rows], a warp's 32 rows of one token contiguous). Every
+      // contributor adds one combined value per real token atomically into the
+      // slot of the CTA that holds the tile's last unit; the CTA whose count
+      // completes the tile reads the slot, clears it and finishes the tile.
       if constexpr (kSwap) {
+        const long long tile_u0 = static_cast<long long>(w.tile) * sc.kb_tile;
+        const int slot = sc.owner(tile_u0 + sc.kb_tile - 1);
+        using SV = typename SwapVal<MODE>::T;
+        SV* vcol = reinterpret_cast<SV*>(p.slots + static_cast<long long>(slot) * kTileRows * p.bn) + row;
         for (int ci = half; ci < nch; ci += 2) {
           const int c = ci * kChunk;
           uint32_t v[48];
@@ -738,36 +734,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (tok0 + lt < p.n_tokens) atomicAdd(vcol + lt * kTileRows, swap_combine<MODE>(v + 3 * j));
           }
         }
-      } else {
-        for (int ci = half; ci < nch; ci += 2) {
-          const int c = ci * kChunk;
-          uint32_t v[16];
-          __syncwarp();
-          tmem_ld16(tbase + c, v);
-          tmem_ld_wait();
-          #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(scol + (c + j) * kTileRows, v[j]);
+        release_accum();
+        // The barrier orders every epilogue thread's slot writes before thread
+        // 0's release-acquire count; the finisher's acquire plus the second
+        // barrier make all contributors' writes visible to its threads.
+        named_bar_sync(1, kEpiThreads);
+        const unsigned long long tp1 = trace ? globaltimer() : 0;
+        if (trace) epi_pub += tp1 - tp0;
+        if (ethread == 0) {
+          const int done = atom_add_acq_rel_gpu(p.counters + w.tile, w.kb1 - w.kb0) + (w.kb1 - w.kb0);
+          const int last = (done == sc.kb_tile);
+          if (last) p.counters[w.tile] = 0;  // ready for the next call
+          *bcast = last;
         }
-      }
-      release_accum();
-      // The barrier orders every epilogue thread's slot writes before thread
-      // 0's release-acquire count; the finisher's acquire plus the second
-      // barrier make all contributors' writes visible to its threads.
-      named_bar_sync(1, kEpiThreads);
-      const unsigned long long tp1 = trace ? globaltimer() : 0;
-      if (trace) epi_pub += tp1 - tp0;
-      if (ethread == 0) {
-        const int done = atom_add_acq_rel_gpu(p.counters + w.tile, w.kb1 - w.kb0) + (w.kb1 - w.kb0);
-        const int last = (done == sc.kb_tile);
-        if (last) p.counters[w.tile] = 0;  // ready for the next call
-        *bcast = last;
-      }
-      named_bar_sync(1, kEpiThreads);
-      const unsigned long long tp2 = trace ? globaltimer() : 0;
-      if (trace) epi_cnt += tp2 - tp1;
-      const int last = *bcast;
-      if (!last) continue;
-      if constexpr (kSwap) {
+        named_bar_sync(1, kEpiThreads);
+        const unsigned long long tp2 = trace ? globaltimer() : 0;
+        if (trace) epi_cnt += tp2 - tp1;
+        const int last = *bcast;
+        if (!last) continue;
         const int ntok = min(p.tok_per_tile, p.n_tokens - tok0);
         for (int lt0 = half * 8; lt0 < ntok; lt0 += 16) {
           SV vals[8];
@@ -783,44 +767,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 swap_finish<MODE>(p, grow, tok0 + lt0 + j, lt0 + j, vals[j], scale_n, s_exp, s_bad);
           }
         }
-      } else {
-        const int c_first = sc.owner(tile_u0);
-        const int c_last = sc.owner(tile_u0 + sc.kb_tile - 1);
-        for (int ci = half; ci < nch; ci += 2) {
-          const int c = ci * kChunk;
-          uint32_t v[16];
-          #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0u;
-          for (int q = c_first; q <= c_last; q += 2) {
-            // two contributors' loads in flight at a time, summed in CTA order
-            const int wq0 = (sc.start(q) >= tile_u0) ? 0 : 1;
-            const uint32_t* s0 = p.pieces + static_cast<long long>(2 * q + wq0) * kTileRows * p.bn + row;
-            const bool has1 = q + 1 <= c_last;
-            const uint32_t* s1 = p.pieces + static_cast<long long>(2 * (q + 1)) * kTileRows * p.bn + row;
-            uint32_t a[16], b[16];
-            #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              a[j] = __ldcg(s0 + (c + j) * kTileRows);
-              b[j] = has1 ? __ldcg(s1 + (c + j) * kTileRows) : 0u;
-            }
-            #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if constexpr (kInt) {
-                v[j] += a[j];
-                if (has1) v[j] += b[j];
-              } else {
-                float f = __fadd_rn(__uint_as_float(v[j]), __uint_as_float(a[j]));
-                if (has1) f = __fadd_rn(f, __uint_as_float(b[j]));
-                v[j] = __float_as_uint(f);
-              }
-            }
-          }
-          epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, reinterpret_cast<const float*>(s_exp) + c);
+        if (trace) {
+          epi_fin += globaltimer() - tp2;
+          epi_items += 1;
         }
-      }
-      if (trace) {
-        epi_fin += globaltimer() - tp2;
-        epi_items += 1;
       }
     }
   }

@@ -84,7 +84,6 @@ struct Ctx {
   DevBuf act;       // digit planes / split terms
   DevBuf small;     // exps | nonfinite | term_flags, each [M] int
   DevBuf slots;     // swap-mode split-tile accumulators (zeroed once, self-clearing)
-  DevBuf pieces;    // normal-mode split-tile partials (overwritten every call)
   DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
   DevBuf sync;      // prep completion counter and term-flag OR (zeroed once, self-resetting)
   // bf16 normal mode: term planes and per-row dirty bits of their own (zeroed
@@ -387,16 +386,12 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   }
   if (grid < 1) grid = 1;
   p.streamk = streamk ? 1 : 0;
-  if (streamk && p.csplit == 0) {
-    if (kSwapMode)
-      VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
-    else
-      VMLM_TRY(ensure(c->pieces, static_cast<size_t>(2 * grid) * kTileRows * p.bn * 4));
+  if (streamk && kSwapMode) {
+    VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
     VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
   }
   const int cluster = p.csplit > 1 ? p.csplit : 1;
   p.slots = static_cast<uint32_t*>(c->slots.p);
-  p.pieces = static_cast<uint32_t*>(c->pieces.p);
   p.counters = static_cast<int*>(c->counters.p);
   p.err = c->err;
   p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
@@ -782,8 +777,8 @@ int vmlm_shutdown(void) {
     Ctx* c = kv.second;
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
-    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->pieces, &c->counters, &c->sync, &c->h_a, &c->h_c, &c->h_w,
-                      &c->h_s, &c->h_acc})
+    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->sync, &c->norm_terms, &c->norm_dirty,
+                      &c->norm_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
