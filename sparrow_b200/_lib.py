@@ -35,6 +35,12 @@ SIGNATURES = {
     "vmlm_gemm_i8i8_dev": (I, [P, P, P, P, P, S, S, S, P]),
     "vmlm_gemm_nt_int8_dev_noalloc": (I, [P, P, P, P, S, S, S, P]),
     "vmlm_sync": (I, [P]),
+    "vmlm_sharded_gemm_nt_int8_dev": (I, [P, P, P, P, P, I, I, S, S, S, P]),
+    "vmlm_sharded_gemm_i8i8_dev": (I, [P, P, P, P, P, I, I, S, S, S, P]),
+    "vmlm_sharded_reset": (I, [P]),
+    "vmlm_ipc_handle": (I, [P, P]),
+    "vmlm_ipc_open": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
+    "vmlm_ipc_close": (I, [P]),
     "vmlm_launch_count": (ctypes.c_uint64, []),
     "vmlm_profile_enable": (I, [I]),
     "vmlm_profile_take": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),

@@ -21,7 +21,11 @@ enum DevErr : int {
   kDevTimeoutAccum = 3,     // epilogue waited too long for an accumulator
   kDevTimeoutAccumFree = 4, // MMA warp waited too long for a free accumulator
   kDevTimeoutDrain = 5,
+  kDevTimeoutPeers = 6,     // a row-sharded call waited too long for the other ranks' outputs
 };
+
+// Waits on other GPUs (row-sharded calls) allow for ranks that launch later.
+constexpr unsigned long long kPeerWaitLimitNs = 5000000000ull;  // 5 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -251,6 +255,17 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+
+// System-scope signalling between GPUs of a row-sharded call.
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_release_sys(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Named barrier over a subset of warps (ids 1..15; 0 is __syncthreads). The

@@ -54,6 +54,7 @@ constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, splitting the
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kMaxTokPerTile = 128;   // swap modes: tokens per column tile (bn/3 <= 85)
+constexpr int kMaxPeers = 8;          // ranks of a row-sharded call
 
 struct TcParams {
   int rows;          // extent of A rows (W rows in swap modes, tokens in normal modes)
@@ -89,6 +90,19 @@ struct TcParams {
   uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
+  // Row-sharded call with the all-gather in the epilogue (npeers > 0): this
+  // rank computes output columns [col_off, col_off + its rows) and stores every
+  // value into all npeers ranks' full C (peer_out[q], row stride ldo) over
+  // NVLink. When its last CTA is done it adds 1 to every rank's inbox, and the
+  // kernel ends once its own inbox reaches inbox_target (npeers per call made
+  // on that inbox so far, this one included).
+  int npeers;
+  int rank;
+  long long col_off;
+  float* peer_out[kMaxPeers];
+  unsigned* peer_inbox[kMaxPeers];
+  unsigned* done_ctr;    // this rank's CTA completion counter (self-resetting)
+  unsigned inbox_target;
   int* err;          // device error word
   unsigned long long* trace;  // optional: kTraceSlots globaltimer stamps per CTA (diagnostics)
 };
@@ -228,15 +242,25 @@ __device__ __forceinline__ void epi_norm16(const TcParams& p, int row0, int col0
     if (p.acc_out)
       store_block_32x16(reinterpret_cast<uint32_t*>(p.acc_out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf,
                         v);
-    if (p.out) {
+    if (p.out || p.npeers) {
       uint32_t f[16];
       #pragma unroll
       for (int j = 0; j < 16; ++j)
         f[j] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), s_scale[j]));
-      store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, f);
+      if (p.npeers == 0) {
+        store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, f);
+      } else {
+        for (int q = 0; q < p.npeers; ++q)
+          store_block_32x16(reinterpret_cast<uint32_t*>(p.peer_out[q] + p.col_off), p.ldo, row0, p.rows, col0,
+                            p.cols, p.vec_out, buf, f);
+      }
     }
-  } else {
+  } else if (p.npeers == 0) {
     store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, v);
+  } else {
+    for (int q = 0; q < p.npeers; ++q)
+      store_block_32x16(reinterpret_cast<uint32_t*>(p.peer_out[q] + p.col_off), p.ldo, row0, p.rows, col0, p.cols,
+                        p.vec_out, buf, v);
   }
 }
 
@@ -300,7 +324,12 @@ __device__ __forceinline__ void swap_finish(const TcParams& p, int n, int t, int
   } else {
     r = val;
   }
-  p.out[static_cast<long long>(t) * p.ldo + n] = r;
+  const long long idx = static_cast<long long>(t) * p.ldo + n;
+  if (p.npeers == 0) {
+    p.out[idx] = r;
+  } else {
+    for (int q = 0; q < p.npeers; ++q) p.peer_out[q][idx + p.col_off] = r;
+  }
 }
 
 // Finish 16 tokens (48 accumulator columns) of one weight row of a whole tile.
@@ -583,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Stage the tile's column scales (bn <= 256 floats, in the token-table
         // words) while the accumulator is still being computed.
         named_bar_sync(1, kEpiThreads);
-        if (p.out) {
+        if (p.out || p.npeers) {
           float* s_scale = reinterpret_cast<float*>(s_exp);
           for (int j = ethread; j < p.bn; j += kEpiThreads) {
             const int col = tn * p.bn + j;
@@ -814,6 +843,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tmem_dealloc(tmem_base, p.tmem_cols);
     if (trace && lane == 0) trace[7] = globaltimer();
+  }
+
+  // Row-sharded call: after this rank's last CTA has stored its outputs into
+  // every rank's C, every rank's inbox gets 1; the kernel ends when this rank's
+  // inbox holds all ranks' counts for this call (bounded wait). This follows
+  // the TMEM release, so the wait holds no tensor-core resources.
+  if (p.npeers > 0 && warp >= 2) {
+    fence_sc_sys();  // this thread's peer stores are visible before the counts below
+    named_bar_sync(1, kEpiThreads);
+    if (threadIdx.x == 64) {
+      const unsigned done = static_cast<unsigned>(atom_add_acq_rel_gpu(p.done_ctr, 1u)) + 1u;
+      if (done == gridDim.x) {
+        *p.done_ctr = 0u;  // ready for the next call
+        for (int q = 0; q < p.npeers; ++q) red_add_release_sys(p.peer_inbox[q], 1u);
+        const unsigned* own = p.peer_inbox[p.rank];
+        const unsigned long long t0 = globaltimer();
+        while (static_cast<int>(ld_acquire_sys(own) - p.inbox_target) < 0) {
+          if (globaltimer() - t0 > kPeerWaitLimitNs) {
+            atomicCAS(p.err, 0, kDevTimeoutPeers);
+            break;
+          }
+          __nanosleep(256);
+        }
+      }
+    }
   }
 }
 

@@ -85,6 +85,7 @@ struct Ctx {
   DevBuf small;     // exps | nonfinite | term_flags, each [M] int
   DevBuf slots;     // swap-mode split-tile accumulators (zeroed once, self-clearing)
   DevBuf counters;  // split-tile counters (zeroed once, self-resetting)
+  DevBuf shard_done;  // row-sharded calls: CTA completion counter (zeroed once, self-resetting)
   DevBuf sync;      // prep completion counter and term-flag OR (zeroed once, self-resetting)
   // bf16 normal mode: term planes and per-row dirty bits of their own (zeroed
   // whenever the layout changes), and two term-flag words used by alternate calls
@@ -120,6 +121,18 @@ struct Reg {
   int dev;
 };
 std::map<uintptr_t, Reg> g_reg;
+
+// Row-sharded calls: calls made so far on each rank's own inbox word.
+std::map<uintptr_t, unsigned> g_inbox_calls;
+
+// Peer buffers opened from IPC handles: one mapping per handle, shared by
+// every open of it, released when the last user closes.
+struct IpcMap {
+  void* base;
+  int refs;
+};
+std::map<std::string, IpcMap> g_ipc;            // handle bytes -> mapping
+std::map<uintptr_t, std::string> g_ipc_users;    // pointer handed out -> handle bytes
 
 int load_encoder() {
   if (g_encode) return VMLM_OK;
@@ -505,11 +518,77 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   return VMLM_OK;
 }
 
+// ------------------------------------------------------ row-sharded calls
+
+// One rank's part of a row-sharded call: its output columns start at col_off
+// in every rank's full C (row stride n_total); out[q] / inbox[q] are rank q's
+// C and inbox, mapped into this process.
+struct Shard {
+  int world = 0, rank = 0;
+  long long col_off = 0, n_total = 0;
+  float* out[kMaxPeers] = {};
+  unsigned* inbox[kMaxPeers] = {};
+  unsigned* done = nullptr;
+  unsigned target = 0;
+};
+
+void apply_shard(TcParams& p, const Shard& sh) {
+  p.npeers = sh.world;
+  p.rank = sh.rank;
+  p.col_off = sh.col_off;
+  p.ldo = sh.n_total;
+  bool vec = (sh.n_total % 4 == 0) && (sh.col_off % 4 == 0);
+  for (int q = 0; q < sh.world; ++q) {
+    p.peer_out[q] = sh.out[q];
+    p.peer_inbox[q] = sh.inbox[q];
+    vec = vec && aligned16(sh.out[q]);
+  }
+  p.vec_out = vec ? 1 : 0;
+  p.done_ctr = sh.done;
+  p.inbox_target = sh.target;
+  p.out = nullptr;
+}
+
+// Validate a row-sharded call and fill this rank's part. Rows are split in
+// ceil(n / world) blocks; every rank must get at least one.
+int shard_check(float* const* c_peers, unsigned* const* inbox_peers, int rank, int world, size_t m, size_t n) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(VMLM_ERR_ARG, "sharded call: rank %d of world %d (1 <= world <= %d)", rank, world, kMaxPeers);
+  if (!c_peers || !inbox_peers) return fail(VMLM_ERR_ARG, "sharded call: null peer list");
+  for (int q = 0; q < world; ++q)
+    if (!c_peers[q] || !inbox_peers[q]) return fail(VMLM_ERR_ARG, "sharded call: null pointer for rank %d", q);
+  if (m == 0 || n == 0) return fail(VMLM_ERR_SHAPE, "sharded call: m and n must be positive");
+  const size_t rows = (n + world - 1) / world;
+  if (rows * (world - 1) >= n) return fail(VMLM_ERR_SHAPE, "sharded call: n=%zu leaves a rank without rows", n);
+  return VMLM_OK;
+}
+
+int shard_setup(Ctx* ctx, float* const* c_peers, unsigned* const* inbox_peers, int rank, int world, size_t m,
+                size_t n, Shard* sh, size_t* nloc) {
+  VMLM_TRY(shard_check(c_peers, inbox_peers, rank, world, m, n));
+  const size_t rows = (n + world - 1) / world;
+  const size_t r0 = rows * rank;
+  *nloc = (r0 + rows < n ? r0 + rows : n) - r0;
+  VMLM_TRY(ensure(ctx->shard_done, 256, true));
+  sh->world = world;
+  sh->rank = rank;
+  sh->col_off = static_cast<long long>(r0);
+  sh->n_total = static_cast<long long>(n);
+  for (int q = 0; q < world; ++q) {
+    sh->out[q] = c_peers[q];
+    sh->inbox[q] = inbox_peers[q];
+  }
+  sh->done = static_cast<unsigned*>(ctx->shard_done.p);
+  const unsigned calls = ++g_inbox_calls[reinterpret_cast<uintptr_t>(inbox_peers[rank])];
+  sh->target = calls * static_cast<unsigned>(world);
+  return VMLM_OK;
+}
+
 // ------------------------------------------------------------- Q8 path
 
 int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
-           cudaStream_t st) {
-  if (K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q)) {
+           cudaStream_t st, const Shard* sh = nullptr) {
+  if (!sh && K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q)) {
     DecPlan dp;
     VMLM_TRY(plan_decode(c, M, N, K, &dp));
     if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp);
@@ -557,6 +636,7 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn));
+  if (sh) apply_shard(p, *sh);
   return run_tc<TcMode::kQ8Swap>(c, st, ma, mb, p, use_streamk(p, c->sms), true);
 }
 
@@ -666,7 +746,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
 // ---------------------------------------------------------- int8 x int8
 
 int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float* out, int32_t* acc, int M, int N,
-             int K, cudaStream_t st) {
+             int K, cudaStream_t st, const Shard* sh = nullptr) {
   const bool tc_ok = K > 0 && K % 16 == 0 && aligned16(x) && aligned16(w);
   if (!tc_ok) {
     const long long warps = static_cast<long long>(M) * N;
@@ -694,6 +774,7 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
+  if (sh) apply_shard(p, *sh);
   return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false, plan.split);
 }
 
@@ -777,8 +858,8 @@ int vmlm_shutdown(void) {
     Ctx* c = kv.second;
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
-    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->sync, &c->norm_terms, &c->norm_dirty,
-                      &c->norm_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
+    for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->shard_done, &c->sync, &c->norm_terms,
+                      &c->norm_dirty, &c->norm_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
@@ -973,6 +1054,112 @@ int vmlm_profile_take(double* gemm_ms, uint64_t* launches) {
   return VMLM_OK;
 }
 
+// ------------------------------------------------------------ row-sharded
+
+int vmlm_ipc_handle(const void* dptr, void* handle) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!dptr || !handle) return fail(VMLM_ERR_ARG, "ipc_handle: null pointer");
+  typedef CUresult (*RangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = nullptr;
+  if (!range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    VMLM_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) return fail(VMLM_ERR_CUDA, "cuMemGetAddressRange not available");
+    range = reinterpret_cast<RangeFn>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)) != CUDA_SUCCESS)
+    return fail(VMLM_ERR_ARG, "ipc_handle: %p is not device memory", dptr);
+  cudaIpcMemHandle_t h;
+  VMLM_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  const uint64_t off = reinterpret_cast<uint64_t>(dptr) - static_cast<uint64_t>(base);
+  std::memcpy(handle, &h, sizeof h);
+  std::memcpy(static_cast<char*>(handle) + sizeof h, &off, sizeof off);
+  return VMLM_OK;
+}
+
+int vmlm_ipc_open(const void* handle, void** dptr) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!handle || !dptr) return fail(VMLM_ERR_ARG, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  uint64_t off = 0;
+  std::memcpy(&h, handle, sizeof h);
+  std::memcpy(&off, static_cast<const char*>(handle) + sizeof h, sizeof off);
+  const std::string key(reinterpret_cast<const char*>(&h), sizeof h);
+  auto it = g_ipc.find(key);
+  if (it == g_ipc.end()) {
+    void* base = nullptr;
+    VMLM_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    it = g_ipc.emplace(key, IpcMap{base, 0}).first;
+  }
+  ++it->second.refs;
+  *dptr = static_cast<char*>(it->second.base) + off;
+  g_ipc_users[reinterpret_cast<uintptr_t>(*dptr)] = key;
+  return VMLM_OK;
+}
+
+int vmlm_ipc_close(void* dptr) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto u = g_ipc_users.find(reinterpret_cast<uintptr_t>(dptr));
+  if (u == g_ipc_users.end()) return fail(VMLM_ERR_ARG, "ipc_close: %p was not opened by vmlm_ipc_open", dptr);
+  auto it = g_ipc.find(u->second);
+  g_ipc_users.erase(u);
+  if (it != g_ipc.end() && --it->second.refs == 0) {
+    const cudaError_t e = cudaIpcCloseMemHandle(it->second.base);
+    g_ipc.erase(it);
+    if (e != cudaSuccess) return fail(VMLM_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  }
+  return VMLM_OK;
+}
+
+int vmlm_sharded_reset(unsigned* inbox) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!inbox) return fail(VMLM_ERR_ARG, "sharded_reset: null pointer");
+  VMLM_CUDA(cudaMemset(inbox, 0, sizeof(unsigned)));
+  g_inbox_calls.erase(reinterpret_cast<uintptr_t>(inbox));
+  return VMLM_OK;
+}
+
+int vmlm_sharded_gemm_nt_int8_dev(const float* a, const int8_t* q_shard, const float* scale_shard,
+                                  float* const* c_peers, unsigned* const* inbox_peers, int rank, int world, size_t m,
+                                  size_t n, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (!a || !q_shard || !scale_shard) return fail(VMLM_ERR_ARG, "sharded_gemm_nt_int8_dev: null pointer");
+  if (k == 0 || k % 16 != 0 || k > 131072 || !aligned16(q_shard))
+    return fail(VMLM_ERR_SHAPE, "sharded_gemm_nt_int8_dev: needs k %% 16 == 0, k <= 131072, 16-byte aligned q");
+  VMLM_TRY(shard_check(c_peers, inbox_peers, rank, world, m, n));
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  Shard sh;
+  size_t nloc = 0;
+  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, &sh, &nloc));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_q8(ctx, a, q_shard, scale_shard, nullptr, static_cast<int>(m), static_cast<int>(nloc),
+                static_cast<int>(k), st, &sh);
+}
+
+int vmlm_sharded_gemm_i8i8_dev(const int8_t* x, const int8_t* w_shard, const float* scale_shard,
+                               float* const* c_peers, unsigned* const* inbox_peers, int rank, int world, size_t m,
+                               size_t n, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (!x || !w_shard || !scale_shard) return fail(VMLM_ERR_ARG, "sharded_gemm_i8i8_dev: null pointer");
+  if (k == 0 || k % 16 != 0 || k > 131072 || !aligned16(x) || !aligned16(w_shard))
+    return fail(VMLM_ERR_SHAPE, "sharded_gemm_i8i8_dev: needs k %% 16 == 0, k <= 131072, 16-byte aligned x and w");
+  VMLM_TRY(shard_check(c_peers, inbox_peers, rank, world, m, n));
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  Shard sh;
+  size_t nloc = 0;
+  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, &sh, &nloc));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_i8i8(ctx, x, w_shard, scale_shard, nullptr, nullptr, static_cast<int>(m), static_cast<int>(nloc),
+                  static_cast<int>(k), st, &sh);
+}
+
 int vmlm_sync(void* stream) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   Ctx* ctx = nullptr;
@@ -986,6 +1173,7 @@ int vmlm_sync(void* stream) {
     if (ctx->counters.p) cudaMemset(ctx->counters.p, 0, ctx->counters.bytes);
     if (ctx->sync.p) cudaMemset(ctx->sync.p, 0, ctx->sync.bytes);
     if (ctx->slots.p) cudaMemset(ctx->slots.p, 0, ctx->slots.bytes);
+    if (ctx->shard_done.p) cudaMemset(ctx->shard_done.p, 0, ctx->shard_done.bytes);
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
   return VMLM_OK;

@@ -1,0 +1,157 @@
+"""GPU tests of the row-sharded entry points, whose GEMM epilogue stores every
+output into every rank's C (the all-gather fused into the kernel).
+
+One GPU: a single-rank group (the rank is its own only peer) against the
+oracle, twice in a row so the inbox count advances. Two or more GPUs: two
+processes, one per GPU, exchange IPC handles over gloo and must both end with
+the full result, equal to the single-GPU call on the whole weight."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TIGHT_Q8 = 2e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 20000, 2304), (64, 16384, 2304), (5, 300, 256)])
+def test_single_rank_sharded_q8_matches_oracle(kernels, oracle, m, n, k):
+    import torch
+    from sparrow_b200.sharded import PeerOutputs, sharded_gemm_nt_int8
+    x = oracle.fill_normal(m * k, 60 + m, 1.0).reshape(m, k)
+    q, s = oracle.quant_int8(oracle.fill_normal(n * k, 61 + m, 0.02).reshape(n, k))
+    ref = oracle.gemm_nt_int8(x, q, s, nt=os.cpu_count() or 1)
+    dx, dq, ds = torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    peers = PeerOutputs(m, n)
+    try:
+        for _ in range(2):
+            peers.c.fill_(float("nan"))
+            sharded_gemm_nt_int8(dx, dq, ds, peers, m, n, k, stream=torch.cuda.current_stream())
+            torch.cuda.synchronize()
+            kernels.sync()
+            err = oracle.max_rel_err(peers.c.cpu().numpy(), ref)
+            assert err <= TIGHT_Q8, err
+    finally:
+        peers.close()
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 1000, 512), (1024, 4096, 1024)])
+def test_single_rank_sharded_i8i8_bit_exact(kernels, oracle, m, n, k):
+    import torch
+    from sparrow_b200.sharded import PeerOutputs, sharded_gemm_i8i8
+    x = oracle.fill_int8(m * k, 70).reshape(m, k)
+    w = oracle.fill_int8(n * k, 71).reshape(n, k)
+    s = np.abs(oracle.fill_normal(n, 72, 0.02)) + np.float32(1e-3)
+    rc, _ = oracle.gemm_i8i8(x, w, s, nt=os.cpu_count() or 1)
+    peers = PeerOutputs(m, n)
+    try:
+        for _ in range(2):
+            peers.c.zero_()
+            sharded_gemm_i8i8(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(),
+                              peers, m, n, k, stream=torch.cuda.current_stream())
+            torch.cuda.synchronize()
+            kernels.sync()
+            assert np.array_equal(peers.c.cpu().numpy().view(np.uint32), rc.view(np.uint32))
+    finally:
+        peers.close()
+
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _two_gpu_rank(rank, world, port, errors):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    import sparrow_b200.kernels as K
+    from sparrow_b200.sharded import PeerOutputs, shard_rows, sharded_gemm_i8i8, sharded_gemm_nt_int8
+    K.init(rank)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        g = torch.Generator(device="cuda")
+        # Q8 LM-head shape, M = 1 and 64: full weight on every rank for the comparison
+        for m, n, k in ((1, 30011, 2304), (64, 16384, 2304)):
+            g.manual_seed(7 + m)
+            x = torch.randn((m, k), generator=g, device="cuda")
+            q = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+            s = torch.rand((n,), generator=g, device="cuda") * 0.01 + 1e-3
+            full = torch.empty((m, n), device="cuda")
+            st = torch.cuda.current_stream()
+            K.gemm_nt_int8_dev(x, q, s, full, m, n, k, stream=st)
+            r0, r1 = shard_rows(n, world, rank)
+            qs, ss = q[r0:r1].contiguous(), s[r0:r1].contiguous()
+            peers = PeerOutputs(m, n)
+            for _ in range(2):
+                peers.c.fill_(float("nan"))
+                torch.cuda.synchronize()  # no peer may write into C before it is reset
+                dist.barrier()
+                sharded_gemm_nt_int8(x, qs, ss, peers, m, n, k, stream=st)
+                torch.cuda.synchronize()
+                K.sync()
+                got = peers.c.cpu().numpy()
+                ref = full.cpu().numpy()
+                err = float(np.abs(got - ref).max() / np.abs(ref).max())
+                if not err <= TIGHT_Q8:
+                    errors.put(f"rank {rank} q8 {m}x{n}: max rel err {err}")
+            dist.barrier()
+            peers.close()
+            dist.barrier()
+        # int8 x int8 FFN shape (smaller), bit-exact
+        m, n, k = 512, 8192, 1024
+        g.manual_seed(99)
+        x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
+        w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+        s = torch.rand((n,), generator=g, device="cuda") * 0.01 + 1e-3
+        full = torch.empty((m, n), device="cuda")
+        st = torch.cuda.current_stream()
+        K.gemm_i8i8_dev(x, w, s, full, None, m, n, k, stream=st)
+        r0, r1 = shard_rows(n, world, rank)
+        ws, ss = w[r0:r1].contiguous(), s[r0:r1].contiguous()
+        peers = PeerOutputs(m, n)
+        torch.cuda.synchronize()
+        dist.barrier()
+        sharded_gemm_i8i8(x, ws, ss, peers, m, n, k, stream=st)
+        torch.cuda.synchronize()
+        K.sync()
+        if not torch.equal(peers.c.view(torch.int32), full.view(torch.int32)):
+            errors.put(f"rank {rank} i8i8: results differ")
+        dist.barrier()
+        peers.close()
+        dist.barrier()
+    except Exception as e:  # reported to the parent, which fails the test
+        errors.put(f"rank {rank}: {type(e).__name__}: {e}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_gpu_sharded_calls_give_every_rank_the_whole_result():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    errors = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_gpu_rank, args=(r, 2, port, errors)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join(timeout=10)
+    msgs = []
+    while not errors.empty():
+        msgs.append(errors.get())
+    assert all(p.exitcode == 0 for p in procs), msgs
+    assert not msgs, msgs
