@@ -371,6 +371,7 @@ def cpu_baseline_c2(x_dev, w_dev, budget_s):
 def bench_configs(K, dist, rank, world, flush, pk):
     """Per-configuration device times: C1, C3, C4, C5, and C2 with general f32 X."""
     import torch
+    from sparrow_b200.sharded import PeerOutputs, sharded_gemm_i8i8, sharded_gemm_nt_int8
     st = torch.cuda.current_stream()
     res = {}
     hbm = pk["hbm_gbs"]
@@ -433,6 +434,17 @@ def bench_configs(K, dist, rank, world, flush, pk):
                 dist.all_gather_into_tensor(gathered, c)
             tag = time_steps(step_ag, 20, 3, flush, dist)
             entry.update({"step_allgather_us": tag * 1e3, "GBps_with_allgather": nbytes / tag / 1e6})
+            # the same call through the sharded entry point: the all-gather is in the GEMM epilogue
+            peers = PeerOutputs(m, n4)
+
+            def step_fused():
+                sharded_gemm_nt_int8(x, q4, s4, peers, m, n4, k4, stream=st)
+            tf = time_steps(step_fused, 20, 3, flush, dist)
+            entry.update({"step_fused_allgather_us": tf * 1e3, "GBps_fused_allgather": nbytes / tf / 1e6})
+            torch.cuda.synchronize()
+            dist.barrier()
+            peers.close()
+            dist.barrier()
         res[f"C4_q8_lm_head_M{m}"] = entry
     del q4, s4
     # C5: int8 x int8 FFN, W rows sharded, all-gather of the output slices
@@ -461,6 +473,16 @@ def bench_configs(K, dist, rank, world, flush, pk):
             dist.all_gather_into_tensor(gathered, c5)
         tag = time_steps(step_ag, 5, 2, flush, dist)
         entry.update({"step_allgather_us": tag * 1e3, "TOPS_with_allgather": ops / tag / 1e9})
+        peers = PeerOutputs(m5, n5)
+
+        def step_fused():
+            sharded_gemm_i8i8(x5, w5, s5, peers, m5, n5, k5, stream=st)
+        tf = time_steps(step_fused, 5, 2, flush, dist)
+        entry.update({"step_fused_allgather_us": tf * 1e3, "TOPS_fused_allgather": ops / tf / 1e9})
+        torch.cuda.synchronize()
+        dist.barrier()
+        peers.close()
+        dist.barrier()
     res["C5_i8i8_ffn_4096x28672x8192"] = entry
     del x5, w5, c5
     # C2 shape with activations that are not bf16 values (three split terms active)
