@@ -111,13 +111,11 @@ __device__ __forceinline__ void dec_load_batch(const DecParams& p, float4 (&keep
   }
 }
 
-// Exact f32 recompute of one output of a token that holds NaN or Inf.
-__device__ float dec_nonfinite_dot(const DecParams& p, int t, int n) {
-  const float* xr = p.x + static_cast<long long>(t) * p.ldx;
-  const int8_t* wr = p.w + static_cast<long long>(n) * p.k;
-  float s = 0.f;
-  for (int kk = 0; kk < p.k; ++kk) s = __fadd_rn(s, __fmul_rn(xr[kk], static_cast<float>(wr[kk])));
-  return __fmul_rn(s, __ldg(p.scale + n));
+// Exact f32 recompute of one output of a token that holds NaN or Inf (out of
+// line: see nonfinite_dot_q8).
+__device__ __forceinline__ float dec_nonfinite_dot(const DecParams& p, int t, int n) {
+  return nonfinite_dot_q8(p.x + static_cast<long long>(t) * p.ldx, p.w + static_cast<long long>(n) * p.k, p.k,
+                          __ldg(p.scale + n));
 }
 
 __global__ void __launch_bounds__(kDecThreads, 1)

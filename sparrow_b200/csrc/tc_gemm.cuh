@@ -267,20 +267,35 @@ __device__ __forceinline__ void epi_norm16(const TcParams& p, int row0, int col0
 // Exact f32 recompute of one output for a token whose activations hold NaN or
 // Inf (the digit-plane / split-term encodings cannot carry them). Summation is
 // sequential, which gives the same NaN/Inf classification as any order.
-template <TcMode MODE>
-__device__ float nonfinite_dot(const TcParams& p, int t, int n) {
-  const float* xr = p.x + static_cast<long long>(t) * p.ldx;
+// Cold paths of the epilogue stay out of line (plain arguments, no parameter
+// struct), so the unrolled hot loops that call them stay small in the
+// instruction cache.
+__device__ __noinline__ float nonfinite_dot_q8(const float* xr, const int8_t* wr, int k, float sc) {
   float s = 0.f;
-  if constexpr (MODE == TcMode::kQ8Swap) {
-    const int8_t* wr = static_cast<const int8_t*>(p.w) + static_cast<long long>(n) * p.k;
-    for (int kk = 0; kk < p.k; ++kk) s = __fadd_rn(s, __fmul_rn(xr[kk], static_cast<float>(wr[kk])));
-    return __fmul_rn(s, __ldg(p.scale + n));
-  } else {
-    const uint16_t* wr = static_cast<const uint16_t*>(p.w) + static_cast<long long>(n) * p.k;
-    for (int kk = 0; kk < p.k; ++kk)
-      s = __fadd_rn(s, __fmul_rn(xr[kk], __uint_as_float(static_cast<uint32_t>(wr[kk]) << 16)));
-    return s;
-  }
+  for (int kk = 0; kk < k; ++kk) s = __fadd_rn(s, __fmul_rn(xr[kk], static_cast<float>(wr[kk])));
+  return __fmul_rn(s, sc);
+}
+
+__device__ __noinline__ float nonfinite_dot_bf16(const float* xr, const uint16_t* wr, int k) {
+  float s = 0.f;
+  for (int kk = 0; kk < k; ++kk)
+    s = __fadd_rn(s, __fmul_rn(xr[kk], __uint_as_float(static_cast<uint32_t>(wr[kk]) << 16)));
+  return s;
+}
+
+// f32(v * 2^-e) * sc for exponents outside the single-precision fast path.
+__device__ __noinline__ float q8_scale_wide(long long v, int e, float sc) {
+  return __fmul_rn(__double2float_rn(ldexp(static_cast<double>(v), -e)), sc);
+}
+
+template <TcMode MODE>
+__device__ __forceinline__ float nonfinite_dot(const TcParams& p, int t, int n) {
+  const float* xr = p.x + static_cast<long long>(t) * p.ldx;
+  if constexpr (MODE == TcMode::kQ8Swap)
+    return nonfinite_dot_q8(xr, static_cast<const int8_t*>(p.w) + static_cast<long long>(n) * p.k, p.k,
+                            __ldg(p.scale + n));
+  else
+    return nonfinite_dot_bf16(xr, static_cast<const uint16_t*>(p.w) + static_cast<long long>(n) * p.k, p.k);
 }
 
 // Swap modes combine one token's three accumulator columns (token-major
@@ -319,7 +334,7 @@ __device__ __forceinline__ void swap_finish(const TcParams& p, int n, int t, int
     if (e >= -70 && e <= 100) {
       r = __fmul_rn(__fmul_rn(__ll2float_rn(v), __int_as_float((127 - e) << 23)), sc);
     } else {
-      r = __fmul_rn(__double2float_rn(ldexp(static_cast<double>(v), -e)), sc);
+      r = q8_scale_wide(v, e, sc);
     }
   } else {
     r = val;
@@ -646,12 +661,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int c = ci * kChunk;
             uint32_t v[48];
             __syncwarp();
+            const unsigned long long tl0 = trace ? globaltimer() : 0;
             tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
             tmem_ld16(tbase + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
             tmem_ld16(tbase + c + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
             tmem_ld_wait();
+            const unsigned long long tl1 = trace ? globaltimer() : 0;
             if (ci == my_last) release_accum();
             epi_swap48<MODE>(p, grow, tok0, c / 3, scale_n, s_exp, s_bad, v);
+            if (trace) {
+              epi_pub += tl1 - tl0;
+              epi_cnt += globaltimer() - tl1;
+            }
           }
         } else {
           for (int ci = half; ci < nch; ci += 2) {
