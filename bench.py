@@ -98,7 +98,8 @@ def parse():
 CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf16f", M2, N2, K2),
          "c3q_m8": ("q8", 8, 2304, 2304), "c4m1": ("q8", 1, 122753, 2304), "c4m64": ("q8", 64, 122753, 2304),
          "c5": ("i8", 4096, 28672, 8192), "c5small": ("i8", 1024, 4096, 8192),
-         "c4m64small": ("q8", 64, 16384, 2304)}
+         "c4m64small": ("q8", 64, 16384, 2304), "c3q_m32": ("q8", 32, 2304, 2304), "c3d_m32": ("q8", 32, 2304, 5760),
+         "c3g_m32": ("q8", 32, 5760, 2304)}
 
 
 def run_case(args):

@@ -44,6 +44,7 @@ constexpr int kDecMaxTok = 32;
 constexpr int kDecMaxCluster = 8;
 constexpr int kDecStageBytes = kTileRows * kBlockBytes;  // one 128 x 128 int8 W box
 constexpr int kDecRegChunks = 8;                         // x float4 chunks per thread kept in registers
+constexpr int kDecGroup = 4;                              // chunks per thread per rolled step of the digit pass
 
 struct DecParams {
   int n, k, m;
@@ -292,35 +293,52 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       s_exp[et] = e;
     }
     named_bar_sync(1, kDecEpiThreads);
-    // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte rows)
+    // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte
+    // rows), in groups of kDecGroup chunks per thread: taken from the kept
+    // batch when the range fits it, else loaded again (L2 hits) with the
+    // group's loads in flight together. The loop stays rolled: its body is
+    // the hot code of this phase and must stay small in the instruction cache.
     uint8_t* planes = smem + L.b_off;
-    for (int s = 0; s < nsteps; ++s) {
-      const int qi = et + s * kDecEpiThreads;
-      if (qi >= nq) break;
-      const int t = qi / qpt;
-      const int kk = (qi - t * qpt) * 4;  // offset in this CTA's range
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (kept) {
-        #pragma unroll
-        for (int r = 0; r < kDecRegChunks; ++r)
-          if (r == s) v = keep[r];
-      } else if (k_lo + kk < p.k) {
-        v = dec_load4(p.x + static_cast<long long>(t) * p.ldx + k_lo + kk, vec);
-      }
-      if (s_bad[t]) v = make_float4(0.f, 0.f, 0.f, 0.f);
-      const int e = s_exp[t];
-      int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
-      q8_digits(v.x, e, a0, a1, a2);
-      q8_digits(v.y, e, b0, b1, b2);
-      q8_digits(v.z, e, c0, c1, c2);
-      q8_digits(v.w, e, f0, f1, f2);
-      const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
-      const int j = kk >> 7, b = kk & 127;
-      uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+    #pragma unroll 1
+    for (int s0 = 0; s0 < nsteps; s0 += kDecGroup) {
+      float4 g[kDecGroup];
       #pragma unroll
-      for (int pl = 0; pl < 3; ++pl) {
-        const int r = 3 * t + pl;
-        *reinterpret_cast<uint32_t*>(blk + r * kBlockBytes + ((((b >> 4) ^ (r & 7)) << 4) | (b & 15))) = w3[pl];
+      for (int i = 0; i < kDecGroup; ++i) {
+        const int s = s0 + i;
+        const int qi = et + s * kDecEpiThreads;
+        g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kept) {
+          #pragma unroll
+          for (int r = 0; r < kDecRegChunks; ++r)
+            if (r == s) g[i] = keep[r];
+        } else if (s < nsteps && qi < nq) {
+          const int t = qi / qpt;
+          const int k = k_lo + (qi - t * qpt) * 4;
+          if (k < p.k) g[i] = dec_load4(p.x + static_cast<long long>(t) * p.ldx + k, vec);
+        }
+      }
+      #pragma unroll
+      for (int i = 0; i < kDecGroup; ++i) {
+        const int qi = et + (s0 + i) * kDecEpiThreads;
+        if (s0 + i >= nsteps || qi >= nq) break;
+        const int t = qi / qpt;
+        const int kk = (qi - t * qpt) * 4;  // offset in this CTA's range
+        const float4 v = s_bad[t] ? make_float4(0.f, 0.f, 0.f, 0.f) : g[i];
+        const int e = s_exp[t];
+        int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
+        q8_digits(v.x, e, a0, a1, a2);
+        q8_digits(v.y, e, b0, b1, b2);
+        q8_digits(v.z, e, c0, c1, c2);
+        q8_digits(v.w, e, f0, f1, f2);
+        const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
+        const int j = kk >> 7, b = kk & 127;
+        uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+        #pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+          const int row = 3 * t + pl;
+          *reinterpret_cast<uint32_t*>(blk + row * kBlockBytes + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))) =
+              w3[pl];
+        }
       }
     }
     fence_proxy_async_smem();

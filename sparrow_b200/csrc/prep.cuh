@@ -65,10 +65,14 @@ __device__ __forceinline__ int block_or(int v, int* red) {
   return warp_or(v);
 }
 
+// x * 2^e for exponents outside the normal range of a single 2^e factor (out
+// of line, so the callers' unrolled loops stay small).
+__device__ __noinline__ float scale_pow2_wide(float x, int e) { return scalbnf(x, e); }
+
 // x * 2^e exactly (power-of-two scaling), for any e the encoder produces.
 __device__ __forceinline__ float scale_pow2(float x, int e) {
   if (e >= -126 && e <= 127) return __fmul_rn(x, __int_as_float((127 + e) << 23));
-  return scalbnf(x, e);
+  return scale_pow2_wide(x, e);
 }
 
 __device__ __forceinline__ void q8_digits(float x, int e, int& d0, int& d1, int& d2) {
