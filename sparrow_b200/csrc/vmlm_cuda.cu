@@ -16,6 +16,7 @@
 #include "../../include/vmlm_cuda.h"
 #include "prep.cuh"
 #include "decode.cuh"
+#include "tc2_gemm.cuh"
 #include "tc_gemm.cuh"
 
 using namespace vmlm;
@@ -180,6 +181,10 @@ int get_ctx(int dev, Ctx** out) {
   VMLM_TRY(set_smem_attr<TcMode::kBf16Swap>());
   VMLM_TRY(set_smem_attr<TcMode::kBf16Norm>());
   VMLM_TRY(set_smem_attr<TcMode::kI8Norm>());
+  VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kI8Norm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMaxSmem));
+  VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kBf16Norm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
@@ -416,6 +421,74 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   VMLM_TRY(prof_begin(c, st, &pp));
   VMLM_TRY(launch_ex(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false,
                      cluster, ma, mb, p));
+  return prof_end(st, pp);
+}
+
+// Large prefill GEMMs on CTA pairs (tc2_gemm_kernel): 256 x 256 tiles, one
+// pair per cluster, persistent. Taken when there is at least about one pair
+// tile per co-resident pair and no K split is planned.
+constexpr int kPairBn = 256;
+
+template <TcMode MODE>
+int tc2_max_pairs(Ctx* ctx, uint32_t smem, int* out) {
+  const auto key = std::make_pair(2000 + static_cast<int>(MODE), smem);
+  auto it = ctx->dec_clusters.find(key);
+  if (it != ctx->dec_clusters.end()) {
+    *out = it->second;
+    return VMLM_OK;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * ctx->sms));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  VMLM_CUDA(cudaOccupancyMaxActiveClusters(&n, tc2_gemm_kernel<MODE>, &cfg));
+  ctx->dec_clusters[key] = n;
+  *out = n;
+  return VMLM_OK;
+}
+
+int tc2_stages() {
+  int stages = 16;
+  while (stages >= 2 && tc2_smem_layout(stages, kPairBn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  return stages;
+}
+
+bool use_pairs(const NormPlan& plan, long long rows, long long cols, int sms) {
+  const long long pair_tiles = cdiv(rows, 2 * kTileRows) * cdiv(cols, kPairBn);
+  return plan.split == 1 && rows >= 2 * kTileRows && pair_tiles * 5 >= static_cast<long long>(sms) * 2;
+}
+
+// p: a normal-mode parameter set whose tiles_m / bn / maps the caller fills for
+// pair tiles (A box 128 rows, B box kPairBn / 2 rows).
+template <TcMode MODE>
+int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool pdl) {
+  p.stages = tc2_stages();
+  p.tmem_cols = pow2_at_least(2 * p.bn);
+  p.csplit = 0;
+  p.streamk = 0;
+  const Tc2Smem L = tc2_smem_layout(p.stages, p.bn);
+  int max_pairs = 0;
+  VMLM_TRY(tc2_max_pairs<MODE>(c, L.total, &max_pairs));
+  if (max_pairs < 1) return fail(VMLM_ERR_CUDA, "no CTA pair fits on this device");
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long pairs = tiles < max_pairs ? tiles : max_pairs;
+  p.err = c->err;
+  p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(2 * pairs) <= g_trace_ctas) ? g_trace : nullptr;
+  if (!g_profile)
+    return launch_ex(tc2_gemm_kernel<MODE>, dim3(static_cast<unsigned>(2 * pairs)), dim3(kThreads), L.total, st, pdl,
+                     2, ma, mb, p);
+  ProfPair pp;
+  VMLM_TRY(prof_begin(c, st, &pp));
+  VMLM_TRY(launch_ex(tc2_gemm_kernel<MODE>, dim3(static_cast<unsigned>(2 * pairs)), dim3(kThreads), L.total, st,
+                     false, 2, ma, mb, p));
   return prof_end(st, pp);
 }
 
@@ -690,6 +763,13 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   p.k = K;
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
+  if (use_pairs(plan, M, N, c->sms)) {
+    p.bn = kPairBn;
+    p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
+    p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, kPairBn / 2));
+    return run_tc2<TcMode::kBf16Norm>(c, st, ma, mb, p, true);
+  }
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
   return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true, plan.split);
 }
@@ -773,6 +853,14 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   p.n_tokens = M;
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, kTileRows));
+  if (use_pairs(plan, M, N, c->sms)) {
+    p.bn = kPairBn;
+    p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
+    p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, kPairBn / 2));
+    if (sh) apply_shard(p, *sh);
+    return run_tc2<TcMode::kI8Norm>(c, st, ma, mb, p, false);
+  }
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
   if (sh) apply_shard(p, *sh);
   return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false, plan.split);

@@ -369,3 +369,23 @@ def test_device_entry_points_match_host_ones(kernels, oracle):
     kernels.sync(st)
     # bf16 tiles split between CTAs are summed with f32 atomics: equal up to the last bits
     assert oracle.max_rel_err(dcb.cpu().numpy(), hb) <= 1e-6
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 4096, 1024), (1000, 3000, 520), (4096, 2048, 4096)])
+def test_i8i8_cta_pairs_bit_exact(kernels, oracle, m, n, k):
+    # shapes large enough for the CTA-pair kernel (256-row tiles over two SMs)
+    x = oracle.fill_int8(m * k, 80).reshape(m, k)
+    w = oracle.fill_int8(n * k, 81).reshape(n, k)
+    s = np.abs(oracle.fill_normal(n, 82, 0.02)) + np.float32(1e-3)
+    c = np.empty((m, n), np.float32)
+    acc = np.empty((m, n), np.int32)
+    kernels.gemm_i8i8(x, w, s, c, acc, m, n, k)
+    rc, ra = oracle.gemm_i8i8(x, w, s, nt=NT)
+    assert np.array_equal(acc, ra)
+    assert np.array_equal(c.view(np.uint32), rc.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k,exact", [(2048, 3072, 1024, True), (1536, 2304, 768, False)])
+def test_bf16_cta_pairs(kernels, oracle, m, n, k, exact):
+    x, w = bf16_case(oracle, m, n, k, seed=83, exact_x=exact)
+    check_bf16(kernels, oracle, x, w)
