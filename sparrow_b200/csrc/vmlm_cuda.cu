@@ -501,8 +501,9 @@ int check_dims(size_t m, size_t n, size_t k) {
 // ------------------------------------------------------- Q8 decode path
 
 // Cluster size and stage ring for the decode kernel, or c == 0 when the call
-// does not fit it (more than 32 tokens, or more tiles than one wave of
-// clusters: the persistent kernel streams those better).
+// does not fit it (more than 32 tokens, an x slice per CTA larger than one
+// register batch, or more tiles than one wave of clusters: the persistent
+// kernel streams those better).
 struct DecPlan {
   int c = 0;
   int stages = 0;
@@ -544,6 +545,12 @@ int plan_decode(Ctx* ctx, int M, int N, int K, DecPlan* plan) {
   long long best_ctas = 0;
   for (int c = 1; c <= kDecMaxCluster && c <= kb; ++c) {
     const int kbr = static_cast<int>(cdiv(kb, c));
+    // A CTA's x slice must fit one register batch of the plane warps: a
+    // second batch and the reloads of the digit pass queue behind the weight
+    // stream (at M = 32 the persistent swap-mode GEMM is then faster).
+    // (float4 chunks of x per k-block: kBlockBytes / 4)
+    if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
+      continue;
     int stages = kbr < 16 ? kbr : 16;
     while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
     if (stages < 1 || (stages < 2 && kbr > 1)) continue;

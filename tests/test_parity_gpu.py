@@ -146,10 +146,14 @@ def test_q8_zero_rows_and_extreme_scales(kernels, oracle):
 
 
 @pytest.mark.parametrize("m,n,k", [(32, 2304, 2304), (17, 5760, 2304), (16, 2304, 5760), (5, 640, 2304),
-                                   (2, 130, 1040), (1, 18944, 512), (9, 1, 128)])
+                                   (2, 130, 1040), (1, 18944, 512), (9, 1, 128), (8, 2304, 5760),
+                                   (21, 2304, 2304), (16, 2304, 2304)])
 def test_q8_decode_cluster_shapes(kernels, oracle, m, n, k):
     # decode kernel: K split over a cluster of CTAs, partial k-blocks, both
-    # token halves of the accumulator, a single row
+    # token halves of the accumulator, a single row; x slices of exactly one
+    # register batch (8 x 2304 x 5760: 8 tokens x 8 k-blocks per CTA) and just
+    # under it (21 x 3); the first three shapes exceed it and take the
+    # persistent swap-mode GEMM
     x, q, s = q8_case(oracle, m, n, k, seed=m * 7 + k)
     check_q8(kernels, oracle, x, q, s)
 
