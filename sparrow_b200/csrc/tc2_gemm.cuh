@@ -1,13 +1,15 @@
 // tc2_gemm.cuh -- the prefill GEMM on CTA pairs (tcgen05 cta_group::2).
 //
-// For large normal-mode GEMMs (kI8Norm, kBf16Norm): C[rows, cols] = A . B^T
-// with A the activations and B the weight rows. A cluster of two CTAs owns a
-// 256 x bn tile: CTA r holds A rows [256*tm + 128*r, +128) and B rows
+// For large normal-mode GEMMs (kI8Norm, kBf16Norm: A the activations, B the
+// weight rows) and for Q8 calls with many weight tiles (kQ8Swap: A the weight
+// rows, B the activation digit planes): C = A . B^T. A cluster of two CTAs
+// owns a 256 x bn tile: CTA r holds A rows [256*tm + 128*r, +128) and B rows
 // [bn*tn + (bn/2)*r, +bn/2) in its own shared memory (same offsets in both),
 // and its 128 accumulator rows x bn columns in its own TMEM (same address).
 // The even CTA issues tcgen05.mma.cta_group::2 with M = 256, N = bn. Per MAC
-// each SM loads 1.5x fewer operand bytes than a 128 x bn tile on one SM,
-// which is what bounds these GEMMs (per-SM L2 -> SM bandwidth).
+// each SM loads fewer operand bytes than a 128 x bn tile on one SM (B is
+// split between the two), which is what bounds these GEMMs (per-SM L2 -> SM
+// bandwidth; in swap mode the planes are re-read for every weight tile).
 //
 // Warp roles as in tc_gemm_kernel (320 threads). Barriers:
 //   full[s]   even CTA only: its producer expects both CTAs' bytes; both CTAs'
@@ -45,7 +47,8 @@ __host__ __device__ inline Tc2Smem tc2_smem_layout(int stages, int bn) {
   s.bar_off = s.b_off + stages * s.b_bytes;
   // full[stages], empty[stages], tfull[2], tempty[2], drain, done, then 64 bytes of words
   s.meta_off = s.bar_off + (2 * stages + 6) * 8 + 64;
-  // column scales of a tile (bn <= 256 floats)
+  // column scales of a tile (bn <= 256 floats), or in swap mode the tile's
+  // token exponents and flags (2 x 128 words)
   s.stg_off = s.meta_off + 256 * 4;
   s.total = s.stg_off + kEpiWarps * 32 * 17 * 4 + 1024;
   return s;
@@ -55,8 +58,10 @@ template <TcMode MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const TcParams p) {
-  static_assert(MODE == TcMode::kI8Norm || MODE == TcMode::kBf16Norm, "normal modes only");
-  constexpr bool kInt = (MODE == TcMode::kI8Norm);
+  static_assert(MODE == TcMode::kI8Norm || MODE == TcMode::kBf16Norm || MODE == TcMode::kQ8Swap,
+                "kI8Norm, kBf16Norm, kQ8Swap");
+  constexpr bool kInt = (MODE == TcMode::kI8Norm || MODE == TcMode::kQ8Swap);
+  constexpr bool kSwap = (MODE == TcMode::kQ8Swap);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -70,6 +75,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_scale = reinterpret_cast<float*>(smem + L.meta_off);
+  int* s_exp = reinterpret_cast<int*>(s_scale);  // swap mode: tokens of a tile (<= 80)
+  int* s_bad = s_exp + 128;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -109,29 +116,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tempty_even = mapa_shared(smem_u32(tempty_bar), 0);
   const int kbt = p.kb_per_term;
 
+  // Tile i of this pair (round-robin over pairs): this CTA's 128 rows of A
+  // start at a_row; tn is the column tile. Both CTAs see the same sequence.
+  auto tile_of = [&](int i, int& a_row, int& tn) -> bool {
+    const int tile = pair + i * npairs;
+    if (tile >= tiles) return false;
+    tn = tile / p.tiles_m;
+    a_row = (tile % p.tiles_m) * kPairRows + static_cast<int>(crank) * kTileRows;
+    return true;
+  };
+
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_first();
+      // weights stream once (evict first), activations are re-read by every tile
+      const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
+      uint32_t issued_mask = 0, last_phase = 0;
+      unsigned long long wait_empty = 0;  // trace: time waiting for free stages
+      // (issuing the weight half of the first stages before this wait, as the
+      // one-CTA kernel does, delays the previous kernel in the stream here)
       pdl_wait_prior();
       const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_mask = 0, last_phase = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < tiles; tile += npairs) {
-        const int tm = tile % p.tiles_m;
-        const int tn = tile / p.tiles_m;
-        const int a_row = tm * kPairRows + static_cast<int>(crank) * kTileRows;
+      int a_row, tn;
+      for (int i = 0; ok && tile_of(i, a_row, tn); ++i) {
         const int b_row = tn * p.bn + static_cast<int>(crank) * (p.bn / 2);
         for (int j = 0; j < T * kbt; ++j) {
           const int term = j / kbt;
           const int kin = j - term * kbt;
+          const unsigned long long tw = trace ? globaltimer() : 0;
           if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
+          if (trace) wait_empty += globaltimer() - tw;
           if (crank == 0) mbar_arrive_expect_tx(full_bar + stage, 2 * (L.a_bytes + L.b_bytes));
           const int kbx = kin * p.a_box_elems;
           const uint32_t fb = full_even + stage * 8;
@@ -145,7 +166,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (trace) trace[2] = globaltimer();
+      if (trace) {
+        trace[2] = globaltimer();
+        trace[8] = wait_empty;
+      }
       if (*abort_flag && crank == 0) {
         // The even CTA's full barriers count both CTAs' copies: once they are
         // complete, no copy of either CTA is in flight.
@@ -163,17 +187,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued = false;
-      int i = 0;
-      for (int tile = pair; ok && tile < tiles; tile += npairs, ++i) {
+      unsigned long long wait_accum = 0, wait_full = 0;  // trace: time waiting for TMEM / for stages
+      int a_row, tn;
+      for (int i = 0; ok && tile_of(i, a_row, tn); ++i) {
         const int buf = i & 1;
+        const unsigned long long tw0 = trace ? globaltimer() : 0;
         if (!mbar_wait(tempty_bar + buf, ((i >> 1) & 1) ^ 1, p.err, abort_flag, kDevTimeoutAccumFree)) break;
+        if (trace) wait_accum += globaltimer() - tw0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
         for (int j = 0; j < T * kbt; ++j) {
+          const unsigned long long tw1 = trace ? globaltimer() : 0;
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
             break;
           }
+          if (trace) wait_full += globaltimer() - tw1;
           tc_fence_after();
           if (trace && !issued) trace[3] = globaltimer();
           const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
@@ -198,7 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         umma_commit_pair(tfull_bar + buf);
       }
-      if (trace) trace[4] = globaltimer();
+      if (trace) {
+        trace[4] = globaltimer();
+        trace[9] = wait_full;
+        trace[10] = wait_accum;
+      }
       if (issued && *abort_flag) {
         umma_commit_pair(drain_bar);
         mbar_wait(drain_bar, 0, nullptr, abort_flag, kDevTimeoutDrain, false);
@@ -211,13 +244,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const int ethread = threadIdx.x - 64;
     pdl_wait_prior();
-    int i = 0;
-    for (int tile = pair; tile < tiles; tile += npairs, ++i) {
+    unsigned long long epi_wait = 0;  // trace: time waiting for accumulators
+    unsigned long long epi_ld = 0, epi_fin = 0;  // trace: time in TMEM loads / finishing and storing
+    int a_row, tn;
+    for (int i = 0; tile_of(i, a_row, tn); ++i) {
       const int buf = i & 1;
-      const int tm = tile % p.tiles_m;
-      const int tn = tile / p.tiles_m;
-      const int grow = tm * kPairRows + static_cast<int>(crank) * kTileRows + row;
-      if constexpr (MODE == TcMode::kI8Norm) {
+      const int grow = a_row + row;
+      float scale_n = 0.f;
+      if constexpr (kSwap) {
+        // the tile's per-token exponents and flags, and this row's scale
+        named_bar_sync(1, kEpiThreads);
+        if (ethread < p.tok_per_tile) {
+          const int t = tn * p.tok_per_tile + ethread;
+          s_exp[ethread] = t < p.n_tokens ? __ldg(p.exps + t) : 0;
+          s_bad[ethread] = t < p.n_tokens ? __ldg(p.nonfinite + t) : 0;
+        }
+        if (grow < p.n_out) scale_n = __ldg(p.scale + grow);
+        named_bar_sync(1, kEpiThreads);
+      } else if constexpr (MODE == TcMode::kI8Norm) {
         // column scales of the tile, staged while the accumulator is computed
         named_bar_sync(1, kEpiThreads);
         if (p.out || p.npeers)
@@ -227,18 +271,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         named_bar_sync(1, kEpiThreads);
       }
+      const unsigned long long tw = trace ? globaltimer() : 0;
       if (!mbar_wait(tfull_bar + buf, (i >> 1) & 1, p.err, abort_flag, kDevTimeoutAccum, false)) break;
+      if (trace) epi_wait += globaltimer() - tw;
       tc_fence_after();
       if (trace && ethread == 0 && i == 0) trace[5] = globaltimer();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * p.bn;
-      const int nch = p.bn / 16;
-      for (int ci = half; ci < nch; ci += 2) {
-        const int c = ci * 16;
-        uint32_t v[16];
-        __syncwarp();
-        tmem_ld16(tbase + c, v);
-        tmem_ld_wait();
-        epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, s_scale + c);
+      if constexpr (kSwap) {
+        // 48 columns = 16 tokens per chunk
+        const int nch = p.bn / 48;
+        for (int ci = half; ci < nch; ci += 2) {
+          const int c = ci * 48;
+          uint32_t v[48];
+          __syncwarp();
+          const unsigned long long tl0 = trace ? globaltimer() : 0;
+          tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(v));
+          tmem_ld16(tbase + c + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+          tmem_ld16(tbase + c + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
+          tmem_ld_wait();
+          const unsigned long long tl1 = trace ? globaltimer() : 0;
+          epi_swap48<MODE>(p, grow, tn * p.tok_per_tile, c / 3, scale_n, s_exp, s_bad, v);
+          if (trace) {
+            epi_ld += tl1 - tl0;
+            epi_fin += globaltimer() - tl1;
+          }
+        }
+      } else {
+        const int nch = p.bn / 16;
+        for (int ci = half; ci < nch; ci += 2) {
+          const int c = ci * 16;
+          uint32_t v[16];
+          __syncwarp();
+          tmem_ld16(tbase + c, v);
+          tmem_ld_wait();
+          epi_norm16<MODE>(p, grow - lane, tn * p.bn + c, v, s_stage, s_scale + c);
+        }
       }
       // this warp has read the accumulator: the even CTA's MMA may reuse it
       tc_fence_before();
@@ -250,7 +317,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_remote(tempty_even + buf * 8);
       }
     }
-    if (trace && threadIdx.x == 64) trace[6] = globaltimer();
+    if (trace && threadIdx.x == 64) {
+      trace[6] = globaltimer();
+      trace[11] = epi_wait;
+      trace[12] = epi_ld;
+      trace[13] = epi_fin;
+    }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(done_bar);

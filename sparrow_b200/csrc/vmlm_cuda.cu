@@ -185,6 +185,8 @@ int get_ctx(int dev, Ctx** out) {
                                  kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kBf16Norm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMaxSmem));
+  VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kQ8Swap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
@@ -455,9 +457,9 @@ int tc2_max_pairs(Ctx* ctx, uint32_t smem, int* out) {
   return VMLM_OK;
 }
 
-int tc2_stages() {
+int tc2_stages(int bn) {
   int stages = 16;
-  while (stages >= 2 && tc2_smem_layout(stages, kPairBn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  while (stages >= 2 && tc2_smem_layout(stages, bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   return stages;
 }
 
@@ -466,11 +468,11 @@ bool use_pairs(const NormPlan& plan, long long rows, long long cols, int sms) {
   return plan.split == 1 && rows >= 2 * kTileRows && pair_tiles * 5 >= static_cast<long long>(sms) * 2;
 }
 
-// p: a normal-mode parameter set whose tiles_m / bn / maps the caller fills for
-// pair tiles (A box 128 rows, B box kPairBn / 2 rows).
+// p: a parameter set whose tiles_m / bn / maps the caller fills for pair
+// tiles (A box 128 rows, B box bn / 2 rows).
 template <TcMode MODE>
 int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool pdl) {
-  p.stages = tc2_stages();
+  p.stages = tc2_stages(p.bn);
   p.tmem_cols = pow2_at_least(2 * p.bn);
   p.csplit = 0;
   p.streamk = 0;
@@ -714,9 +716,16 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   p.w = q;
   p.k = K;
   CUtensorMap ma, mb;
+  if (sh) apply_shard(p, *sh);
+  if (!use_streamk(p, c->sms) && N >= kPairRows) {
+    // whole tiles: CTA pairs over 256 weight rows, each SM loading half the planes
+    p.tiles_m = static_cast<int>(cdiv(N, kPairRows));
+    VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn / 2));
+    return run_tc2<TcMode::kQ8Swap>(c, st, ma, mb, p, true);
+  }
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn));
-  if (sh) apply_shard(p, *sh);
   return run_tc<TcMode::kQ8Swap>(c, st, ma, mb, p, use_streamk(p, c->sms), true);
 }
 

@@ -116,6 +116,28 @@ def test_q8_edge_shapes(kernels, oracle, m, n, k):
     check_q8(kernels, oracle, a, q, s)
 
 
+@pytest.mark.parametrize("m,n,k", [(80, 76000, 256), (17, 80001, 512), (200, 30000, 256)])
+def test_q8_cta_pair_tiles(kernels, oracle, m, n, k):
+    # enough whole weight tiles for the CTA-pair kernel: 256 weight rows per
+    # pair, each SM loading half of the digit planes (ragged N, up to 80
+    # tokens per tile, several token tiles with a ragged last one)
+    x, q, s = q8_case(oracle, m, n, k, seed=n % 97)
+    check_q8(kernels, oracle, x, q, s)
+
+
+def test_q8_cta_pair_nonfinite(kernels, oracle):
+    m, n, k = 40, 76000, 256
+    x, q, s = q8_case(oracle, m, n, k, seed=12)
+    x[3, 17] = np.nan
+    x[39, 0] = -np.inf
+    got = kernels.q8_linear(x, q, s)
+    ref = oracle.gemm_nt_int8(x, q, s, nt=NT)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    fin = np.isfinite(ref)
+    assert oracle.max_rel_err(np.ascontiguousarray(got[fin]), np.ascontiguousarray(ref[fin])) <= TIGHT_Q8
+
+
 def test_q8_nonfinite_rows_match_reference(kernels, oracle):
     m, n, k = 4, 300, 512
     x, q, s = q8_case(oracle, m, n, k, seed=3)

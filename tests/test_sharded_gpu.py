@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 TIGHT_Q8 = 2e-5
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 20000, 2304), (64, 16384, 2304), (5, 300, 256)])
+@pytest.mark.parametrize("m,n,k", [(1, 20000, 2304), (64, 16384, 2304), (5, 300, 256), (64, 80000, 1024)])
 def test_single_rank_sharded_q8_matches_oracle(kernels, oracle, m, n, k):
     import torch
     from sparrow_b200.sharded import PeerOutputs, sharded_gemm_nt_int8
