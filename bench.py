@@ -99,7 +99,8 @@ CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf1
          "c3q_m8": ("q8", 8, 2304, 2304), "c4m1": ("q8", 1, 122753, 2304), "c4m64": ("q8", 64, 122753, 2304),
          "c5": ("i8", 4096, 28672, 8192), "c5small": ("i8", 1024, 4096, 8192),
          "c4m64small": ("q8", 64, 16384, 2304), "c3q_m32": ("q8", 32, 2304, 2304), "c3d_m32": ("q8", 32, 2304, 5760),
-         "c3g_m32": ("q8", 32, 5760, 2304)}
+         "c3g_m32": ("q8", 32, 5760, 2304),
+         "f32nt": ("f32nt", M2, N2, K2), "f32nn": ("f32nn", M2, N2, K2)}
 
 
 def run_case(args):
@@ -121,6 +122,11 @@ def run_case(args):
             x = x.to(torch.bfloat16).float().contiguous()
         w = gen((n, k), 1, 0.02).to(torch.bfloat16)
         step = lambda: K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)  # noqa: E731
+    elif kind in ("f32nt", "f32nn"):
+        x = gen((m, k), 0, 1.0)
+        w = gen((k, n) if kind == "f32nn" else (n, k), 1, 0.02)
+        fn = K.gemm_f32_dev if kind == "f32nn" else K.gemm_nt_f32_dev
+        step = lambda: fn(x, w, c, m, n, k, stream=st)  # noqa: E731
     else:
         g = torch.Generator(device="cuda")
         g.manual_seed(5)
@@ -495,6 +501,31 @@ def bench_configs(K, dist, rank, world, flush, pk):
     tg = gemm_only(K, step, 20, flush, dist)
     res["C2_general_f32_activations"] = {"step_us": t * 1e3, "gemm_us": tg * 1e3, "TFLOPS": FLOP_C2 / t / 1e9,
                                          "note": "3 bf16 split terms of X active: 3x tensor work"}
+    del x, w
+    # f32 GEMMs (gemm_nt, NN gemm) at the C2 shape, general f32 operands: six
+    # bf16 term-pair passes on the tensor cores
+    for name, fn, bshape in (("F32_gemm_nt_512x2304x2304", K.gemm_nt_f32_dev, (N2, K2)),
+                             ("F32_gemm_nn_512x2304x2304", K.gemm_f32_dev, (K2, N2))):
+        a = gen((M2, K2), 9, 1.0)
+        b = gen(bshape, 10, 0.02)
+        step = lambda: fn(a, b, c, M2, N2, K2, stream=st)  # noqa: E731
+        t = time_steps(step, 50, 5, flush, dist)
+        tg = gemm_only(K, step, 20, flush, dist)
+        entry = {"step_us": t * 1e3, "gemm_us": tg * 1e3, "TFLOPS": FLOP_C2 / t / 1e9,
+                 "tensor_TFLOPS_gemm": 6 * FLOP_C2 / tg / 1e9,
+                 "frac_bf16_peak_gemm": 6 * FLOP_C2 / tg / 1e9 / pk["bf16_tflops"],
+                 "note": "both operands split into 3 exact bf16 terms; 6 term-pair passes (i + j <= 2)"}
+        if rank == 0 and world == 1 and name.startswith("F32_gemm_nt"):
+            from oracle import oracle as O
+            an, bn = a.cpu().numpy(), b.cpu().numpy()
+            nt = os.cpu_count() or 1
+            t0 = time.perf_counter()
+            O.gemm_nt_f32(an, bn, nt=nt)
+            tc = time.perf_counter() - t0
+            entry["cpu_oracle"] = {"value": FLOP_C2 / tc / 1e12, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+                                   "sample": "one full run of the restated gemm_nt_scalar (ops/src/kernels.rs:947-967)"}
+        res[name] = entry
+        del a, b
     return res
 
 

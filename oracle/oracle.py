@@ -40,6 +40,8 @@ def lib() -> ctypes.CDLL:
             "oracle_gemm_nt_int8_par": [P, P, P, P, S, S, S, I],
             "oracle_gemm_nt_bf16_par": [P, P, P, S, S, S, I],
             "oracle_gemm_i8i8_par": [P, P, P, P, P, S, S, S, I],
+            "oracle_gemm_nt_f32_par": [P, P, P, S, S, S, I, I],
+            "oracle_gemm_f32_par": [P, P, P, S, S, S, I, I],
             "oracle_fill_uniform": [P, S, U64, F, I],
             "oracle_fill_normal": [P, S, U64, F, I],
             "oracle_fill_gauss_ref": [P, S, U64, F, I],
@@ -115,6 +117,32 @@ def gemm_naive_f32(a, b):
     c = np.empty((m, n), np.float32)
     lib().oracle_gemm_naive_f32(_p(a), _p(b), _p(c), m, n, k)
     return c
+
+
+def gemm_nt_f32(a, b, c=None, nt=1):
+    """ops/src/kernels.rs:947-967 (gemm_nt_scalar): C[M,N] = A[M,K] . B[N,K]^T, plus the
+    old C (one add per element) when c is given (acc)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[0]
+    assert b.shape == (n, k)
+    out = np.array(c, np.float32, order="C", copy=True) if c is not None else np.empty((m, n), np.float32)
+    lib().oracle_gemm_nt_f32_par(_p(a), _p(b), _p(out), m, n, k, int(c is not None), _threads(nt))
+    return out
+
+
+def gemm_f32(a, b, c=None, nt=1):
+    """ops/src/kernels.rs:383-403 (gemm_scalar, which gemm at :407-419 calls): C[M,N] =
+    A[M,K] . B[K,N], plus the old C when c is given (acc)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    assert b.shape == (k, n)
+    out = np.array(c, np.float32, order="C", copy=True) if c is not None else np.empty((m, n), np.float32)
+    lib().oracle_gemm_f32_par(_p(a), _p(b), _p(out), m, n, k, int(c is not None), _threads(nt))
+    return out
 
 
 def gemm_i8i8(x, w, scale, nt=1, want_acc=True):

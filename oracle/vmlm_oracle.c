@@ -19,6 +19,11 @@
  *   oracle_fill_gauss_ref      tests/src/quant.rs:605-613 (Box-Muller on lcg, as written)
  *   oracle_fill_normal         the same lcg with full-range uniforms: true N(0, sigma)
  *   oracle_gemm_naive_f32      tests/src/main.rs:283-295 (naive triple loop)
+ *   oracle_gemm_nt_f32_par     ops/src/kernels.rs:947-967 (gemm_nt_scalar: f32
+ *                              C = A . B^T, B [n,k], sequential mul then add,
+ *                              then `s += c` when acc)
+ *   oracle_gemm_f32_par        ops/src/kernels.rs:383-403 (gemm_scalar, the
+ *                              whole of gemm NN at :407-419: B [k,n])
  *   parallel split             ops/src/par.rs:44-62 (chunk = ceil(n/nt) over N)
  *
  * The AVX2 bodies use the same intrinsic sequence as the reference, so the
@@ -226,15 +231,35 @@ EXPORT void oracle_gemm_i8i8(const int8_t *x, const int8_t *w, const float *scal
     gemm_i8i8_cols(x, w, scale, acc_out, c, m, n, k, 0, n);
 }
 
+/* ------------------------------------------------------- f32 GEMMs
+ * gemm_nt_scalar (ops/src/kernels.rs:947-967) and gemm_scalar (:383-403):
+ * per output a sequential sum of separately rounded products, then one add of
+ * the old C when acc. (The reference's AVX2 8x8 and packed gemm_nt kernels
+ * run FMA chains in other orders; the f32 GEMM's parity is a tolerance.) */
+static void gemm_f32_cols(int nn, const float *a, const float *b, float *c, size_t m, size_t n,
+                          size_t k, int acc, size_t j0, size_t j1) {
+    for (size_t i = 0; i < m; i++)
+        for (size_t j = j0; j < j1; j++) {
+            float s = 0.0f;
+            for (size_t p = 0; p < k; p++) {
+                float prod = a[i * k + p] * (nn ? b[p * n + j] : b[j * k + p]);
+                s = s + prod;
+            }
+            if (acc) s = s + c[i * n + j];
+            c[i * n + j] = s;
+        }
+}
+
 /* ------------------------------------------------ ops/src/par.rs split */
 
 typedef struct {
-    int kind; /* 0 int8, 1 bf16, 2 i8i8 */
+    int kind; /* 0 int8, 1 bf16, 2 i8i8, 3 f32 NT, 4 f32 NN */
     const void *a, *b;
     const float *scale;
     int32_t *acc;
     float *c;
     size_t m, n, k, j0, j1;
+    int accf; /* f32: C += */
 } job_t;
 
 static void *run_job(void *p) {
@@ -245,6 +270,9 @@ static void *run_job(void *p) {
     else if (jb->kind == 1)
         gemm_nt_bf16_cols((const float *)jb->a, (const uint16_t *)jb->b, jb->c,
                           jb->m, jb->n, jb->k, jb->j0, jb->j1);
+    else if (jb->kind == 3 || jb->kind == 4)
+        gemm_f32_cols(jb->kind == 4, (const float *)jb->a, (const float *)jb->b, jb->c, jb->m, jb->n,
+                      jb->k, jb->accf, jb->j0, jb->j1);
     else
         gemm_i8i8_cols((const int8_t *)jb->a, (const int8_t *)jb->b, jb->scale, jb->acc,
                        jb->c, jb->m, jb->n, jb->k, jb->j0, jb->j1);
@@ -288,20 +316,32 @@ static void par_run(job_t base, int nt) {
  * bounded sample of a large problem ([j0,j1) of n, row stride of c is n). */
 EXPORT void oracle_gemm_nt_int8_par(const float *a, const int8_t *q, const float *scale,
                                     float *c, size_t m, size_t n, size_t k, int nt) {
-    job_t b = {0, a, q, scale, NULL, c, m, n, k, 0, n};
+    job_t b = {0, a, q, scale, NULL, c, m, n, k, 0, n, 0};
     par_run(b, nt);
 }
 
 EXPORT void oracle_gemm_nt_bf16_par(const float *a, const uint16_t *w, float *c,
                                     size_t m, size_t n, size_t k, int nt) {
-    job_t b = {1, a, w, NULL, NULL, c, m, n, k, 0, n};
+    job_t b = {1, a, w, NULL, NULL, c, m, n, k, 0, n, 0};
     par_run(b, nt);
 }
 
 EXPORT void oracle_gemm_i8i8_par(const int8_t *x, const int8_t *w, const float *scale,
                                  int32_t *acc, float *c, size_t m, size_t n, size_t k, int nt) {
-    job_t b = {2, x, w, scale, acc, c, m, n, k, 0, n};
+    job_t b = {2, x, w, scale, acc, c, m, n, k, 0, n, 0};
     par_run(b, nt);
+}
+
+EXPORT void oracle_gemm_nt_f32_par(const float *a, const float *b, float *c, size_t m, size_t n,
+                                   size_t k, int acc, int nt) {
+    job_t jb = {3, a, b, NULL, NULL, c, m, n, k, 0, n, acc};
+    par_run(jb, nt);
+}
+
+EXPORT void oracle_gemm_f32_par(const float *a, const float *b, float *c, size_t m, size_t n,
+                                size_t k, int acc, int nt) {
+    job_t jb = {4, a, b, NULL, NULL, c, m, n, k, 0, n, acc};
+    par_run(jb, nt);
 }
 
 /* ------------------------------------------------------------ generators */

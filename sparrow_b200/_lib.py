@@ -30,6 +30,10 @@ SIGNATURES = {
     "vmlm_gemm_nt_int8": (I, [P, P, P, P, S, S, S]),
     "vmlm_gemm_nt_bf16": (I, [P, P, P, S, S, S]),
     "vmlm_gemm_i8i8": (I, [P, P, P, P, P, S, S, S]),
+    "vmlm_gemm_nt_f32": (I, [P, P, P, S, S, S, I]),
+    "vmlm_gemm_f32": (I, [P, P, P, S, S, S, I]),
+    "vmlm_gemm_nt_f32_dev": (I, [P, P, P, S, S, S, I, P]),
+    "vmlm_gemm_f32_dev": (I, [P, P, P, S, S, S, I, P]),
     "vmlm_gemm_nt_int8_dev": (I, [P, P, P, P, S, S, S, P]),
     "vmlm_gemm_nt_bf16_dev": (I, [P, P, P, S, S, S, P]),
     "vmlm_gemm_i8i8_dev": (I, [P, P, P, P, P, S, S, S, P]),

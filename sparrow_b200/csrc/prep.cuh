@@ -218,19 +218,16 @@ __device__ __forceinline__ uint2 pack_bf16x4(const uint16_t (&h)[4]) {
   return make_uint2(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16));
 }
 
-__global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
-    const float* __restrict__ x, long long ldx, int M, int K, int kp, int vec, uint16_t* __restrict__ out,
-    uint8_t* __restrict__ dirty, unsigned* __restrict__ orword, unsigned* __restrict__ orword_next) {
-  pdl_launch_dependents();
-  __shared__ int redi[32];
-  const int t = blockIdx.x;
-  if (t >= M) return;
-  if (t == 0 && threadIdx.x == 0) *orword_next = 0u;
-  const float* xr = x + static_cast<long long>(t) * ldx;
-  uint16_t* o0 = out + static_cast<long long>(t) * 3 * kp;
+// The split of one row (the body of the normal-mode prep kernels). kNf: also
+// flag NaN / Inf (bit 256 of the row's flags; *nf = 1 for such a row, else 0)
+// for the f32 GEMM, whose two split operands cannot carry them.
+template <bool kNf>
+__device__ __forceinline__ void norm_terms_row(const float* __restrict__ xr, int K, int kp, int vec,
+                                               uint16_t* __restrict__ o0, uint8_t* __restrict__ dirty_t,
+                                               int* __restrict__ nf_t, unsigned* __restrict__ orword, int* redi) {
   const int nchunk = kp >> 2;  // kp % 8 == 0
   const bool kept = nchunk <= kNormPrepKeep * kNormPrepThreads;
-  const int old_dirty = dirty[t];
+  const int old_dirty = *dirty_t;
   auto load = [&](int ch) -> float4 {
     const int k = ch * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -263,6 +260,10 @@ __global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
       if (((ux | uy | uz | uw) & 0xffffu) == 0u) {
         // already bf16 values (NaN and Inf included): hi is the top half
         hi = make_uint2((ux >> 16) | (uy & 0xffff0000u), (uz >> 16) | (uw & 0xffff0000u));
+        if constexpr (kNf) {
+          constexpr uint32_t E = 0x7f800000u;
+          if ((ux & E) == E || (uy & E) == E || (uz & E) == E || (uw & E) == E) flags |= 256;
+        }
       } else {
         uint16_t h[4], m[4], l[4];
         bf16_split(v.x, h[0], m[0], l[0], flags);
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
       reinterpret_cast<uint2*>(o0)[ch] = hi;
     }
   }
-  flags = block_or(flags & 6, redi);
+  flags = block_or(flags & (kNf ? (6 | 256) : 6), redi);
   const int need = (flags | old_dirty) & 6;
   // pass 2: mid / lo planes where needed
   if (need) {
@@ -299,9 +300,93 @@ __global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
     }
   }
   if (threadIdx.x == 0) {
-    if (flags != old_dirty) dirty[t] = static_cast<uint8_t>(flags);
+    if ((flags & 6) != old_dirty) *dirty_t = static_cast<uint8_t>(flags & 6);
+    if constexpr (kNf) *nf_t = (flags & 256) ? 1 : 0;
     if (flags) atomicOr(orword, static_cast<unsigned>(flags));
   }
+}
+
+__global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
+    const float* __restrict__ x, long long ldx, int M, int K, int kp, int vec, uint16_t* __restrict__ out,
+    uint8_t* __restrict__ dirty, unsigned* __restrict__ orword, unsigned* __restrict__ orword_next) {
+  pdl_launch_dependents();
+  __shared__ int redi[32];
+  const int t = blockIdx.x;
+  if (t >= M) return;
+  if (t == 0 && threadIdx.x == 0) *orword_next = 0u;
+  norm_terms_row<false>(x + static_cast<long long>(t) * ldx, K, kp, vec, out + static_cast<long long>(t) * 3 * kp,
+                        dirty + t, nullptr, orword, redi);
+}
+
+// Split terms of both operands of the f32 GEMM C = A . B^T (A [M][K], B [N][K],
+// row-major): CTA r < M splits row r of A, CTA M + r row r of B, into their
+// own term buffers, dirty bits, non-finite flags and OR words (flag words as
+// in bf16_terms_norm_kernel; CTA 0 clears both next words).
+__global__ void __launch_bounds__(kNormPrepThreads) f32_terms_nt_kernel(
+    const float* __restrict__ a, long long lda, int M, int vec_a, const float* __restrict__ b, long long ldb, int N,
+    int vec_b, int K, int kp, uint16_t* __restrict__ ta, uint16_t* __restrict__ tb, uint8_t* __restrict__ dirty_a,
+    uint8_t* __restrict__ dirty_b, int* __restrict__ nf_a, int* __restrict__ nf_b, unsigned* __restrict__ or_a,
+    unsigned* __restrict__ or_a_next, unsigned* __restrict__ or_b, unsigned* __restrict__ or_b_next) {
+  pdl_launch_dependents();
+  __shared__ int redi[32];
+  const int r = blockIdx.x;
+  if (r == 0 && threadIdx.x == 0) {
+    *or_a_next = 0u;
+    *or_b_next = 0u;
+  }
+  if (r < M)
+    norm_terms_row<true>(a + static_cast<long long>(r) * lda, K, kp, vec_a, ta + static_cast<long long>(r) * 3 * kp,
+                         dirty_a + r, nf_a + r, or_a, redi);
+  else if (r - M < N)
+    norm_terms_row<true>(b + static_cast<long long>(r - M) * ldb, K, kp, vec_b,
+                         tb + static_cast<long long>(r - M) * 3 * kp, dirty_b + (r - M), nf_b + (r - M), or_b, redi);
+}
+
+// Split terms of the B operand of the NN f32 GEMM C = A . B (B [K][N],
+// row-major), transposed: out[n*3*kp + j*kp + k], columns [K, kp) zero,
+// kp % 64 == 0. A CTA splits a 64 (k) x 64 (n) tile through shared memory
+// (loads coalesced along n, stores along k). nf[n] (zeroed by the caller)
+// becomes 1 for a column of B holding NaN / Inf; each CTA ORs its term flags
+// (2 / 4, 256 for NaN / Inf) into *orword; CTA (0, 0) clears *orword_next.
+constexpr int kTransTile = 64;
+__global__ void __launch_bounds__(256) f32_terms_t_kernel(const float* __restrict__ b, long long ldb, int K, int N,
+                                                          int kp, uint16_t* __restrict__ out, int* __restrict__ nf,
+                                                          unsigned* __restrict__ orword,
+                                                          unsigned* __restrict__ orword_next) {
+  pdl_launch_dependents();
+  __shared__ float tile[kTransTile][kTransTile + 1];
+  __shared__ int cta_flags;
+  const int n0 = blockIdx.x * kTransTile, k0 = blockIdx.y * kTransTile;
+  if (threadIdx.x == 0) {
+    cta_flags = 0;
+    if (blockIdx.x == 0 && blockIdx.y == 0) *orword_next = 0u;
+  }
+  for (int i = threadIdx.x; i < kTransTile * kTransTile; i += 256) {
+    const int kk = i / kTransTile, nn = i - kk * kTransTile;
+    const int k = k0 + kk, n = n0 + nn;
+    tile[kk][nn] = (k < K && n < N) ? b[static_cast<long long>(k) * ldb + n] : 0.f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int my_flags = 0;
+  for (int nn = warp; nn < kTransTile; nn += 8) {
+    const int n = n0 + nn;
+    if (n >= N) break;
+    int f = 0;
+    uint16_t h0, m0, l0, h1, m1, l1;
+    bf16_split(tile[2 * lane][nn], h0, m0, l0, f);
+    bf16_split(tile[2 * lane + 1][nn], h1, m1, l1, f);
+    uint32_t* o = reinterpret_cast<uint32_t*>(out + static_cast<long long>(n) * 3 * kp + k0) + lane;
+    o[0] = h0 | (static_cast<uint32_t>(h1) << 16);
+    o[kp / 2] = m0 | (static_cast<uint32_t>(m1) << 16);
+    o[kp] = l0 | (static_cast<uint32_t>(l1) << 16);
+    f = warp_or(f);
+    if (lane == 0 && (f & 256)) atomicOr(nf + n, 1);
+    my_flags |= f;
+  }
+  if (lane == 0 && my_flags) atomicOr(&cta_flags, my_flags);
+  __syncthreads();
+  if (threadIdx.x == 0 && cta_flags) atomicOr(orword, static_cast<unsigned>(cta_flags));
 }
 
 // One CTA per token. Layout 0 (swap): out[(3t+j)*kp + k]. Layout 1 (normal):

@@ -19,6 +19,10 @@
 //              C[m][n] straight from the accumulator.
 //   kI8Norm    A = int8 activations X[m,:], B = int8 weights W[n,:]:
 //              C[m][n] = f32(acc) * scale[n], and/or the raw int32 acc.
+//   kF32Norm   A and B = bf16 split terms of two f32 operands, both laid out
+//              term-major along K; the passes run the term pairs (i, j) with
+//              i + j <= 2. C[m][n] (+)= the f32 accumulator; outputs touching
+//              a NaN/Inf row are recomputed exactly from the terms.
 //
 // Warp roles (320 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
 // the MMAs, warps 2..9 are the epilogue: warp w reads TMEM lanes
@@ -45,7 +49,7 @@
 
 namespace vmlm {
 
-enum class TcMode : int { kQ8Swap = 0, kBf16Swap = 1, kBf16Norm = 2, kI8Norm = 3 };
+enum class TcMode : int { kQ8Swap = 0, kBf16Swap = 1, kBf16Norm = 2, kI8Norm = 3, kF32Norm = 4 };
 
 constexpr int kTileRows = 128;        // UMMA M
 constexpr int kBlockBytes = 128;      // bytes of K per stage (one 128B swizzle row)
@@ -61,14 +65,14 @@ struct TcParams {
   int cols;          // extent of B rows (plane/term rows in swap modes, W rows in normal modes)
   int bn;            // UMMA N per tile (multiple of 16, <= 256; multiple of 48 in swap modes)
   int kb_per_term;   // k-blocks per pass over K
-  int max_terms;     // kBf16Norm: term passes allocated in A (1..3); 1 otherwise
+  int max_terms;     // kBf16Norm / kF32Norm: terms allocated per operand (1..3); 1 otherwise
   int tiles_m, tiles_n;
   int streamk;       // 1 = stream-K ranges, 0 = round-robin whole tiles
   int tm_fastest;    // tile index -> (tm, tn): 1 = tm varies fastest, 0 = tn fastest
   int stages;
   int tmem_cols;     // allocated TMEM columns (power of two >= 2*bn)
   int a_box_elems;   // TMA box inner extent of A/B in elements (128 int8 or 64 bf16)
-  int term_stride;   // kBf16Norm: element offset between terms along A's K
+  int term_stride;   // kBf16Norm / kF32Norm: element offset between terms along K
   // epilogue
   float* out;        // C, row-major
   long long ldo;     // row stride of C (elements)
@@ -77,7 +81,7 @@ struct TcParams {
   const float* scale;
   const int* exps;        // kQ8Swap: per-token exponent e (value = v * 2^-e)
   const int* nonfinite;   // per-token flag: row of x holds NaN/Inf
-  const int* term_flags;  // kBf16Norm: OR over tokens of (1<<j) for every non-zero term j
+  const int* term_flags;  // kBf16Norm / kF32Norm: OR over A's rows of (1<<j) for every non-zero term j
   int n_tokens;           // tokens (swap modes: real tokens; used for bounds)
   int tok_per_tile;       // swap modes: tokens per column tile (bn/3)
   int n_out;              // swap modes: W rows (bounds on n)
@@ -90,6 +94,17 @@ struct TcParams {
   uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
+  // kF32Norm (C = A . B^T, both operands f32 split into three bf16 terms):
+  // B's terms at j * term_stride along its K, B's OR word, per-row NaN/Inf
+  // flags of A and B, both term buffers ([rows][3 * term_stride]) for the
+  // exact recompute of outputs that touch a NaN/Inf row, and acc_c = add the
+  // old C (C += A . B^T).
+  const int* term_flags_b;
+  const int* nf_a;
+  const int* nf_b;
+  const uint16_t* terms_a;
+  const uint16_t* terms_b;
+  int acc_c;
   // Row-sharded call with the all-gather in the epilogue (npeers > 0): this
   // rank computes output columns [col_off, col_off + its rows) and stores every
   // value into all npeers ranks' full C (peer_out[q], row stride ldo) over
@@ -193,13 +208,49 @@ struct Sched {
 
 // Number of split terms with any non-zero value (term_flags points at the OR of
 // all tokens' flags, written by the prep kernel).
-__device__ __forceinline__ int active_terms(const TcParams& p) {
-  if (p.max_terms <= 1) return 1;
-  const int orv = __ldcg(p.term_flags);
+__device__ __forceinline__ int terms_of_word(const int* word, int max_terms) {
+  if (max_terms <= 1) return 1;
+  const int orv = __ldcg(word);
   int T = 1;
   if (orv & 2) T = 2;
   if (orv & 4) T = 3;
-  return T < p.max_terms ? T : p.max_terms;
+  return T < max_terms ? T : max_terms;
+}
+
+__device__ __forceinline__ int active_terms(const TcParams& p) { return terms_of_word(p.term_flags, p.max_terms); }
+
+// The passes over K: a list of (A term i, B term j) pairs, 4 bits each
+// (i | j << 2) in pass order; *np = their count. kBf16Norm runs A's active
+// terms against the bf16 weights; kF32Norm the pairs with i + j <= 2 of both
+// operands' active terms (the dropped products are below 2^-24 relative),
+// smallest first: the tensor cores' f32 accumulation does not round each add
+// to nearest, so the correction passes accumulate while the accumulator is
+// still small, and the hi x hi pass comes last.
+template <TcMode MODE>
+__device__ __forceinline__ uint32_t term_pairs(const TcParams& p, int* np) {
+  if constexpr (MODE == TcMode::kBf16Norm) {
+    const int T = active_terms(p);
+    *np = T;
+    return 0x210u & ((1u << (4 * T)) - 1u);
+  } else if constexpr (MODE == TcMode::kF32Norm) {
+    const int ta = active_terms(p), tb = terms_of_word(p.term_flags_b, p.max_terms);
+    constexpr uint32_t kCand = 0x041852u;  // (2,0) (1,1) (0,2) (1,0) (0,1) (0,0)
+    uint32_t list = 0;
+    int n = 0;
+    #pragma unroll
+    for (int c = 0; c < 6; ++c) {
+      const uint32_t code = (kCand >> (4 * c)) & 15u;
+      if (static_cast<int>(code & 3u) < ta && static_cast<int>(code >> 2) < tb) {
+        list |= code << (4 * n);
+        ++n;
+      }
+    }
+    *np = n;
+    return list;
+  } else {
+    *np = 1;
+    return 0u;
+  }
 }
 
 // ------------------------------------------------------------- epilogues
@@ -207,6 +258,8 @@ __device__ __forceinline__ int active_terms(const TcParams& p) {
 // Store a 32-row x 16-column block held one row per lane (lane = row - row0)
 // through a per-warp shared buffer, so that each store instruction writes 8
 // rows x 64 contiguous bytes instead of 32 rows x 16 bytes.
+// kAdd: f32 values added to the destination's old values (C += ...).
+template <bool kAdd = false>
 __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, int row0, int nrows, int col0,
                                                   int ncols, bool vec, uint32_t* buf, const uint32_t (&v)[16]) {
   const int lane = threadIdx.x & 31;
@@ -222,14 +275,43 @@ __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, i
       uint32_t* d = dst + static_cast<long long>(grow) * ld + col0 + c;
       const uint32_t* s = buf + r * 17 + c;
       if (vec && col0 + c + 4 <= ncols) {
-        *reinterpret_cast<uint4*>(d) = make_uint4(s[0], s[1], s[2], s[3]);
+        uint4 o = make_uint4(s[0], s[1], s[2], s[3]);
+        if constexpr (kAdd) {
+          const float4 q = *reinterpret_cast<const float4*>(d);
+          o = make_uint4(__float_as_uint(__fadd_rn(__uint_as_float(o.x), q.x)),
+                         __float_as_uint(__fadd_rn(__uint_as_float(o.y), q.y)),
+                         __float_as_uint(__fadd_rn(__uint_as_float(o.z), q.z)),
+                         __float_as_uint(__fadd_rn(__uint_as_float(o.w), q.w)));
+        }
+        *reinterpret_cast<uint4*>(d) = o;
       } else {
         for (int j = 0; j < 4; ++j)
-          if (col0 + c + j < ncols) d[j] = s[j];
+          if (col0 + c + j < ncols) {
+            if constexpr (kAdd)
+              d[j] = __float_as_uint(__fadd_rn(__uint_as_float(s[j]), __uint_as_float(d[j])));
+            else
+              d[j] = s[j];
+          }
       }
     }
   }
   __syncwarp();
+}
+
+// Exact f32 recompute of C[t][n] for the f32 GEMM when row t of A or row n of
+// B holds NaN / Inf: the values are rebuilt from their three terms (exact, and
+// NaN / Inf survive in the first term) and summed sequentially. Out of line
+// (a cold path).
+__device__ __noinline__ float f32_terms_dot(const uint16_t* ta, const uint16_t* tb, int k, int kp) {
+  auto val = [&](const uint16_t* t, int kk) {
+    const float h = __uint_as_float(static_cast<uint32_t>(t[kk]) << 16);
+    const float m = __uint_as_float(static_cast<uint32_t>(t[kp + kk]) << 16);
+    const float l = __uint_as_float(static_cast<uint32_t>(t[2 * kp + kk]) << 16);
+    return __fadd_rn(__fadd_rn(h, m), l);
+  };
+  float s = 0.f;
+  for (int kk = 0; kk < k; ++kk) s = __fadd_rn(s, __fmul_rn(val(ta, kk), val(tb, kk)));
+  return s;
 }
 
 // Finish 16 columns [col0, col0+16) of the warp's 32 accumulator rows
@@ -255,6 +337,26 @@ __device__ __forceinline__ void epi_norm16(const TcParams& p, int row0, int col0
                             p.cols, p.vec_out, buf, f);
       }
     }
+  } else if constexpr (MODE == TcMode::kF32Norm) {
+    uint32_t f[16];
+    #pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = v[j];
+    if ((__ldcg(p.term_flags) | __ldcg(p.term_flags_b)) & 256) {
+      // some row of A or B holds NaN / Inf: recompute the outputs that touch one
+      const int t = row0 + (threadIdx.x & 31);
+      const bool bad_t = t < p.rows && __ldg(p.nf_a + t);
+      const long long tp = 3ll * p.term_stride;
+      for (int j = 0; j < 16; ++j) {
+        const int n = col0 + j;
+        if (t < p.rows && n < p.cols && (bad_t || __ldg(p.nf_b + n)))
+          f[j] = __float_as_uint(f32_terms_dot(p.terms_a + t * tp, p.terms_b + n * tp, p.k, p.term_stride));
+      }
+    }
+    if (p.acc_c)
+      store_block_32x16<true>(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf,
+                              f);
+    else
+      store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, f);
   } else if (p.npeers == 0) {
     store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, v);
   } else {
@@ -460,8 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int npre = 0;  // stages of item 0 whose weight half is already in flight
       uint32_t issued_mask0 = 0;
       const Sched sc = make_sched();
-      {
-        // The first k-blocks of item 0 belong to term 0 whatever T turns out to be.
+      if constexpr (MODE != TcMode::kF32Norm) {
+        // The first k-blocks of item 0 belong to term 0 whatever T turns out to
+        // be. (kF32Norm: both operands come from the previous kernel.)
         long long cur0 = 0;
         WorkItem w0;
         if (sc.item(cta, 0, cur0, w0)) {
@@ -481,7 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait_prior();
       if (trace) trace[1] = globaltimer();
-      const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
+      int T;  // passes over K (term pairs)
+      const uint32_t pairs = term_pairs<MODE>(p, &T);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = issued_mask0, last_phase = 0;  // per stage: ever issued / parity of last issue
@@ -494,8 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tn = p.tm_fastest ? w.tile / p.tiles_m : w.tile % p.tiles_n;
         const int nkb = w.kb1 - w.kb0;
         for (int j = 0; j < T * nkb; ++j) {
-          const int term = j / nkb;
-          const int kin = w.kb0 + (j - term * nkb);
+          const int pass = j / nkb;
+          const uint32_t code = (pairs >> (4 * pass)) & 15u;  // A term | B term << 2
+          const int kin = w.kb0 + (j - pass * nkb);
           const bool pre = (i == 0 && j < npre);
           const unsigned long long tw = trace ? globaltimer() : 0;
           if (!pre && !mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
@@ -507,9 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = smem + L.b_off + stage * L.b_bytes;
           if (!pre) mbar_arrive_expect_tx(full_bar + stage, L.a_bytes + L.b_bytes);
           const int kbx = kin * p.a_box_elems;
-          const int ka = term * p.term_stride + kbx;
+          const int ka = static_cast<int>(code & 3u) * p.term_stride + kbx;
+          const int kb = static_cast<int>(code >> 2) * p.term_stride + kbx;
           if (!pre || !kWeightIsA) tma_load_2d(sa, &tmA, full_bar + stage, ka, tm * kTileRows, pol_a);
-          if (!pre || kWeightIsA) tma_load_2d(sb, &tmB, full_bar + stage, kbx, tn * p.bn, pol_b);
+          if (!pre || kWeightIsA) tma_load_2d(sb, &tmB, full_bar + stage, kb, tn * p.bn, pol_b);
           issued_mask |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
@@ -534,7 +640,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       pdl_wait_prior();
       const Sched sc = make_sched();
-      const int T = (MODE == TcMode::kBf16Norm) ? active_terms(p) : 1;
+      int T;  // passes over K (term pairs)
+      term_pairs<MODE>(p, &T);
       int stage = 0;
       uint32_t phase = 0;
       long long cur = 0;

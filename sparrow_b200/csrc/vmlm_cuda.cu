@@ -93,9 +93,15 @@ struct Ctx {
   DevBuf norm_terms, norm_dirty, norm_flags;
   int norm_m = -1, norm_kp = -1;
   unsigned norm_parity = 0;
+  // f32 GEMM: term planes, dirty bits and NaN/Inf flags of both operands, and
+  // their term-flag words (two per operand, used by alternate calls)
+  DevBuf f32_ta, f32_tb, f32_da, f32_db, f32_nfa, f32_nfb, f32_flags;
+  int f32_m = -1, f32_n = -1, f32_kp = -1;
+  bool f32_b_from_t = false;  // B's planes were last written by the transposing kernel
+  unsigned f32_parity = 0;
   int* err = nullptr;       // device error word
   int* err_host = nullptr;  // pinned copy read after host-API calls
-  DevBuf h_a, h_c, h_w, h_s, h_acc;  // host-API staging
+  DevBuf h_a, h_c, h_w, h_s, h_acc, h_b;  // host-API staging
   bool attrs_set = false;
   std::map<std::pair<int, uint32_t>, int> dec_clusters;  // (cluster size, smem) -> co-resident clusters
 };
@@ -181,6 +187,7 @@ int get_ctx(int dev, Ctx** out) {
   VMLM_TRY(set_smem_attr<TcMode::kBf16Swap>());
   VMLM_TRY(set_smem_attr<TcMode::kBf16Norm>());
   VMLM_TRY(set_smem_attr<TcMode::kI8Norm>());
+  VMLM_TRY(set_smem_attr<TcMode::kF32Norm>());
   VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kI8Norm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kBf16Norm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -790,6 +797,106 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   return run_tc<TcMode::kBf16Norm>(c, st, ma, mb, p, false, true, plan.split);
 }
 
+// ------------------------------------------------------------- f32 path
+
+// C[M,N] (+)= A[M,K] . op(B): nn == false takes B as [N,K] (gemm_nt), nn ==
+// true as [K,N] (gemm). Both operands are split into three bf16 terms (B
+// transposed to [N][K'] when nn), then the tcgen05 GEMM runs the term pairs
+// with i + j <= 2; outputs touching a NaN/Inf row are recomputed exactly.
+int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, int K, bool acc, bool nn,
+            cudaStream_t st) {
+  if (K == 0) {
+    // the dot products are empty: C = 0, or C unchanged when accumulating
+    if (!acc) VMLM_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(M) * N * 4, st));
+    return VMLM_OK;
+  }
+  const int kp = static_cast<int>(cdiv(K, 64) * 64);  // a k-block never runs into the next term
+  const size_t ta_bytes = static_cast<size_t>(3) * M * kp * 2, tb_bytes = static_cast<size_t>(3) * N * kp * 2;
+  if (M != c->f32_m || N != c->f32_n || kp != c->f32_kp) {
+    // a new layout: planes and dirty bits start over at zero
+    VMLM_TRY(ensure(c->f32_ta, ta_bytes));
+    VMLM_TRY(ensure(c->f32_tb, tb_bytes));
+    VMLM_TRY(ensure(c->f32_da, static_cast<size_t>(M)));
+    VMLM_TRY(ensure(c->f32_db, static_cast<size_t>(N)));
+    VMLM_TRY(ensure(c->f32_nfa, static_cast<size_t>(M) * 4));
+    VMLM_TRY(ensure(c->f32_nfb, static_cast<size_t>(N) * 4));
+    VMLM_CUDA(cudaMemsetAsync(c->f32_ta.p, 0, ta_bytes, st));
+    VMLM_CUDA(cudaMemsetAsync(c->f32_tb.p, 0, tb_bytes, st));
+    VMLM_CUDA(cudaMemsetAsync(c->f32_da.p, 0, static_cast<size_t>(M), st));
+    VMLM_CUDA(cudaMemsetAsync(c->f32_db.p, 0, static_cast<size_t>(N), st));
+    c->f32_m = M;
+    c->f32_n = N;
+    c->f32_kp = kp;
+    c->f32_b_from_t = false;
+  }
+  VMLM_TRY(ensure(c->f32_flags, 512, true));
+  unsigned* fw = static_cast<unsigned*>(c->f32_flags.p);  // four words on separate 128-byte lines
+  const unsigned par = c->f32_parity;
+  c->f32_parity ^= 1u;
+  unsigned* or_a = fw + 32 * par;
+  unsigned* or_a_next = fw + 32 * (par ^ 1u);
+  unsigned* or_b = fw + 64 + 32 * par;
+  unsigned* or_b_next = fw + 64 + 32 * (par ^ 1u);
+  uint16_t* ta = static_cast<uint16_t*>(c->f32_ta.p);
+  uint16_t* tb = static_cast<uint16_t*>(c->f32_tb.p);
+  uint8_t* da = static_cast<uint8_t*>(c->f32_da.p);
+  uint8_t* db = static_cast<uint8_t*>(c->f32_db.p);
+  int* nfa = static_cast<int*>(c->f32_nfa.p);
+  int* nfb = static_cast<int*>(c->f32_nfb.p);
+  const int vec_a = (K % 4 == 0) && aligned16(a);
+  if (nn) {
+    // B^T's terms by the transposing kernel (every plane written), then A's;
+    // neither launch overlaps its predecessor, so the GEMM's wait for the
+    // previous kernel covers both
+    VMLM_CUDA(cudaMemsetAsync(nfb, 0, static_cast<size_t>(N) * 4, st));
+    VMLM_TRY(launch(f32_terms_t_kernel, dim3(static_cast<unsigned>(cdiv(N, kTransTile)),
+                                             static_cast<unsigned>(kp / kTransTile)),
+                    dim3(256), 0, st, false, b, static_cast<long long>(N), K, N, kp, tb, nfb, or_b, or_b_next));
+    c->f32_b_from_t = true;
+    VMLM_TRY(launch(f32_terms_nt_kernel, dim3(static_cast<unsigned>(M)), dim3(kNormPrepThreads), 0, st, false, a,
+                    static_cast<long long>(K), M, vec_a, static_cast<const float*>(nullptr), 0ll, 0, 0, K, kp, ta,
+                    tb, da, db, nfa, nfb, or_a, or_a_next, or_b, or_b_next));
+  } else {
+    if (c->f32_b_from_t) {
+      // the transposing kernel wrote every plane of B: rewrite them all once
+      VMLM_CUDA(cudaMemsetAsync(db, 6, static_cast<size_t>(N), st));
+      c->f32_b_from_t = false;
+    }
+    const int vec_b = (K % 4 == 0) && aligned16(b);
+    VMLM_TRY(launch(f32_terms_nt_kernel, dim3(static_cast<unsigned>(M + N)), dim3(kNormPrepThreads), 0, st, false,
+                    a, static_cast<long long>(K), M, vec_a, b, static_cast<long long>(K), N, vec_b, K, kp, ta, tb, da,
+                    db, nfa, nfb, or_a, or_a_next, or_b, or_b_next));
+  }
+  NormPlan plan;
+  VMLM_TRY(plan_norm<TcMode::kF32Norm>(c, M, N, kp, 2, false, &plan));
+  TcParams p = {};
+  p.rows = M;
+  p.cols = N;
+  p.bn = plan.bn;
+  p.max_terms = 3;
+  p.a_box_elems = 64;
+  p.kb_per_term = kp / 64;
+  p.term_stride = kp;
+  p.term_flags = reinterpret_cast<const int*>(or_a);
+  p.term_flags_b = reinterpret_cast<const int*>(or_b);
+  p.nf_a = nfa;
+  p.nf_b = nfb;
+  p.terms_a = ta;
+  p.terms_b = tb;
+  p.acc_c = acc ? 1 : 0;
+  p.tiles_m = static_cast<int>(cdiv(M, kTileRows));
+  p.tiles_n = static_cast<int>(cdiv(N, p.bn));
+  p.tm_fastest = 1;
+  p.out = out;
+  p.ldo = N;
+  p.vec_out = (N % 4 == 0) && aligned16(out);
+  p.k = K;
+  CUtensorMap ma, mb;
+  VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ta, 3ull * kp, M, 6ull * kp, 64, kTileRows));
+  VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, tb, 3ull * kp, N, 6ull * kp, 64, p.bn));
+  return run_tc<TcMode::kF32Norm>(c, st, ma, mb, p, false, true, plan.split);
+}
+
 int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, cudaStream_t st) {
   const bool tc_ok = K > 0 && K % 8 == 0 && aligned16(b);
   if (!tc_ok) {
@@ -913,12 +1020,44 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
     if (c->sync.p) cudaMemset(c->sync.p, 0, c->sync.bytes);
     if (c->slots.p) cudaMemset(c->slots.p, 0, c->slots.bytes);
     if (c->norm_flags.p) cudaMemset(c->norm_flags.p, 0, c->norm_flags.bytes);
+    if (c->f32_flags.p) cudaMemset(c->f32_flags.p, 0, c->f32_flags.bytes);
     *c->err_host = 0;
     return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
   }
   return VMLM_OK;
 }
 
+int host_f32(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc, bool nn,
+             const char* what) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "%s: null pointer", what);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *db = nullptr;
+  if (k > 0) {
+    VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+    VMLM_TRY(resolve(ctx, b, n * k * 4, ctx->h_b, ctx->stream, &db));
+  }
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  if (acc) VMLM_CUDA(cudaMemcpyAsync(ctx->h_c.p, c, m * n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  VMLM_TRY(run_f32(ctx, static_cast<const float*>(da), static_cast<const float*>(db), static_cast<float*>(ctx->h_c.p),
+                   static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), acc != 0, nn, ctx->stream));
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int dev_f32(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc, bool nn, void* stream,
+            const char* what) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "%s: null pointer", what);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_f32(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), acc != 0, nn, st);
+}
 }  // namespace
 
 // =================================================================== C ABI
@@ -963,7 +1102,8 @@ int vmlm_shutdown(void) {
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
     for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->shard_done, &c->sync, &c->norm_terms,
-                      &c->norm_dirty, &c->norm_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc})
+                      &c->norm_dirty, &c->norm_flags, &c->f32_ta, &c->f32_tb, &c->f32_da, &c->f32_db, &c->f32_nfa,
+                      &c->f32_nfb, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
@@ -1066,6 +1206,24 @@ int vmlm_gemm_i8i8(const int8_t* x, const int8_t* w, const float* scale, float* 
                     acc ? static_cast<int32_t*>(ctx->h_acc.p) : nullptr, static_cast<int>(m), static_cast<int>(n),
                     static_cast<int>(k), ctx->stream));
   return finish_host_call(ctx, c, m * n * 4, acc, m * n * 4);
+}
+
+int vmlm_gemm_nt_f32(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc) {
+  return host_f32(a, b, c, m, n, k, acc, false, "gemm_nt_f32");
+}
+
+int vmlm_gemm_f32(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc) {
+  return host_f32(a, b, c, m, n, k, acc, true, "gemm_f32");
+}
+
+int vmlm_gemm_nt_f32_dev(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc,
+                         void* stream) {
+  return dev_f32(a, b, c, m, n, k, acc, false, stream, "gemm_nt_f32_dev");
+}
+
+int vmlm_gemm_f32_dev(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int acc,
+                      void* stream) {
+  return dev_f32(a, b, c, m, n, k, acc, true, stream, "gemm_f32_dev");
 }
 
 int vmlm_gemm_nt_int8_dev(const float* a, const int8_t* q, const float* scale, float* c, size_t m, size_t n,

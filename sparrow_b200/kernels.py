@@ -148,6 +148,20 @@ def gemm_i8i8(x, w, scale, c, acc, m, n, k) -> None:
         _host_ptr(acc, np.int32, m * n, "acc") if acc is not None else None, m, n, k))
 
 
+def gemm_nt_f32(a, b, c, m, n, k, acc=False) -> None:
+    """C[M,N] = A[M,K] . B[N,K]^T, plus the old C when acc  (ops/src/kernels.rs:987-1015)."""
+    check(lib().vmlm_gemm_nt_f32(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(b, np.float32, n * k, "b"),
+        _host_ptr(c, np.float32, m * n, "c"), m, n, k, int(bool(acc))))
+
+
+def gemm_f32(a, b, c, m, n, k, acc=False) -> None:
+    """C[M,N] = A[M,K] . B[K,N], plus the old C when acc  (ops/src/kernels.rs:383-419)."""
+    check(lib().vmlm_gemm_f32(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(b, np.float32, k * n, "b"),
+        _host_ptr(c, np.float32, m * n, "c"), m, n, k, int(bool(acc))))
+
+
 # ----------------------------------------------------------- device variants
 
 def gemm_nt_int8_dev(a, q, scale, c, m, n, k, stream=None) -> None:
@@ -184,6 +198,18 @@ def gemm_i8i8_dev(x, w, scale, c, acc, m, n, k, stream=None) -> None:
         _dev_ptr(x, "int8", m * k, "x"), _dev_ptr(w, "int8", n * k, "w"),
         _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"),
         _dev_ptr(acc, "int32", m * n, "acc"), m, n, k, _stream_ptr(stream)))
+
+
+def gemm_nt_f32_dev(a, b, c, m, n, k, acc=False, stream=None) -> None:
+    check(lib().vmlm_gemm_nt_f32_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(b, "float32", n * k, "b"),
+        _dev_ptr(c, "float32", m * n, "c"), m, n, k, int(bool(acc)), _stream_ptr(stream)))
+
+
+def gemm_f32_dev(a, b, c, m, n, k, acc=False, stream=None) -> None:
+    check(lib().vmlm_gemm_f32_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(b, "float32", k * n, "b"),
+        _dev_ptr(c, "float32", m * n, "c"), m, n, k, int(bool(acc)), _stream_ptr(stream)))
 
 
 # ---------------------------------------------------------- conveniences

@@ -214,3 +214,19 @@ def test_i8i8_oracle_exact(oracle):
     ref = x.astype(np.int64) @ w.astype(np.int64).T
     assert np.array_equal(acc, ref.astype(np.int32))
     assert np.array_equal(c, (ref.astype(np.float32) * s[None, :]).astype(np.float32))
+
+
+@pytest.mark.parametrize("m,n,k", EDGE_SHAPES)
+def test_f32_gemm_restatements_match_the_reference_naive_loop(oracle, m, n, k):
+    # gemm_nt_scalar (ops/src/kernels.rs:947-967) sums in the order of the
+    # reference test's naive loop (tests/src/main.rs:283-295): bit-identical;
+    # gemm_scalar (NN, :383-403) on B^T too; acc adds the old C once
+    a, b = edge_inputs(m, n, k)
+    ref = oracle.gemm_naive_f32(a, b)
+    got = oracle.gemm_nt_f32(a, b)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    got_nn = oracle.gemm_f32(a, np.ascontiguousarray(b.T))
+    assert np.array_equal(got_nn.view(np.uint32), ref.view(np.uint32))
+    c0 = (np.arange(m * n, dtype=np.float32).reshape(m, n) % 7) - 3.0
+    got_acc = oracle.gemm_nt_f32(a, b, c0)
+    assert np.array_equal(got_acc.view(np.uint32), (ref + c0).astype(np.float32).view(np.uint32))
