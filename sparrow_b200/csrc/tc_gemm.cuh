@@ -298,6 +298,45 @@ __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, i
   __syncwarp();
 }
 
+// The K-split (csplit) epilogue of kBf16Norm, out of line so that one copy of
+// the code serves the real calls and a dry run the epilogue warps make while
+// the MMAs still run: code a warp executes for the first time waits for
+// instruction fetches from L2 (about 2000 cycles per phase here), and the dry
+// run takes those off the critical path.
+//
+// Publish 16 accumulator columns at TMEM address taddr: word j of each lane
+// goes to cluster shared-memory address dst + j * stride.
+__device__ __noinline__ void csplit_publish16(uint32_t taddr, uint32_t dst, uint32_t stride) {
+  uint32_t v[16];
+  tmem_ld16(taddr, v);
+  tmem_ld_wait();
+  #pragma unroll
+  for (int j = 0; j < 16; ++j) st_cluster_u32(dst + static_cast<uint32_t>(j) * stride, v[j]);
+}
+
+// Finish 16 columns: this CTA's partial (TMEM at taddr) and the other S - 1
+// partials in shared memory (sender slot s at recv + s * slot_stride, column j
+// at j * col_stride), summed in rank order in f32, stored as a 32 x 16 block
+// of C (store_block_32x16's arguments; nrows = 0 stores nothing).
+__device__ __noinline__ void csplit_finish16_f32(uint32_t taddr, const uint32_t* recv, int slot_stride,
+                                                 int col_stride, int S, int rank, uint32_t* dst, long long ld,
+                                                 int row0, int nrows, int col0, int ncols, int vec, uint32_t* buf) {
+  uint32_t own[16], v[16];
+  tmem_ld16(taddr, own);
+  tmem_ld_wait();
+  #pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = 0u;
+  for (int q = 0; q < S; ++q) {
+    const uint32_t* src = recv + (q - (q > rank ? 1 : 0)) * slot_stride;
+    #pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t a = (q == rank) ? own[j] : src[j * col_stride];
+      v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __uint_as_float(a)));
+    }
+  }
+  store_block_32x16(dst, ld, row0, nrows, col0, ncols, vec != 0, buf, v);
+}
+
 // Exact f32 recompute of C[t][n] for the f32 GEMM when row t of A or row n of
 // B holds NaN / Inf: the values are rebuilt from their three terms (exact, and
 // NaN / Inf survive in the first term) and summed sequentially. Out of line
@@ -708,6 +747,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Column chunks: 48 columns (16 tokens) in swap modes, 16 otherwise; warp
     // pair (quarter, half) takes chunks ci with ci % 2 == half.
     constexpr int kChunk = kSwap ? 48 : 16;
+    if constexpr (MODE == TcMode::kBf16Norm) {
+      if (p.csplit > 1) {
+        // Dry run of the split-tile epilogue (see csplit_publish16): TMEM of
+        // the idle second accumulator buffer (one item per CTA here), into
+        // this warp's own staging buffer, and no stores to C.
+        const uint32_t idle = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + p.bn;
+        __syncwarp();
+        csplit_publish16(idle, mapa_shared(smem_u32(s_stage) + lane * 4, cluster_ctarank()), 4);
+        __syncwarp();
+        csplit_finish16_f32(idle, s_stage, 0, 1, p.csplit, 0, reinterpret_cast<uint32_t*>(p.out), p.ldo, 0, 0, 0,
+                            p.cols, 0, s_stage);
+        __syncwarp();
+      }
+    }
     pdl_wait_prior();
     const Sched sc = make_sched();
     long long cur = 0;
@@ -822,12 +875,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t base = mapa_shared(smem_u32(smem), static_cast<uint32_t>(q)) +
                                   static_cast<uint32_t>(((rank - (rank > q ? 1 : 0)) * slice * kTileRows + row) * 4);
             for (int ci = half; ci < nsc; ci += 2) {
-              uint32_t v[16];
               __syncwarp();
-              tmem_ld16(tbase + q * slice + ci * 16, v);
-              tmem_ld_wait();
-              #pragma unroll
-              for (int j = 0; j < 16; ++j) st_cluster_u32(base + static_cast<uint32_t>((ci * 16 + j) * kTileRows * 4), v[j]);
+              if constexpr (MODE == TcMode::kBf16Norm) {
+                csplit_publish16(tbase + q * slice + ci * 16, base + static_cast<uint32_t>(ci * 16 * kTileRows * 4),
+                                 kTileRows * 4);
+              } else {
+                uint32_t v[16];
+                tmem_ld16(tbase + q * slice + ci * 16, v);
+                tmem_ld_wait();
+                #pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  st_cluster_u32(base + static_cast<uint32_t>((ci * 16 + j) * kTileRows * 4), v[j]);
+              }
             }
           }
           const unsigned long long tp1 = trace ? globaltimer() : 0;
@@ -837,6 +896,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const unsigned long long tp2 = trace ? globaltimer() : 0;
           if (trace) epi_cnt += tp2 - tp1;
           for (int ci = half; ci < nsc; ci += 2) {
+            if constexpr (MODE == TcMode::kBf16Norm) {
+              __syncwarp();
+              csplit_finish16_f32(tbase + rank * slice + ci * 16, recv + ci * 16 * kTileRows + row, slice * kTileRows,
+                                  kTileRows, S, rank, reinterpret_cast<uint32_t*>(p.out), p.ldo, grow - lane, p.rows,
+                                  tn * p.bn + rank * slice + ci * 16, p.cols, p.vec_out, s_stage);
+              continue;
+            }
             uint32_t own[16], v[16];
             __syncwarp();
             tmem_ld16(tbase + rank * slice + ci * 16, own);
