@@ -104,28 +104,29 @@ def _two_gpu_rank(rank, world, port, errors):
             dist.barrier()
             peers.close()
             dist.barrier()
-        # int8 x int8 FFN shape (smaller), bit-exact
-        m, n, k = 512, 8192, 1024
-        g.manual_seed(99)
-        x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
-        w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
-        s = torch.rand((n,), generator=g, device="cuda") * 0.01 + 1e-3
-        full = torch.empty((m, n), device="cuda")
-        st = torch.cuda.current_stream()
-        K.gemm_i8i8_dev(x, w, s, full, None, m, n, k, stream=st)
-        r0, r1 = shard_rows(n, world, rank)
-        ws, ss = w[r0:r1].contiguous(), s[r0:r1].contiguous()
-        peers = PeerOutputs(m, n)
-        torch.cuda.synchronize()
-        dist.barrier()
-        sharded_gemm_i8i8(x, ws, ss, peers, m, n, k, stream=st)
-        torch.cuda.synchronize()
-        K.sync()
-        if not torch.equal(peers.c.view(torch.int32), full.view(torch.int32)):
-            errors.put(f"rank {rank} i8i8: results differ")
-        dist.barrier()
-        peers.close()
-        dist.barrier()
+        # int8 x int8 FFN shapes (smaller), bit-exact: a K-split plan, and one
+        # on CTA pairs (256-row tiles over two SMs) with the peer stores
+        for m, n, k in ((512, 8192, 1024), (2048, 8192, 1024)):
+            g.manual_seed(99 + m)
+            x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
+            w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+            s = torch.rand((n,), generator=g, device="cuda") * 0.01 + 1e-3
+            full = torch.empty((m, n), device="cuda")
+            st = torch.cuda.current_stream()
+            K.gemm_i8i8_dev(x, w, s, full, None, m, n, k, stream=st)
+            r0, r1 = shard_rows(n, world, rank)
+            ws, ss = w[r0:r1].contiguous(), s[r0:r1].contiguous()
+            peers = PeerOutputs(m, n)
+            torch.cuda.synchronize()
+            dist.barrier()
+            sharded_gemm_i8i8(x, ws, ss, peers, m, n, k, stream=st)
+            torch.cuda.synchronize()
+            K.sync()
+            if not torch.equal(peers.c.view(torch.int32), full.view(torch.int32)):
+                errors.put(f"rank {rank} i8i8 {m}x{n}: results differ")
+            dist.barrier()
+            peers.close()
+            dist.barrier()
     except Exception as e:  # reported to the parent, which fails the test
         errors.put(f"rank {rank}: {type(e).__name__}: {e}")
     finally:
