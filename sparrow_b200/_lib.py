@@ -14,9 +14,19 @@ STATUS = {
     5: "VMLM_ERR_STATE",
     6: "VMLM_ERR_OOM",
     7: "VMLM_ERR_DEVICE_TIMEOUT",
+    8: "VMLM_ERR_OPERATOR",
 }
 
 P, S, I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+
+
+class Slot(ctypes.Structure):
+    """vmlm_slot: a VM slot as the OP_GEMM operator reads it."""
+    _fields_ = [("ptr", ctypes.c_void_p), ("rows", ctypes.c_size_t), ("cols", ctypes.c_size_t),
+                ("dtype", ctypes.c_int)]
+
+
+SP = ctypes.POINTER(Slot)
 
 # name -> (restype, argtypes); must list every symbol the header declares.
 SIGNATURES = {
@@ -50,6 +60,8 @@ SIGNATURES = {
     "vmlm_profile_take": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
     "vmlm_trace_enable": (I, [I]),
     "vmlm_trace_take": (I, [P, S]),
+    "vmlm_op_gemm": (I, [ctypes.c_uint, SP, SP, SP, SP]),
+    "vmlm_op_gemm_dev": (I, [ctypes.c_uint, SP, SP, SP, SP, P]),
 }
 
 

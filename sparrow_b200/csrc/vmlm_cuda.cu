@@ -1058,6 +1058,58 @@ int dev_f32(const float* a, const float* b, float* c, size_t m, size_t n, size_t
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_f32(ctx, a, b, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), acc != 0, nn, st);
 }
+// The OP_GEMM arm of Vm::run (core/src/interp.rs:734-812): the VM's guards,
+// in its order and with its messages, then the dispatch on B's dtype. The
+// guards run before any device work, so a refused call changes nothing.
+int op_gemm(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot* b, const vmlm_slot* scale,
+            bool dev, void* stream) {
+  if (!d || !a || !b) return fail(VMLM_ERR_ARG, "op_gemm: null slot");
+  const size_t m = a->rows, k = a->cols, b_rows = b->rows, b_cols = b->cols;
+  const bool nt = (fl & VMLM_FL_TRANS_B) == 0;
+  const bool acc = (fl & VMLM_FL_ACC) != 0;
+  auto refuse = [](const char* msg) { return fail(VMLM_ERR_OPERATOR, "%s", msg); };
+  // bounds the reference leaves unchecked (it would read or write past a slot)
+  auto bounds = [&](size_t n, size_t kb) -> int {
+    if (a->dtype != VMLM_DT_F32 || d->dtype != VMLM_DT_F32) return refuse("gemm: activations and output must be f32");
+    if (kb != k) return refuse("gemm: K of B differs from cols(A)");
+    if (d->rows * d->cols < m * n) return refuse("gemm: output slot smaller than M x N");
+    return VMLM_OK;
+  };
+  if (b->dtype == VMLM_DT_BF16) {
+    if (!nt) return refuse("bf16 NN gemm unimplemented");
+    if (acc) return refuse("bf16 acc gemm unimplemented");
+    VMLM_TRY(bounds(b_rows, b_cols));
+    const float* pa = static_cast<const float*>(a->ptr);
+    const uint16_t* pb = static_cast<const uint16_t*>(b->ptr);
+    float* pc = static_cast<float*>(d->ptr);
+    return dev ? vmlm_gemm_nt_bf16_dev(pa, pb, pc, m, b_rows, k, stream) : vmlm_gemm_nt_bf16(pa, pb, pc, m, b_rows, k);
+  }
+  if (b->dtype == VMLM_DT_I8) {
+    if (!nt) return refuse("int8 NN gemm unimplemented");
+    if (acc) return refuse("int8 acc gemm unimplemented");
+    if (!scale || scale->dtype != VMLM_DT_F32) return refuse("int8 gemm: scale slot must be f32");
+    if (scale->rows * scale->cols < b_rows) return refuse("int8 gemm: scale shorter than N rows");
+    VMLM_TRY(bounds(b_rows, b_cols));
+    const float* pa = static_cast<const float*>(a->ptr);
+    const int8_t* pq = static_cast<const int8_t*>(b->ptr);
+    const float* ps = static_cast<const float*>(scale->ptr);
+    float* pc = static_cast<float*>(d->ptr);
+    return dev ? vmlm_gemm_nt_int8_dev(pa, pq, ps, pc, m, b_rows, k, stream)
+               : vmlm_gemm_nt_int8(pa, pq, ps, pc, m, b_rows, k);
+  }
+  if (b->dtype != VMLM_DT_F32) return refuse("gemm operand dtype unsupported");
+  const float* pa = static_cast<const float*>(a->ptr);
+  const float* pb = static_cast<const float*>(b->ptr);
+  float* pc = static_cast<float*>(d->ptr);
+  if (nt) {
+    VMLM_TRY(bounds(b_rows, b_cols));
+    return dev ? vmlm_gemm_nt_f32_dev(pa, pb, pc, m, b_rows, k, acc, stream)
+               : vmlm_gemm_nt_f32(pa, pb, pc, m, b_rows, k, acc);
+  }
+  VMLM_TRY(bounds(b_cols, b_rows));
+  return dev ? vmlm_gemm_f32_dev(pa, pb, pc, m, b_cols, k, acc, stream) : vmlm_gemm_f32(pa, pb, pc, m, b_cols, k, acc);
+}
+
 }  // namespace
 
 // =================================================================== C ABI
@@ -1261,6 +1313,15 @@ int vmlm_gemm_i8i8_dev(const int8_t* x, const int8_t* w, const float* scale, flo
   VMLM_TRY(current_ctx(&ctx));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_i8i8(ctx, x, w, scale, c, acc, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_op_gemm(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot* b, const vmlm_slot* scale) {
+  return op_gemm(fl, d, a, b, scale, false, nullptr);
+}
+
+int vmlm_op_gemm_dev(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot* b, const vmlm_slot* scale,
+                     void* stream) {
+  return op_gemm(fl, d, a, b, scale, true, stream);
 }
 
 int vmlm_trace_enable(int max_ctas) {

@@ -212,6 +212,48 @@ def gemm_f32_dev(a, b, c, m, n, k, acc=False, stream=None) -> None:
         _dev_ptr(c, "float32", m * n, "c"), m, n, k, int(bool(acc)), _stream_ptr(stream)))
 
 
+# ------------------------------------------------------ the OP_GEMM operator
+
+DT_F32, DT_F16, DT_I8, DT_I32, DT_BF16 = 0, 1, 2, 3, 4  # core/src/format.rs:73-79
+FL_ACC, FL_TRANS_B = 1, 2                                # trans/src/opcode.rs:303-304
+_NP_DT = {"float32": DT_F32, "float16": DT_F16, "int8": DT_I8, "int32": DT_I32, "uint16": DT_BF16}
+
+
+def slot(x, dtype=None):
+    """A VM slot over a 2-D numpy array or CUDA tensor (uint16 / bfloat16 / int16 data is bf16)."""
+    from ._lib import Slot
+    if x is None:
+        return None
+    rows, cols = x.shape
+    if isinstance(x, np.ndarray):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("slot: must be C-contiguous")
+        ptr, dt = x.ctypes.data, _NP_DT.get(x.dtype.name, -1)
+    else:
+        if not x.is_contiguous():
+            raise ValueError("slot: must be contiguous")
+        name = str(x.dtype)[6:]
+        ptr, dt = x.data_ptr(), DT_BF16 if name in ("bfloat16", "int16") else _NP_DT.get(name, -1)
+    return Slot(ptr, rows, cols, dt if dtype is None else dtype)
+
+
+def _slot_ref(s):
+    return ctypes.byref(s) if s is not None else None
+
+
+def op_gemm(fl, d, a, b, scale=None) -> None:
+    """The VM's OP_GEMM (core/src/interp.rs:734-812) on host arrays: d = a . op(b) (+ d with FL_ACC)."""
+    sd, sa, sb, ss = slot(d), slot(a), slot(b), slot(scale)
+    check(lib().vmlm_op_gemm(fl, _slot_ref(sd), _slot_ref(sa), _slot_ref(sb), _slot_ref(ss)))
+
+
+def op_gemm_dev(fl, d, a, b, scale=None, stream=None) -> None:
+    """OP_GEMM on CUDA tensors, on `stream`."""
+    sd, sa, sb, ss = slot(d), slot(a), slot(b), slot(scale)
+    check(lib().vmlm_op_gemm_dev(fl, _slot_ref(sd), _slot_ref(sa), _slot_ref(sb), _slot_ref(ss),
+                                 _stream_ptr(stream)))
+
+
 # ---------------------------------------------------------- conveniences
 
 def q8_linear(x: np.ndarray, q: np.ndarray, scale: np.ndarray) -> np.ndarray:
