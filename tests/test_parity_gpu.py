@@ -415,3 +415,12 @@ def test_i8i8_cta_pairs_bit_exact(kernels, oracle, m, n, k):
 def test_bf16_cta_pairs(kernels, oracle, m, n, k, exact):
     x, w = bf16_case(oracle, m, n, k, seed=83, exact_x=exact)
     check_bf16(kernels, oracle, x, w)
+
+
+@pytest.mark.parametrize("m,n,k,exact", [(512, 2304, 2304, True), (512, 2304, 2304, False), (256, 4096, 1024, True),
+                                         (600, 3000, 520, True), (384, 2304, 2304, False)])
+def test_bf16_prefill_k_split_shapes(kernels, oracle, m, n, k, exact):
+    # prefill shapes whose tiles are split over K across a cluster (partials
+    # exchanged through distributed shared memory), general and bf16-valued X
+    x, w = bf16_case(oracle, m, n, k, seed=m + k, exact_x=exact)
+    check_bf16(kernels, oracle, x, w)
