@@ -342,26 +342,42 @@ __global__ void __launch_bounds__(kNormPrepThreads) f32_terms_nt_kernel(
                          tb + static_cast<long long>(r - M) * 3 * kp, dirty_b + (r - M), nf_b + (r - M), or_b, redi);
 }
 
-// Split terms of the B operand of the NN f32 GEMM C = A . B (B [K][N],
-// row-major), transposed: out[n*3*kp + j*kp + k], columns [K, kp) zero,
-// kp % 64 == 0. A CTA splits a 64 (k) x 64 (n) tile through shared memory
-// (loads coalesced along n, stores along k). nf[n] (zeroed by the caller)
-// becomes 1 for a column of B holding NaN / Inf; each CTA ORs its term flags
-// (2 / 4, 256 for NaN / Inf) into *orword; CTA (0, 0) clears *orword_next.
+// Split terms of both operands of the NN f32 GEMM C = A . B (A [M][K], B
+// [K][N], row-major) in one launch of kNormPrepThreads-thread CTAs.
+//  - CTAs [0, ntx * nty) split B transposed: out_b[n*3*kp + j*kp + k],
+//    columns [K, kp) zero, kp % 64 == 0; CTA (tx, ty) takes the 64 (k) x 64
+//    (n) tile (ty, tx) through shared memory (loads coalesced along n, stores
+//    along k). nf_b[n] becomes 1 for a column holding NaN / Inf (nf_b is
+//    cleared by the previous NN call; CTAs with ty == 0 clear their columns of
+//    nf_b_next for the next one); the tiles OR their term flags into *or_b.
+//  - CTAs [ntx * nty, + M) split the rows of A as f32_terms_nt_kernel does.
+// CTA 0 clears both next flag words.
 constexpr int kTransTile = 64;
-__global__ void __launch_bounds__(256) f32_terms_t_kernel(const float* __restrict__ b, long long ldb, int K, int N,
-                                                          int kp, uint16_t* __restrict__ out, int* __restrict__ nf,
-                                                          unsigned* __restrict__ orword,
-                                                          unsigned* __restrict__ orword_next) {
+__global__ void __launch_bounds__(kNormPrepThreads) f32_terms_nn_kernel(
+    const float* __restrict__ a, long long lda, int M, int vec_a, const float* __restrict__ b, long long ldb, int N,
+    int K, int kp, int ntx, int nty, uint16_t* __restrict__ ta, uint16_t* __restrict__ tb,
+    uint8_t* __restrict__ dirty_a, int* __restrict__ nf_a, int* __restrict__ nf_b, int* __restrict__ nf_b_next,
+    unsigned* __restrict__ or_a, unsigned* __restrict__ or_a_next, unsigned* __restrict__ or_b,
+    unsigned* __restrict__ or_b_next) {
   pdl_launch_dependents();
   __shared__ float tile[kTransTile][kTransTile + 1];
-  __shared__ int cta_flags;
-  const int n0 = blockIdx.x * kTransTile, k0 = blockIdx.y * kTransTile;
-  if (threadIdx.x == 0) {
-    cta_flags = 0;
-    if (blockIdx.x == 0 && blockIdx.y == 0) *orword_next = 0u;
+  __shared__ int redi[32];
+  const int cta = blockIdx.x;
+  if (cta == 0 && threadIdx.x == 0) {
+    *or_a_next = 0u;
+    *or_b_next = 0u;
   }
-  for (int i = threadIdx.x; i < kTransTile * kTransTile; i += 256) {
+  if (cta >= ntx * nty) {
+    const int r = cta - ntx * nty;
+    if (r < M)
+      norm_terms_row<true>(a + static_cast<long long>(r) * lda, K, kp, vec_a, ta + static_cast<long long>(r) * 3 * kp,
+                           dirty_a + r, nf_a + r, or_a, redi);
+    return;
+  }
+  const int tx = cta % ntx, ty = cta / ntx;
+  const int n0 = tx * kTransTile, k0 = ty * kTransTile;
+  if (ty == 0 && threadIdx.x < kTransTile && n0 + static_cast<int>(threadIdx.x) < N) nf_b_next[n0 + threadIdx.x] = 0;
+  for (int i = threadIdx.x; i < kTransTile * kTransTile; i += kNormPrepThreads) {
     const int kk = i / kTransTile, nn = i - kk * kTransTile;
     const int k = k0 + kk, n = n0 + nn;
     tile[kk][nn] = (k < K && n < N) ? b[static_cast<long long>(k) * ldb + n] : 0.f;
@@ -369,24 +385,23 @@ __global__ void __launch_bounds__(256) f32_terms_t_kernel(const float* __restric
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int my_flags = 0;
-  for (int nn = warp; nn < kTransTile; nn += 8) {
+  for (int nn = warp; nn < kTransTile; nn += kNormPrepThreads / 32) {
     const int n = n0 + nn;
     if (n >= N) break;
     int f = 0;
     uint16_t h0, m0, l0, h1, m1, l1;
     bf16_split(tile[2 * lane][nn], h0, m0, l0, f);
     bf16_split(tile[2 * lane + 1][nn], h1, m1, l1, f);
-    uint32_t* o = reinterpret_cast<uint32_t*>(out + static_cast<long long>(n) * 3 * kp + k0) + lane;
+    uint32_t* o = reinterpret_cast<uint32_t*>(tb + static_cast<long long>(n) * 3 * kp + k0) + lane;
     o[0] = h0 | (static_cast<uint32_t>(h1) << 16);
     o[kp / 2] = m0 | (static_cast<uint32_t>(m1) << 16);
     o[kp] = l0 | (static_cast<uint32_t>(l1) << 16);
     f = warp_or(f);
-    if (lane == 0 && (f & 256)) atomicOr(nf + n, 1);
+    if (lane == 0 && (f & 256)) atomicOr(nf_b + n, 1);
     my_flags |= f;
   }
-  if (lane == 0 && my_flags) atomicOr(&cta_flags, my_flags);
-  __syncthreads();
-  if (threadIdx.x == 0 && cta_flags) atomicOr(orword, static_cast<unsigned>(cta_flags));
+  my_flags = block_or(my_flags, redi);
+  if (threadIdx.x == 0 && my_flags) atomicOr(or_b, static_cast<unsigned>(my_flags));
 }
 
 // One CTA per token. Layout 0 (swap): out[(3t+j)*kp + k]. Layout 1 (normal):

@@ -96,6 +96,8 @@ struct Ctx {
   // f32 GEMM: term planes, dirty bits and NaN/Inf flags of both operands, and
   // their term-flag words (two per operand, used by alternate calls)
   DevBuf f32_ta, f32_tb, f32_da, f32_db, f32_nfa, f32_nfb, f32_flags;
+  DevBuf f32_nft;            // NN calls: B's NaN/Inf column flags, two arrays used by alternate calls
+  unsigned f32_nft_par = 0;
   int f32_m = -1, f32_n = -1, f32_kp = -1;
   bool f32_b_from_t = false;  // B's planes were last written by the transposing kernel
   unsigned f32_parity = 0;
@@ -820,6 +822,8 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
     VMLM_TRY(ensure(c->f32_db, static_cast<size_t>(N)));
     VMLM_TRY(ensure(c->f32_nfa, static_cast<size_t>(M) * 4));
     VMLM_TRY(ensure(c->f32_nfb, static_cast<size_t>(N) * 4));
+    VMLM_TRY(ensure(c->f32_nft, static_cast<size_t>(N) * 8));
+    VMLM_CUDA(cudaMemsetAsync(c->f32_nft.p, 0, static_cast<size_t>(N) * 8, st));
     VMLM_CUDA(cudaMemsetAsync(c->f32_ta.p, 0, ta_bytes, st));
     VMLM_CUDA(cudaMemsetAsync(c->f32_tb.p, 0, tb_bytes, st));
     VMLM_CUDA(cudaMemsetAsync(c->f32_da.p, 0, static_cast<size_t>(M), st));
@@ -845,17 +849,17 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
   int* nfb = static_cast<int*>(c->f32_nfb.p);
   const int vec_a = (K % 4 == 0) && aligned16(a);
   if (nn) {
-    // B^T's terms by the transposing kernel (every plane written), then A's;
-    // neither launch overlaps its predecessor, so the GEMM's wait for the
-    // previous kernel covers both
-    VMLM_CUDA(cudaMemsetAsync(nfb, 0, static_cast<size_t>(N) * 4, st));
-    VMLM_TRY(launch(f32_terms_t_kernel, dim3(static_cast<unsigned>(cdiv(N, kTransTile)),
-                                             static_cast<unsigned>(kp / kTransTile)),
-                    dim3(256), 0, st, false, b, static_cast<long long>(N), K, N, kp, tb, nfb, or_b, or_b_next));
+    // B^T's terms (every plane written, transposed through shared memory) and
+    // A's in one launch; B's NaN/Inf column flags alternate between two arrays
+    int* nft = static_cast<int*>(c->f32_nft.p);
+    nfb = nft + static_cast<size_t>(N) * c->f32_nft_par;
+    int* nfb_next = nft + static_cast<size_t>(N) * (c->f32_nft_par ^ 1u);
+    c->f32_nft_par ^= 1u;
+    const int ntx = static_cast<int>(cdiv(N, kTransTile)), nty = kp / kTransTile;
+    VMLM_TRY(launch(f32_terms_nn_kernel, dim3(static_cast<unsigned>(ntx * nty + M)), dim3(kNormPrepThreads), 0, st,
+                    false, a, static_cast<long long>(K), M, vec_a, b, static_cast<long long>(N), N, K, kp, ntx, nty,
+                    ta, tb, da, nfa, nfb, nfb_next, or_a, or_a_next, or_b, or_b_next));
     c->f32_b_from_t = true;
-    VMLM_TRY(launch(f32_terms_nt_kernel, dim3(static_cast<unsigned>(M)), dim3(kNormPrepThreads), 0, st, false, a,
-                    static_cast<long long>(K), M, vec_a, static_cast<const float*>(nullptr), 0ll, 0, 0, K, kp, ta,
-                    tb, da, db, nfa, nfb, or_a, or_a_next, or_b, or_b_next));
   } else {
     if (c->f32_b_from_t) {
       // the transposing kernel wrote every plane of B: rewrite them all once
@@ -1155,7 +1159,7 @@ int vmlm_shutdown(void) {
     cudaStreamSynchronize(c->stream);
     for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->shard_done, &c->sync, &c->norm_terms,
                       &c->norm_dirty, &c->norm_flags, &c->f32_ta, &c->f32_tb, &c->f32_da, &c->f32_db, &c->f32_nfa,
-                      &c->f32_nfb, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b})
+                      &c->f32_nfb, &c->f32_nft, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
