@@ -55,6 +55,11 @@ struct DecParams {
   int stages;    // W stage ring depth
   int tmem_cols;
   int vec_x;     // x rows allow float4 loads
+  // planes mode: the digit planes, exponents and non-finite flags come from
+  // q8_planes_kernel (tmP maps its [3m][kp] planes) instead of being made here
+  int planes_mode;
+  const int* exps;
+  const int* nonfinite;
   const float* x;
   long long ldx;
   const int8_t* w;
@@ -120,7 +125,8 @@ __device__ __forceinline__ float dec_nonfinite_dot(const DecParams& p, int t, in
 }
 
 __global__ void __launch_bounds__(kDecThreads, 1)
-    q8_decode_kernel(const __grid_constant__ CUtensorMap tmW, const DecParams p) {
+    q8_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmP,
+                     const DecParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -162,7 +168,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   float4 keep[kDecRegChunks];
   if (warp >= 2) {
     pdl_wait_prior();
-    dec_load_batch(p, keep, 0, et, k_lo, qpt, nq, nsteps, vec);
+    if (!p.planes_mode) dec_load_batch(p, keep, 0, et, k_lo, qpt, nq, nsteps, vec);
   }
 
   if (threadIdx.x == 0) {
@@ -258,94 +264,113 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
   } else {
     // ----------------------------------- digit planes, then the epilogue
-    // pass 1: per-token max |x| and non-finite flag over this CTA's range, in
-    // batches of kDecRegChunks chunks per thread whose loads are all in flight
-    // before any is reduced; the first batch stays in registers for pass 2.
-    // 32 consecutive chunks never straddle a token (qpt % 32 == 0).
-    for (int s0 = 0; s0 < nsteps; s0 += kDecRegChunks) {
-      if (s0 > 0) dec_load_batch(p, keep, s0, et, k_lo, qpt, nq, nsteps, vec);  // batch 0 is in flight
-      #pragma unroll
-      for (int r = 0; r < kDecRegChunks; ++r) {
-        const int qi = et + (s0 + r) * kDecEpiThreads;
-        if (s0 + r >= nsteps || qi - lane >= nq) break;  // warp-uniform
-        const float4 v = keep[r];
-        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        int bad = !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
-        mx = warp_max(mx);
-        bad = warp_or(bad);
-        if (lane == 0) {
-          const int t = (qi - lane) / qpt;
-          atomicMax(s_max + t, __float_as_int(mx));
-          if (bad) atomicOr(s_bad + t, 1);
-        }
+    if (p.planes_mode) {
+      // The planes come from q8_planes_kernel, the previous kernel in the
+      // stream (waited for above): one TMA load per k-block of this CTA's
+      // range, in the layout pass 2 below writes (128-byte swizzle, rows
+      // past 3m read as zero), and the per-token exponents and flags.
+      if (et == 0) {
+        mbar_arrive_expect_tx(planes_bar, static_cast<uint32_t>(nkb * p.rows_b * kBlockBytes));
+        for (int j = 0; j < nkb; ++j)
+          tma_load_2d(smem + L.b_off + j * p.rows_b * kBlockBytes, &tmP, planes_bar, (kb0 + j) * kBlockBytes, 0,
+                      policy_evict_last());
+        if (trace) trace[1] = globaltimer();
       }
-    }
-    const bool kept = nsteps <= kDecRegChunks;  // else pass 2 reloads (L2 hits)
-    named_bar_sync(1, kDecEpiThreads);
-    if (et < p.m) {
-      int e = 0;
-      const float amax = __int_as_float(s_max[et]);
-      if (!s_bad[et] && amax > 0.f) {
-        int E;
-        frexpf(amax, &E);
-        e = 22 - E;
+      if (et < p.m) {
+        s_exp[et] = __ldg(p.exps + et);
+        s_bad[et] = __ldg(p.nonfinite + et);
       }
-      s_exp[et] = e;
-    }
-    named_bar_sync(1, kDecEpiThreads);
-    // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte
-    // rows), in groups of kDecGroup chunks per thread: taken from the kept
-    // batch when the range fits it, else loaded again (L2 hits) with the
-    // group's loads in flight together. The loop stays rolled: its body is
-    // the hot code of this phase and must stay small in the instruction cache.
-    uint8_t* planes = smem + L.b_off;
-    #pragma unroll 1
-    for (int s0 = 0; s0 < nsteps; s0 += kDecGroup) {
-      float4 g[kDecGroup];
-      #pragma unroll
-      for (int i = 0; i < kDecGroup; ++i) {
-        const int s = s0 + i;
-        const int qi = et + s * kDecEpiThreads;
-        g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kept) {
-          #pragma unroll
-          for (int r = 0; r < kDecRegChunks; ++r)
-            if (r == s) g[i] = keep[r];
-        } else if (s < nsteps && qi < nq) {
-          const int t = qi / qpt;
-          const int k = k_lo + (qi - t * qpt) * 4;
-          if (k < p.k) g[i] = dec_load4(p.x + static_cast<long long>(t) * p.ldx + k, vec);
-        }
-      }
-      #pragma unroll
-      for (int i = 0; i < kDecGroup; ++i) {
-        const int qi = et + (s0 + i) * kDecEpiThreads;
-        if (s0 + i >= nsteps || qi >= nq) break;
-        const int t = qi / qpt;
-        const int kk = (qi - t * qpt) * 4;  // offset in this CTA's range
-        const float4 v = s_bad[t] ? make_float4(0.f, 0.f, 0.f, 0.f) : g[i];
-        const int e = s_exp[t];
-        int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
-        q8_digits(v.x, e, a0, a1, a2);
-        q8_digits(v.y, e, b0, b1, b2);
-        q8_digits(v.z, e, c0, c1, c2);
-        q8_digits(v.w, e, f0, f1, f2);
-        const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
-        const int j = kk >> 7, b = kk & 127;
-        uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+      named_bar_sync(1, kDecEpiThreads);
+    } else {
+      // pass 1: per-token max |x| and non-finite flag over this CTA's range, in
+      // batches of kDecRegChunks chunks per thread whose loads are all in flight
+      // before any is reduced; the first batch stays in registers for pass 2.
+      // 32 consecutive chunks never straddle a token (qpt % 32 == 0).
+      for (int s0 = 0; s0 < nsteps; s0 += kDecRegChunks) {
+        if (s0 > 0) dec_load_batch(p, keep, s0, et, k_lo, qpt, nq, nsteps, vec);  // batch 0 is in flight
         #pragma unroll
-        for (int pl = 0; pl < 3; ++pl) {
-          const int row = 3 * t + pl;
-          *reinterpret_cast<uint32_t*>(blk + row * kBlockBytes + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))) =
-              w3[pl];
+        for (int r = 0; r < kDecRegChunks; ++r) {
+          const int qi = et + (s0 + r) * kDecEpiThreads;
+          if (s0 + r >= nsteps || qi - lane >= nq) break;  // warp-uniform
+          const float4 v = keep[r];
+          float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+          int bad = !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+          mx = warp_max(mx);
+          bad = warp_or(bad);
+          if (lane == 0) {
+            const int t = (qi - lane) / qpt;
+            atomicMax(s_max + t, __float_as_int(mx));
+            if (bad) atomicOr(s_bad + t, 1);
+          }
         }
       }
-    }
-    fence_proxy_async_smem();
-    named_bar_sync(1, kDecEpiThreads);
-    if (et == 0) {
-      mbar_arrive(planes_bar);
-      if (trace) trace[1] = globaltimer();
+      const bool kept = nsteps <= kDecRegChunks;  // else pass 2 reloads (L2 hits)
+      named_bar_sync(1, kDecEpiThreads);
+      if (et < p.m) {
+        int e = 0;
+        const float amax = __int_as_float(s_max[et]);
+        if (!s_bad[et] && amax > 0.f) {
+          int E;
+          frexpf(amax, &E);
+          e = 22 - E;
+        }
+        s_exp[et] = e;
+      }
+      named_bar_sync(1, kDecEpiThreads);
+      // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte
+      // rows), in groups of kDecGroup chunks per thread: taken from the kept
+      // batch when the range fits it, else loaded again (L2 hits) with the
+      // group's loads in flight together. The loop stays rolled: its body is
+      // the hot code of this phase and must stay small in the instruction cache.
+      uint8_t* planes = smem + L.b_off;
+      #pragma unroll 1
+      for (int s0 = 0; s0 < nsteps; s0 += kDecGroup) {
+        float4 g[kDecGroup];
+        #pragma unroll
+        for (int i = 0; i < kDecGroup; ++i) {
+          const int s = s0 + i;
+          const int qi = et + s * kDecEpiThreads;
+          g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (kept) {
+            #pragma unroll
+            for (int r = 0; r < kDecRegChunks; ++r)
+              if (r == s) g[i] = keep[r];
+          } else if (s < nsteps && qi < nq) {
+            const int t = qi / qpt;
+            const int k = k_lo + (qi - t * qpt) * 4;
+            if (k < p.k) g[i] = dec_load4(p.x + static_cast<long long>(t) * p.ldx + k, vec);
+          }
+        }
+        #pragma unroll
+        for (int i = 0; i < kDecGroup; ++i) {
+          const int qi = et + (s0 + i) * kDecEpiThreads;
+          if (s0 + i >= nsteps || qi >= nq) break;
+          const int t = qi / qpt;
+          const int kk = (qi - t * qpt) * 4;  // offset in this CTA's range
+          const float4 v = s_bad[t] ? make_float4(0.f, 0.f, 0.f, 0.f) : g[i];
+          const int e = s_exp[t];
+          int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
+          q8_digits(v.x, e, a0, a1, a2);
+          q8_digits(v.y, e, b0, b1, b2);
+          q8_digits(v.z, e, c0, c1, c2);
+          q8_digits(v.w, e, f0, f1, f2);
+          const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
+          const int j = kk >> 7, b = kk & 127;
+          uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+          #pragma unroll
+          for (int pl = 0; pl < 3; ++pl) {
+            const int row = 3 * t + pl;
+            *reinterpret_cast<uint32_t*>(blk + row * kBlockBytes + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))) =
+                w3[pl];
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, kDecEpiThreads);
+      if (et == 0) {
+        mbar_arrive(planes_bar);
+        if (trace) trace[1] = globaltimer();
+      }
     }
 
     // ------------------------------------------------------------ epilogue
@@ -442,6 +467,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         p.out[static_cast<long long>(t) * p.ldo + nn] = r;
       }
     }
+    // planes mode after an abort: the planes copy must land before this
+    // CTA's shared memory is released
+    if (p.planes_mode && et == 0 && *abort_flag) mbar_wait(planes_bar, 0, nullptr, abort_flag, kDevTimeoutDrain, false);
     if (trace && et == 0) trace[6] = globaltimer();
   }
 

@@ -547,7 +547,7 @@ int max_active_clusters(Ctx* ctx, int cl, uint32_t smem, int* out) {
   return VMLM_OK;
 }
 
-int plan_decode(Ctx* ctx, int M, int N, int K, DecPlan* plan) {
+int plan_decode(Ctx* ctx, int M, int N, int K, bool planes_mode, DecPlan* plan) {
   *plan = DecPlan{};
   if (M < 1 || M > kDecMaxTok) return VMLM_OK;
   const long long tiles = cdiv(N, kTileRows);
@@ -556,11 +556,11 @@ int plan_decode(Ctx* ctx, int M, int N, int K, DecPlan* plan) {
   long long best_ctas = 0;
   for (int c = 1; c <= kDecMaxCluster && c <= kb; ++c) {
     const int kbr = static_cast<int>(cdiv(kb, c));
-    // A CTA's x slice must fit one register batch of the plane warps: a
-    // second batch and the reloads of the digit pass queue behind the weight
-    // stream (at M = 32 the persistent swap-mode GEMM is then faster).
-    // (float4 chunks of x per k-block: kBlockBytes / 4)
-    if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
+    // Making the planes here: a CTA's x slice must fit one register batch of
+    // the plane warps; a second batch and the reloads of the digit pass queue
+    // behind the weight stream (float4 chunks of x per k-block: kBlockBytes / 4).
+    if (!planes_mode &&
+        static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
       continue;
     int stages = kbr < 16 ? kbr : 16;
     while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
@@ -577,8 +577,10 @@ int plan_decode(Ctx* ctx, int M, int N, int K, DecPlan* plan) {
   return VMLM_OK;
 }
 
+// planes != nullptr: planes mode (q8_planes_kernel's planes [3M][kp], exps, nonfinite).
 int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
-               cudaStream_t st, const DecPlan& plan) {
+               cudaStream_t st, const DecPlan& plan, const int8_t* planes = nullptr, int kp = 0,
+               const int* exps = nullptr, const int* nonf = nullptr) {
   DecParams p = {};
   p.n = N;
   p.k = K;
@@ -599,12 +601,20 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   p.err = ctx->err;
   const long long grid = cdiv(N, kTileRows) * plan.c;
   p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
-  CUtensorMap mw;
+  p.planes_mode = planes ? 1 : 0;
+  p.exps = exps;
+  p.nonfinite = nonf;
+  CUtensorMap mw, mp;
   VMLM_TRY(make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+  if (planes)
+    VMLM_TRY(make_map(&mp, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128,
+                      static_cast<uint32_t>(p.rows_b)));
+  else
+    mp = mw;  // unused
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   VMLM_TRY(launch_ex(q8_decode_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), plan.smem, st, true,
-                     plan.c, mw, p));
+                     plan.c, mw, mp, p));
   if (g_profile) VMLM_TRY(prof_end(st, pp));
   return VMLM_OK;
 }
@@ -679,9 +689,10 @@ int shard_setup(Ctx* ctx, float* const* c_peers, unsigned* const* inbox_peers, i
 
 int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
            cudaStream_t st, const Shard* sh = nullptr) {
-  if (!sh && K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q)) {
+  const bool dec_ok = !sh && K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
+  if (dec_ok) {
     DecPlan dp;
-    VMLM_TRY(plan_decode(c, M, N, K, &dp));
+    VMLM_TRY(plan_decode(c, M, N, K, false, &dp));
     if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp);
   }
   const int kp = static_cast<int>(cdiv(K, 16) * 16);
@@ -692,6 +703,13 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   int* nonf = exps + M;
   VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
                   kp, planes, exps, nonf));
+  if (dec_ok) {
+    // x slices too large for the decode kernel's own digit pass: the same
+    // kernel on the planes just made (one wave of clusters)
+    DecPlan dp;
+    VMLM_TRY(plan_decode(c, M, N, K, true, &dp));
+    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp, planes, kp, exps, nonf);
+  }
   const bool tc_ok = K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
   if (!tc_ok) {
     const long long warps = static_cast<long long>(M) * N;
