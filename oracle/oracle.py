@@ -42,6 +42,8 @@ def lib() -> ctypes.CDLL:
             "oracle_gemm_i8i8_par": [P, P, P, P, P, S, S, S, I],
             "oracle_gemm_nt_f32_par": [P, P, P, S, S, S, I, I],
             "oracle_gemm_f32_par": [P, P, P, S, S, S, I, I],
+            "oracle_rmsnorm": [P, P, P, S, S, F],
+            "oracle_gemv_f32": [P, P, P, S, S],
             "oracle_fill_uniform": [P, S, U64, F, I],
             "oracle_fill_normal": [P, S, U64, F, I],
             "oracle_fill_gauss_ref": [P, S, U64, F, I],
@@ -54,6 +56,8 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = None
+        L.oracle_emb.argtypes = [P, I, S, S, P, S, P]
+        L.oracle_emb.restype = I
         L.oracle_max_rel_err.argtypes = [P, P, S]
         L.oracle_max_rel_err.restype = ctypes.c_double
         _lib = L
@@ -143,6 +147,37 @@ def gemm_f32(a, b, c=None, nt=1):
     out = np.array(c, np.float32, order="C", copy=True) if c is not None else np.empty((m, n), np.float32)
     lib().oracle_gemm_f32_par(_p(a), _p(b), _p(out), m, n, k, int(c is not None), _threads(nt))
     return out
+
+
+def rmsnorm(x, g, eps):
+    """ops/src/kernels.rs:1346-1370: per row x * (1 / sqrt(mean(x^2) + eps)) * g."""
+    x = np.ascontiguousarray(x, np.float32)
+    g = np.ascontiguousarray(g, np.float32)
+    rows, cols = x.shape
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm(_p(out), _p(x), _p(g), rows, cols, float(eps))
+    return out
+
+
+def gemv_f32(a, b):
+    """core/src/interp.rs:815-827 (OP_GEMV): c[i] = sum_p a[i, p] * b[p], sequential."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    c = np.empty(m, np.float32)
+    lib().oracle_gemv_f32(_p(a), _p(b), _p(c), m, k)
+    return c
+
+
+def emb(table, idx):
+    """core/src/interp.rs:1351-1420 (OP_EMB) for every index: (status, out); status 1 = row index out
+    of range, 2 = not an integer (where the VM exits 9)."""
+    rows, cols = table.shape
+    table = np.ascontiguousarray(table)
+    idx = np.ascontiguousarray(idx, np.float32)
+    out = np.zeros((idx.size, cols), np.float32)
+    st = lib().oracle_emb(_p(table), 4 if table.dtype == np.uint16 else 0, rows, cols, _p(idx), idx.size, _p(out))
+    return st, out
 
 
 def gemm_i8i8(x, w, scale, nt=1, want_acc=True):

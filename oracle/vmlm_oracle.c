@@ -24,6 +24,11 @@
  *                              then `s += c` when acc)
  *   oracle_gemm_f32_par        ops/src/kernels.rs:383-403 (gemm_scalar, the
  *                              whole of gemm NN at :407-419: B [k,n])
+ *   oracle_rmsnorm             ops/src/kernels.rs:1346-1370 (sqrt_f :1371-1376 is
+ *                              _mm_sqrt_ss: correctly rounded, as sqrtf)
+ *   oracle_gemv_f32            core/src/interp.rs:815-827 (OP_GEMV)
+ *   oracle_emb                 core/src/interp.rs:1351-1420 (OP_EMB: index
+ *                              checks, then the row widened or copied)
  *   parallel split             ops/src/par.rs:44-62 (chunk = ceil(n/nt) over N)
  *
  * The AVX2 bodies use the same intrinsic sequence as the reference, so the
@@ -248,6 +253,61 @@ static void gemm_f32_cols(int nn, const float *a, const float *b, float *c, size
             if (acc) s = s + c[i * n + j];
             c[i * n + j] = s;
         }
+}
+
+/* ------------------------------------------- decode-step neighbours */
+
+/* rmsnorm: per row, ss = sequential sum of v*v, ss /= cols, inv = 1 / sqrt(ss + eps),
+ * dst = src * inv * g (left to right). */
+EXPORT void oracle_rmsnorm(float *dst, const float *src, const float *g, size_t rows, size_t cols,
+                           float eps) {
+    for (size_t r = 0; r < rows; r++) {
+        const float *p = src + r * cols;
+        float *q = dst + r * cols;
+        float ss = 0.0f;
+        for (size_t i = 0; i < cols; i++) {
+            float v = p[i];
+            float sq = v * v;
+            ss = ss + sq;
+        }
+        ss = ss / (float)cols;
+        float inv = 1.0f / sqrtf(ss + eps);
+        for (size_t i = 0; i < cols; i++) {
+            float t = p[i] * inv;
+            q[i] = t * g[i];
+        }
+    }
+}
+
+/* OP_GEMV: c[i] = sequential sum over p of a[i*k + p] * b[p]. */
+EXPORT void oracle_gemv_f32(const float *a, const float *b, float *c, size_t m, size_t k) {
+    for (size_t i = 0; i < m; i++) {
+        float s = 0.0f;
+        for (size_t p = 0; p < k; p++) {
+            float prod = a[i * k + p] * b[p];
+            s = s + prod;
+        }
+        c[i] = s;
+    }
+}
+
+/* OP_EMB for m indices: 0 on success; 1 "row index out of range" (negative, NaN,
+ * >= rows); 2 "row index is not an integer". dtype 4: bf16 bits, widened; 0: f32. */
+EXPORT int oracle_emb(const void *table, int dtype, size_t rows, size_t cols, const float *idx,
+                      size_t m, float *out) {
+    for (size_t t = 0; t < m; t++) {
+        float rowf = idx[t];
+        if (!(rowf >= 0.0f) || rowf >= (float)rows) return 1;
+        size_t row = (size_t)rowf;
+        if ((float)row != rowf) return 2;
+        for (size_t i = 0; i < cols; i++) {
+            if (dtype == 4)
+                out[t * cols + i] = bf16_bits_to_f32(((const uint16_t *)table)[row * cols + i]);
+            else
+                out[t * cols + i] = ((const float *)table)[row * cols + i];
+        }
+    }
+    return 0;
 }
 
 /* ------------------------------------------------ ops/src/par.rs split */

@@ -61,6 +61,12 @@ SIGNATURES = {
     "vmlm_trace_enable": (I, [I]),
     "vmlm_trace_take": (I, [P, S]),
     "vmlm_op_gemm": (I, [ctypes.c_uint, SP, SP, SP, SP]),
+    "vmlm_rmsnorm_gemm_nt_int8": (I, [P, P, ctypes.c_float, P, P, P, S, S, S]),
+    "vmlm_rmsnorm_gemm_nt_int8_dev": (I, [P, P, ctypes.c_float, P, P, P, S, S, S, P]),
+    "vmlm_gemv_f32": (I, [P, P, P, S, S]),
+    "vmlm_gemv_f32_dev": (I, [P, P, P, S, S, P]),
+    "vmlm_emb": (I, [P, I, S, S, P, S, P]),
+    "vmlm_emb_dev": (I, [P, I, S, S, P, S, P, P]),
     "vmlm_op_gemm_dev": (I, [ctypes.c_uint, SP, SP, SP, SP, P]),
 }
 

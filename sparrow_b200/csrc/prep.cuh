@@ -173,6 +173,79 @@ __global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __
   }
 }
 
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = (l < static_cast<int>(blockDim.x >> 5)) ? red[l] : 0.f;
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// RMSNorm fused into the Q8 activation encoding (ops/src/kernels.rs:1346-1370,
+// then the planes of q8_planes_kernel). Per row t of src: ss = sum_k src_k^2
+// (f32, per-thread sums then a block tree; the reference sums sequentially),
+// inv = 1 / sqrt(ss / K + eps), x_k = (src_k * inv) * g_k as the reference
+// rounds them. The normalised rows go to xn ([M][K], for the exact recompute
+// of rows holding NaN / Inf), then the digit planes, exponent and flag of x
+// exactly as q8_planes_kernel makes them. One CTA per token.
+__global__ void __launch_bounds__(kPrepThreads) q8_norm_planes_kernel(
+    const float* __restrict__ src, long long lds, const float* __restrict__ g, float eps, int M, int K, int kp,
+    float* __restrict__ xn, int8_t* __restrict__ planes, int* __restrict__ exps, int* __restrict__ nonfinite) {
+  pdl_launch_dependents();
+  __shared__ float redf[32];
+  __shared__ int redi[32];
+  const int t = blockIdx.x;
+  if (t >= M) return;
+  const float* sr = src + static_cast<long long>(t) * lds;
+  float* xr = xn + static_cast<long long>(t) * K;
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = sr[k];
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  ss = block_sum(ss, redf);
+  const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+  float amax = 0.f;
+  int bad = 0;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float x = __fmul_rn(__fmul_rn(sr[k], inv), __ldg(g + k));
+    xr[k] = x;
+    bad |= !isfinite(x);
+    amax = fmaxf(amax, fabsf(x));
+  }
+  block_max_or(amax, bad, redf, redi);  // (its barrier also makes xr visible to the whole CTA)
+  int e = 0;
+  if (!bad && amax > 0.f) {
+    int E;
+    frexpf(amax, &E);
+    e = 22 - E;
+  }
+  uint32_t* p0 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t) * kp);
+  uint32_t* p1 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t + 1) * kp);
+  uint32_t* p2 = reinterpret_cast<uint32_t*>(planes + static_cast<long long>(3 * t + 2) * kp);
+  const int nchunk = (kp + 3) >> 2;
+  for (int ch = threadIdx.x; ch < nchunk; ch += blockDim.x) {
+    int d[3][4];
+    for (int j = 0; j < 4; ++j) {
+      const int k = ch * 4 + j;
+      const float v = (k < K && !bad) ? xr[k] : 0.f;
+      q8_digits(v, e, d[0][j], d[1][j], d[2][j]);
+    }
+    p0[ch] = pack4(d[0][0], d[0][1], d[0][2], d[0][3]);
+    p1[ch] = pack4(d[1][0], d[1][1], d[1][2], d[1][3]);
+    p2[ch] = pack4(d[2][0], d[2][1], d[2][2], d[2][3]);
+  }
+  if (threadIdx.x == 0) {
+    exps[t] = e;
+    nonfinite[t] = bad;
+  }
+}
+
 __device__ __forceinline__ uint16_t bf16_rn_bits(float v) {
   // Round to nearest even; a finite value that would round to infinity is
   // truncated instead so that hi stays finite and the residual stays exact.

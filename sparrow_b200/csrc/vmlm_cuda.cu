@@ -18,6 +18,7 @@
 #include "decode.cuh"
 #include "tc2_gemm.cuh"
 #include "tc_gemm.cuh"
+#include "vm_ops.cuh"
 
 using namespace vmlm;
 
@@ -103,7 +104,8 @@ struct Ctx {
   unsigned f32_parity = 0;
   int* err = nullptr;       // device error word
   int* err_host = nullptr;  // pinned copy read after host-API calls
-  DevBuf h_a, h_c, h_w, h_s, h_acc, h_b;  // host-API staging
+  DevBuf h_a, h_c, h_w, h_s, h_acc, h_b, h_g;  // host-API staging
+  DevBuf xn;  // RMSNorm-fused Q8 calls: the normalised activations [M][K]
   bool attrs_set = false;
   std::map<std::pair<int, uint32_t>, int> dec_clusters;  // (cluster size, smem) -> co-resident clusters
 };
@@ -687,10 +689,13 @@ int shard_setup(Ctx* ctx, float* const* c_peers, unsigned* const* inbox_peers, i
 
 // ------------------------------------------------------------- Q8 path
 
+// norm_g != nullptr: C = Q8 GEMM of rmsnorm(a) (gain norm_g, norm_eps): the
+// norm is fused into the activation encoding, and everything after it reads
+// the normalised rows.
 int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
-           cudaStream_t st, const Shard* sh = nullptr) {
+           cudaStream_t st, const Shard* sh = nullptr, const float* norm_g = nullptr, float norm_eps = 0.f) {
   const bool dec_ok = !sh && K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
-  if (dec_ok) {
+  if (dec_ok && !norm_g) {
     DecPlan dp;
     VMLM_TRY(plan_decode(c, M, N, K, false, &dp));
     if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp);
@@ -701,8 +706,16 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   int8_t* planes = static_cast<int8_t*>(c->act.p);
   int* exps = static_cast<int*>(c->small.p);
   int* nonf = exps + M;
-  VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
-                  kp, planes, exps, nonf));
+  if (norm_g) {
+    VMLM_TRY(ensure(c->xn, static_cast<size_t>(M) * (K ? K : 1) * 4));
+    float* xn = static_cast<float*>(c->xn.p);
+    VMLM_TRY(launch(q8_norm_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K),
+                    norm_g, norm_eps, M, K, kp, xn, planes, exps, nonf));
+    a = xn;
+  } else {
+    VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+                    kp, planes, exps, nonf));
+  }
   if (dec_ok) {
     // x slices too large for the decode kernel's own digit pass: the same
     // kernel on the planes just made (one wave of clusters)
@@ -1030,6 +1043,14 @@ int resolve(Ctx* c, const void* host, size_t bytes, DevBuf& stage, cudaStream_t 
   return VMLM_OK;
 }
 
+// The status for a non-zero device error word: the VM's OP_EMB messages, or a
+// kernel that gave up a bounded wait.
+int device_error(int code) {
+  if (code == kDevEmbRange) return fail(VMLM_ERR_OPERATOR, "EMB: row index out of range");
+  if (code == kDevEmbFraction) return fail(VMLM_ERR_OPERATOR, "EMB: row index is not an integer");
+  return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
+}
+
 int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, size_t acc_bytes) {
   if (host_c) VMLM_CUDA(cudaMemcpyAsync(host_c, c->h_c.p, c_bytes, cudaMemcpyDeviceToHost, c->stream));
   if (host_acc) VMLM_CUDA(cudaMemcpyAsync(host_acc, c->h_acc.p, acc_bytes, cudaMemcpyDeviceToHost, c->stream));
@@ -1044,7 +1065,7 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
     if (c->norm_flags.p) cudaMemset(c->norm_flags.p, 0, c->norm_flags.bytes);
     if (c->f32_flags.p) cudaMemset(c->f32_flags.p, 0, c->f32_flags.bytes);
     *c->err_host = 0;
-    return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
+    return device_error(code);
   }
   return VMLM_OK;
 }
@@ -1177,7 +1198,7 @@ int vmlm_shutdown(void) {
     cudaStreamSynchronize(c->stream);
     for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->shard_done, &c->sync, &c->norm_terms,
                       &c->norm_dirty, &c->norm_flags, &c->f32_ta, &c->f32_tb, &c->f32_da, &c->f32_db, &c->f32_nfa,
-                      &c->f32_nfb, &c->f32_nft, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b})
+                      &c->f32_nfb, &c->f32_nft, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b, &c->h_g, &c->xn})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
@@ -1335,6 +1356,139 @@ int vmlm_gemm_i8i8_dev(const int8_t* x, const int8_t* w, const float* scale, flo
   VMLM_TRY(current_ctx(&ctx));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_i8i8(ctx, x, w, scale, c, acc, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_rmsnorm_gemm_nt_int8(const float* a, const float* g, float eps, const int8_t* q, const float* scale,
+                              float* c, size_t m, size_t n, size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || !scale || (k > 0 && (!a || !q || !g))) return fail(VMLM_ERR_ARG, "rmsnorm_gemm_nt_int8: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *dq = nullptr, *ds = nullptr, *dg = nullptr;
+  VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+  VMLM_TRY(resolve(ctx, q, n * k, ctx->h_w, ctx->stream, &dq));
+  VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+  VMLM_TRY(resolve(ctx, g, k * 4, ctx->h_g, ctx->stream, &dg));
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  VMLM_TRY(run_q8(ctx, static_cast<const float*>(da), static_cast<const int8_t*>(dq), static_cast<const float*>(ds),
+                  static_cast<float*>(ctx->h_c.p), static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                  ctx->stream, nullptr, static_cast<const float*>(dg), eps));
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int vmlm_rmsnorm_gemm_nt_int8_dev(const float* a, const float* g, float eps, const int8_t* q, const float* scale,
+                                  float* c, size_t m, size_t n, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || !scale || (k > 0 && (!a || !q || !g))) return fail(VMLM_ERR_ARG, "rmsnorm_gemm_nt_int8_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_q8(ctx, a, q, scale, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), st, nullptr, g,
+                eps);
+}
+
+int vmlm_gemv_f32(const float* a, const float* b, float* c, size_t m, size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, 1, k));
+  if (m == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "gemv_f32: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *db = nullptr;
+  if (k > 0) {
+    VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_w, ctx->stream, &da));
+    VMLM_TRY(resolve(ctx, b, k * 4, ctx->h_a, ctx->stream, &db));
+  }
+  VMLM_TRY(ensure(ctx->h_c, m * 4));
+  VMLM_TRY(vmlm_gemv_f32_dev(static_cast<const float*>(da), static_cast<const float*>(db),
+                             static_cast<float*>(ctx->h_c.p), m, k, ctx->stream));
+  return finish_host_call(ctx, c, m * 4, nullptr, 0);
+}
+
+int vmlm_gemv_f32_dev(const float* a, const float* b, float* c, size_t m, size_t k, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, 1, k));
+  if (m == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !b))) return fail(VMLM_ERR_ARG, "gemv_f32_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  const int vec = (k % 4 == 0) && aligned16(a) && aligned16(b);
+  return launch(gemv_f32_kernel, dim3(static_cast<unsigned>(cdiv(static_cast<long long>(m), kGemvWarps))),
+                dim3(kGemvWarps * 32), 0, st, false, a, b, c, static_cast<int>(m), static_cast<int>(k), vec);
+}
+
+int vmlm_emb(const void* table, int dtype, size_t rows, size_t cols, const float* idx, size_t m, float* out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (dtype != VMLM_DT_BF16 && dtype != VMLM_DT_F32) return fail(VMLM_ERR_OPERATOR, "EMB: table dtype unsupported");
+  if (m == 0 || cols == 0) return VMLM_OK;
+  if (!table || !idx || !out) return fail(VMLM_ERR_ARG, "emb: null pointer");
+  if (cols >= (static_cast<size_t>(1) << 31)) return fail(VMLM_ERR_SHAPE, "emb: cols must be < 2^31");
+  // the VM's checks (core/src/interp.rs:1375-1397), before any device work
+  for (size_t t = 0; t < m; ++t) {
+    const float r = idx[t];
+    if (!(r >= 0.f) || r >= static_cast<float>(rows)) return fail(VMLM_ERR_OPERATOR, "EMB: row index out of range");
+    if (static_cast<float>(static_cast<long long>(r)) != r)
+      return fail(VMLM_ERR_OPERATOR, "EMB: row index is not an integer");
+  }
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const size_t esz = dtype == VMLM_DT_BF16 ? 2 : 4;
+  const size_t row_bytes = cols * esz;
+  const void* dtab = nullptr;
+  std::vector<float> didx(idx, idx + m);
+  const uintptr_t h = reinterpret_cast<uintptr_t>(table);
+  auto it = g_reg.upper_bound(h);
+  bool registered = false;
+  if (it != g_reg.begin()) {
+    --it;
+    if (it->second.dev == ctx->dev && h >= it->first && h + rows * row_bytes <= it->first + it->second.bytes) {
+      dtab = static_cast<const char*>(it->second.dptr) + (h - it->first);
+      registered = true;
+    }
+  }
+  if (!registered) {
+    // only the m rows the call reads go to the device, as rows 0..m-1
+    std::vector<char> rowsbuf(m * row_bytes);
+    for (size_t t = 0; t < m; ++t) {
+      std::memcpy(rowsbuf.data() + t * row_bytes,
+                  static_cast<const char*>(table) + static_cast<size_t>(idx[t]) * row_bytes, row_bytes);
+      didx[t] = static_cast<float>(t);
+    }
+    VMLM_TRY(ensure(ctx->h_w, rowsbuf.size()));
+    VMLM_CUDA(cudaMemcpyAsync(ctx->h_w.p, rowsbuf.data(), rowsbuf.size(), cudaMemcpyHostToDevice, ctx->stream));
+    VMLM_CUDA(cudaStreamSynchronize(ctx->stream));  // rowsbuf is pageable and goes out of scope
+    dtab = ctx->h_w.p;
+  }
+  VMLM_TRY(ensure(ctx->h_a, m * 4));
+  VMLM_CUDA(cudaMemcpyAsync(ctx->h_a.p, didx.data(), m * 4, cudaMemcpyHostToDevice, ctx->stream));
+  VMLM_TRY(ensure(ctx->h_c, m * cols * 4));
+  VMLM_TRY(launch(emb_kernel, dim3(static_cast<unsigned>(m), static_cast<unsigned>(cdiv(cols, 1024))), dim3(256), 0,
+                  ctx->stream, false, dtab, dtype, static_cast<long long>(registered ? rows : m),
+                  static_cast<int>(cols), static_cast<const float*>(ctx->h_a.p), static_cast<int>(m),
+                  static_cast<float*>(ctx->h_c.p), ctx->err));
+  VMLM_CUDA(cudaStreamSynchronize(ctx->stream));  // didx is pageable
+  return finish_host_call(ctx, out, m * cols * 4, nullptr, 0);
+}
+
+int vmlm_emb_dev(const void* table, int dtype, size_t rows, size_t cols, const float* idx, size_t m, float* out,
+                 void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (dtype != VMLM_DT_BF16 && dtype != VMLM_DT_F32) return fail(VMLM_ERR_OPERATOR, "EMB: table dtype unsupported");
+  if (m == 0 || cols == 0) return VMLM_OK;
+  if (!table || !idx || !out) return fail(VMLM_ERR_ARG, "emb_dev: null pointer");
+  if (cols >= (static_cast<size_t>(1) << 31) || m >= (static_cast<size_t>(1) << 31))
+    return fail(VMLM_ERR_SHAPE, "emb_dev: m and cols must be < 2^31");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return launch(emb_kernel, dim3(static_cast<unsigned>(m), static_cast<unsigned>(cdiv(cols, 1024))), dim3(256), 0, st,
+                false, table, dtype, static_cast<long long>(rows), static_cast<int>(cols), idx, static_cast<int>(m),
+                out, ctx->err);
 }
 
 int vmlm_op_gemm(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot* b, const vmlm_slot* scale) {
@@ -1519,7 +1673,7 @@ int vmlm_sync(void* stream) {
     if (ctx->sync.p) cudaMemset(ctx->sync.p, 0, ctx->sync.bytes);
     if (ctx->slots.p) cudaMemset(ctx->slots.p, 0, ctx->slots.bytes);
     if (ctx->shard_done.p) cudaMemset(ctx->shard_done.p, 0, ctx->shard_done.bytes);
-    return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
+    return device_error(code);
   }
   return VMLM_OK;
 }

@@ -212,6 +212,55 @@ def gemm_f32_dev(a, b, c, m, n, k, acc=False, stream=None) -> None:
         _dev_ptr(c, "float32", m * n, "c"), m, n, k, int(bool(acc)), _stream_ptr(stream)))
 
 
+# ------------------------------------------------ decode-step neighbours
+
+def rmsnorm_gemm_nt_int8(a, g, eps, q, scale, c, m, n, k) -> None:
+    """C = gemm_nt_int8(rmsnorm(a, g, eps), q, scale) (ops/src/kernels.rs:1346-1370, then :1256-1287)."""
+    check(lib().vmlm_rmsnorm_gemm_nt_int8(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(g, np.float32, k, "g"), float(eps),
+        _host_ptr(q, np.int8, n * k, "q"), _host_ptr(scale, np.float32, n, "scale"),
+        _host_ptr(c, np.float32, m * n, "c"), m, n, k))
+
+
+def rmsnorm_gemm_nt_int8_dev(a, g, eps, q, scale, c, m, n, k, stream=None) -> None:
+    check(lib().vmlm_rmsnorm_gemm_nt_int8_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(g, "float32", k, "g"), float(eps),
+        _dev_ptr(q, "int8", n * k, "q"), _dev_ptr(scale, "float32", n, "scale"),
+        _dev_ptr(c, "float32", m * n, "c"), m, n, k, _stream_ptr(stream)))
+
+
+def gemv_f32(a, b, c, m, k) -> None:
+    """OP_GEMV (core/src/interp.rs:815-827): c[i] = sum_p a[i, p] * b[p]."""
+    check(lib().vmlm_gemv_f32(_host_ptr(a, np.float32, m * k, "a"), _host_ptr(b, np.float32, k, "b"),
+                              _host_ptr(c, np.float32, m, "c"), m, k))
+
+
+def gemv_f32_dev(a, b, c, m, k, stream=None) -> None:
+    check(lib().vmlm_gemv_f32_dev(_dev_ptr(a, "float32", m * k, "a"), _dev_ptr(b, "float32", k, "b"),
+                                  _dev_ptr(c, "float32", m, "c"), m, k, _stream_ptr(stream)))
+
+
+def emb(table, idx, out) -> None:
+    """OP_EMB (core/src/interp.rs:1351-1420) for every index: out[t] = f32(table[idx[t]]);
+    table: a [rows, cols] bf16-bit (uint16) or float32 array, idx: float32 row numbers."""
+    rows, cols = table.shape
+    dt = DT_BF16 if table.dtype == np.uint16 else DT_F32
+    m = idx.size
+    check(lib().vmlm_emb(_host_ptr(table, table.dtype, rows * cols, "table"), dt, rows, cols,
+                         _host_ptr(idx, np.float32, m, "idx"), m, _host_ptr(out, np.float32, m * cols, "out")))
+
+
+def emb_dev(table, idx, out, stream=None) -> None:
+    """OP_EMB on CUDA tensors (bfloat16 / int16 bits or float32 table); a bad index is reported by sync()."""
+    rows, cols = table.shape
+    name = str(table.dtype)[6:]
+    dt = DT_BF16 if name in ("bfloat16", "int16", "uint16") else DT_F32
+    m = idx.numel()
+    check(lib().vmlm_emb_dev(_dev_ptr(table, name, rows * cols, "table"), dt, rows, cols,
+                             _dev_ptr(idx, "float32", m, "idx"), m, _dev_ptr(out, "float32", m * cols, "out"),
+                             _stream_ptr(stream)))
+
+
 # ------------------------------------------------------ the OP_GEMM operator
 
 DT_F32, DT_F16, DT_I8, DT_I32, DT_BF16 = 0, 1, 2, 3, 4  # core/src/format.rs:73-79
