@@ -106,6 +106,10 @@ struct Ctx {
   int* err_host = nullptr;  // pinned copy read after host-API calls
   DevBuf h_a, h_c, h_w, h_s, h_acc, h_b, h_g;  // host-API staging
   DevBuf xn;  // RMSNorm-fused Q8 calls: the normalised activations [M][K]
+  // host-pointer calls pipelined by row chunks: copies in and out on streams of
+  // their own, ordered against the compute stream by events
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  std::vector<cudaEvent_t> pipe_ev;
   bool attrs_set = false;
   std::map<std::pair<int, uint32_t>, int> dec_clusters;  // (cluster size, smem) -> co-resident clusters
 };
@@ -774,8 +778,22 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
 // bf16 normal mode (more than 80 tokens): split terms written by
 // bf16_terms_norm_kernel into buffers of their own, then the tcgen05 GEMM
 // with as many term passes as the activations need.
+// The tile plan of a bf16 prefill call (tile width, K split, CTA pairs). A
+// call split into row chunks runs every chunk with the plan of the whole
+// call, so each output is summed in the same order as without chunks.
+struct Bf16Plan {
+  NormPlan plan;
+  bool pairs = false;
+};
+
+int bf16_norm_plan(Ctx* c, int M, int N, int K, Bf16Plan* out) {
+  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &out->plan));
+  out->pairs = use_pairs(out->plan, M, N, c->sms);
+  return VMLM_OK;
+}
+
 int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, int kp,
-                  cudaStream_t st) {
+                  cudaStream_t st, const Bf16Plan* force = nullptr) {
   const size_t tbytes = static_cast<size_t>(3) * M * kp * 2;
   if (M != c->norm_m || kp != c->norm_kp) {
     // a new layout: planes and dirty bits start over at zero
@@ -798,8 +816,12 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   TcParams p = {};
   p.rows = M;
   p.cols = N;
-  NormPlan plan;
-  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &plan));
+  Bf16Plan bp;
+  if (force)
+    bp = *force;
+  else
+    VMLM_TRY(bf16_norm_plan(c, M, N, K, &bp));
+  const NormPlan plan = bp.plan;
   p.bn = plan.bn;
   p.max_terms = 3;
   p.a_box_elems = 64;
@@ -819,7 +841,7 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   p.k = K;
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
-  if (use_pairs(plan, M, N, c->sms)) {
+  if (bp.pairs) {
     p.bn = kPairBn;
     p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
     p.tiles_n = static_cast<int>(cdiv(N, p.bn));
@@ -932,7 +954,8 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
   return run_tc<TcMode::kF32Norm>(c, st, ma, mb, p, false, true, plan.split);
 }
 
-int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, cudaStream_t st) {
+int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N, int K, cudaStream_t st,
+             const Bf16Plan* force = nullptr) {
   const bool tc_ok = K > 0 && K % 8 == 0 && aligned16(b);
   if (!tc_ok) {
     const long long warps = static_cast<long long>(M) * N;
@@ -940,7 +963,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
                   b, a, static_cast<long long>(K), out, static_cast<long long>(N), M, N, K);
   }
   const int kp = static_cast<int>(cdiv(K, 8) * 8);
-  if (M > 80) return run_bf16_norm(c, a, b, out, M, N, K, kp, st);
+  if (M > 80) return run_bf16_norm(c, a, b, out, M, N, K, kp, st, force);
   VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * kp * 2));
   VMLM_TRY(ensure(c->small, static_cast<size_t>(3) * M * 4 + 64));
   uint16_t* terms = static_cast<uint16_t*>(c->act.p);
@@ -1041,6 +1064,69 @@ int resolve(Ctx* c, const void* host, size_t bytes, DevBuf& stage, cudaStream_t 
   VMLM_CUDA(cudaMemcpyAsync(stage.p, host, bytes, cudaMemcpyHostToDevice, st));
   *dptr = stage.p;
   return VMLM_OK;
+}
+
+// A host-pointer call over m activation rows, pipelined by chunks of `chunk`
+// rows: the copy of chunk i + 1 in (s_in), the compute of chunk i (the
+// context's stream) and the copy of chunk i - 1 out (s_out) overlap, and the
+// copies in and out use the two directions of the link at once. compute(r0,
+// rows) enqueues the work for rows [r0, r0 + rows) on c->stream, reading
+// din + r0 * in_row and writing dout + r0 * out_row. Ends as a host call does:
+// wait, then read the device error word.
+int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, size_t acc_bytes);
+
+constexpr size_t kPipeChunkRows = 128;  // rows per chunk of a pipelined host call (a multiple)
+constexpr size_t kPipeMaxChunks = 8;
+
+template <class F>
+int host_pipeline(Ctx* c, size_t m, size_t chunk, const void* host_in, void* din, size_t in_row, void* host_out,
+                  void* dout, size_t out_row, F compute) {
+  constexpr size_t kEvents = 2 * kPipeMaxChunks + 2;
+  if (!c->s_in) {
+    VMLM_CUDA(cudaStreamCreateWithFlags(&c->s_in, cudaStreamNonBlocking));
+    VMLM_CUDA(cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
+    c->pipe_ev.resize(kEvents);
+    for (auto& e : c->pipe_ev) VMLM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  // nothing earlier on the compute stream may still use the staging buffers
+  VMLM_CUDA(cudaEventRecord(c->pipe_ev[0], c->stream));
+  VMLM_CUDA(cudaStreamWaitEvent(c->s_in, c->pipe_ev[0], 0));
+  // every copy in is queued first (events 1 .. nch), so the link is busy
+  // while the host is still queueing the GEMMs; events nch + 1 .. mark the
+  // chunks' GEMMs for the copies out
+  // chunk i covers rows [i * chunk, +chunk); the last one also takes the
+  // remainder, so no chunk is shorter than `chunk` rows
+  const size_t nch = m / chunk > 0 ? m / chunk : 1;
+  if (2 * nch + 2 > kEvents) return fail(VMLM_ERR_SHAPE, "pipelined call: too many chunks");
+  auto rows_of = [&](size_t i) { return i + 1 == nch ? m - i * chunk : chunk; };
+  for (size_t i = 0; i < nch; ++i) {
+    const size_t r0 = i * chunk, rows = rows_of(i);
+    VMLM_CUDA(cudaMemcpyAsync(static_cast<char*>(din) + r0 * in_row, static_cast<const char*>(host_in) + r0 * in_row,
+                              rows * in_row, cudaMemcpyHostToDevice, c->s_in));
+    VMLM_CUDA(cudaEventRecord(c->pipe_ev[1 + i], c->s_in));
+  }
+  for (size_t i = 0; i < nch; ++i) {
+    const size_t r0 = i * chunk, rows = rows_of(i);
+    VMLM_CUDA(cudaStreamWaitEvent(c->stream, c->pipe_ev[1 + i], 0));
+    VMLM_TRY(compute(r0, rows));
+    cudaEvent_t ec = c->pipe_ev[1 + nch + i];
+    VMLM_CUDA(cudaEventRecord(ec, c->stream));
+    VMLM_CUDA(cudaStreamWaitEvent(c->s_out, ec, 0));
+    VMLM_CUDA(cudaMemcpyAsync(static_cast<char*>(host_out) + r0 * out_row, static_cast<char*>(dout) + r0 * out_row,
+                              rows * out_row, cudaMemcpyDeviceToHost, c->s_out));
+  }
+  cudaEvent_t done = c->pipe_ev[1 + 2 * nch];
+  VMLM_CUDA(cudaEventRecord(done, c->s_out));
+  VMLM_CUDA(cudaStreamWaitEvent(c->stream, done, 0));
+  return finish_host_call(c, nullptr, 0, nullptr, 0);
+}
+
+// Rows per chunk of a pipelined host call, 0 for a call too small to gain.
+size_t pipeline_chunk(size_t m, size_t in_row, size_t out_row, size_t unit = kPipeChunkRows) {
+  if (m < 256 || m * (in_row + out_row) < (static_cast<size_t>(2) << 20)) return 0;
+  size_t chunk = unit;
+  while (m / chunk > kPipeMaxChunks) chunk += unit;
+  return chunk;
 }
 
 // The status for a non-zero device error word: the VM's OP_EMB messages, or a
@@ -1202,6 +1288,9 @@ int vmlm_shutdown(void) {
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
+    for (cudaEvent_t e : c->pipe_ev) cudaEventDestroy(e);
+    if (c->s_in) cudaStreamDestroy(c->s_in);
+    if (c->s_out) cudaStreamDestroy(c->s_out);
     cudaStreamDestroy(c->stream);
     delete c;
   }
@@ -1272,6 +1361,26 @@ int vmlm_gemm_nt_bf16(const float* a, const uint16_t* b, float* c, size_t m, siz
   Ctx* ctx = nullptr;
   VMLM_TRY(host_ctx(&ctx));
   const void *da = nullptr, *db = nullptr;
+  // large prefill call (the tensor-core path with 128-byte-aligned rows): A
+  // in, the GEMM and C out pipelined by row chunks, every chunk on the plan
+  // of the whole call (the same sums as one call)
+  size_t chunk = 0;
+  Bf16Plan bp;
+  if (k > 0 && k % 8 == 0 && aligned16(b) && m > 80) {
+    VMLM_TRY(bf16_norm_plan(ctx, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), &bp));
+    chunk = pipeline_chunk(m, k * 4, n * 4, bp.pairs ? 2 * kPipeChunkRows : kPipeChunkRows);
+  }
+  if (chunk) {
+    VMLM_TRY(resolve(ctx, b, n * k * 2, ctx->h_w, ctx->stream, &db));
+    VMLM_TRY(ensure(ctx->h_a, m * k * 4));
+    VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+    const float* dA = static_cast<const float*>(ctx->h_a.p);
+    float* dC = static_cast<float*>(ctx->h_c.p);
+    return host_pipeline(ctx, m, chunk, a, ctx->h_a.p, k * 4, c, ctx->h_c.p, n * 4, [&](size_t r0, size_t rows) {
+      return run_bf16(ctx, dA + r0 * k, static_cast<const uint16_t*>(db), dC + r0 * n, static_cast<int>(rows),
+                      static_cast<int>(n), static_cast<int>(k), ctx->stream, &bp);
+    });
+  }
   VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
   VMLM_TRY(resolve(ctx, b, n * k * 2, ctx->h_w, ctx->stream, &db));
   VMLM_TRY(ensure(ctx->h_c, m * n * 4));
