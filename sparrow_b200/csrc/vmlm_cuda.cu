@@ -1343,6 +1343,21 @@ int vmlm_gemm_nt_int8(const float* a, const int8_t* q, const float* scale, float
   Ctx* ctx = nullptr;
   VMLM_TRY(host_ctx(&ctx));
   const void *da = nullptr, *dq = nullptr, *ds = nullptr;
+  // large call: A in, the GEMM and C out pipelined by row chunks (the digit
+  // planes make every path's sums exact: chunks give the same bits)
+  const size_t chunk = k > 0 ? pipeline_chunk(m, k * 4, n * 4) : 0;
+  if (chunk) {
+    VMLM_TRY(resolve(ctx, q, n * k, ctx->h_w, ctx->stream, &dq));
+    VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+    VMLM_TRY(ensure(ctx->h_a, m * k * 4));
+    VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+    const float* dA = static_cast<const float*>(ctx->h_a.p);
+    float* dC = static_cast<float*>(ctx->h_c.p);
+    return host_pipeline(ctx, m, chunk, a, ctx->h_a.p, k * 4, c, ctx->h_c.p, n * 4, [&](size_t r0, size_t rows) {
+      return run_q8(ctx, dA + r0 * k, static_cast<const int8_t*>(dq), static_cast<const float*>(ds), dC + r0 * n,
+                    static_cast<int>(rows), static_cast<int>(n), static_cast<int>(k), ctx->stream);
+    });
+  }
   VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
   VMLM_TRY(resolve(ctx, q, n * k, ctx->h_w, ctx->stream, &dq));
   VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
@@ -1400,6 +1415,24 @@ int vmlm_gemm_i8i8(const int8_t* x, const int8_t* w, const float* scale, float* 
   Ctx* ctx = nullptr;
   VMLM_TRY(host_ctx(&ctx));
   const void *dx = nullptr, *dw = nullptr, *ds = nullptr;
+  // one output of a large call: X in, the GEMM and the output out pipelined
+  // by row chunks (integer sums: any tile plan gives the same bits)
+  const size_t chunk = (k > 0 && (!c || !acc)) ? pipeline_chunk(m, k, n * 4) : 0;
+  if (chunk) {
+    VMLM_TRY(resolve(ctx, w, n * k, ctx->h_w, ctx->stream, &dw));
+    if (c) VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+    VMLM_TRY(ensure(ctx->h_a, m * k));
+    DevBuf& ob = c ? ctx->h_c : ctx->h_acc;
+    VMLM_TRY(ensure(ob, m * n * 4));
+    const int8_t* dX = static_cast<const int8_t*>(ctx->h_a.p);
+    void* host_out = c ? static_cast<void*>(c) : static_cast<void*>(acc);
+    return host_pipeline(ctx, m, chunk, x, ctx->h_a.p, k, host_out, ob.p, n * 4, [&](size_t r0, size_t rows) {
+      return run_i8i8(ctx, dX + r0 * k, static_cast<const int8_t*>(dw), static_cast<const float*>(ds),
+                      c ? static_cast<float*>(ob.p) + r0 * n : nullptr,
+                      acc ? static_cast<int32_t*>(ob.p) + r0 * n : nullptr, static_cast<int>(rows),
+                      static_cast<int>(n), static_cast<int>(k), ctx->stream);
+    });
+  }
   VMLM_TRY(resolve(ctx, x, m * k, ctx->h_a, ctx->stream, &dx));
   VMLM_TRY(resolve(ctx, w, n * k, ctx->h_w, ctx->stream, &dw));
   if (c) VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));

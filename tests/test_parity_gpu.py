@@ -397,6 +397,36 @@ def test_device_entry_points_match_host_ones(kernels, oracle):
     assert oracle.max_rel_err(dcb.cpu().numpy(), hb) <= 1e-6
 
 
+@pytest.mark.parametrize("m", [512, 1000, 2048])
+def test_pipelined_host_calls_match_device_calls(kernels, oracle, m):
+    """Large host-pointer calls run in row chunks on copy streams; every chunk
+    must give the bits the one device call gives (ragged last chunks too)."""
+    import torch
+    n, k = 2304, 2304
+    st = torch.cuda.current_stream()
+    x, q, s = q8_case(oracle, m, n, k, seed=m)
+    host = kernels.q8_linear(x, q, s)
+    dc = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    kernels.gemm_nt_int8_dev(torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(),
+                             dc, m, n, k, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(dc.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    xb, wb = bf16_case(oracle, m, n, k, seed=m + 1, exact_x=False)
+    hb = kernels.bf16_linear(xb, wb)
+    kernels.gemm_nt_bf16_dev(torch.from_numpy(xb).cuda(), torch.from_numpy(wb.view(np.int16)).cuda(), dc,
+                             m, n, k, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(dc.cpu().numpy().view(np.uint32), hb.view(np.uint32))
+    xi, wi, si = i8_case(oracle, m, n, k, seed=m + 2)
+    c_only = np.empty((m, n), np.float32)
+    acc_only = np.empty((m, n), np.int32)
+    kernels.gemm_i8i8(xi, wi, si, c_only, None, m, n, k)
+    kernels.gemm_i8i8(xi, wi, si, None, acc_only, m, n, k)
+    rc, racc = oracle.gemm_i8i8(xi, wi, si, nt=NT)
+    assert np.array_equal(acc_only, racc)
+    assert np.array_equal(c_only.view(np.uint32), rc.view(np.uint32))
+
+
 @pytest.mark.parametrize("m,n,k", [(2048, 4096, 1024), (1000, 3000, 520), (4096, 2048, 4096)])
 def test_i8i8_cta_pairs_bit_exact(kernels, oracle, m, n, k):
     # shapes large enough for the CTA-pair kernel (256-row tiles over two SMs)
