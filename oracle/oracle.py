@@ -48,6 +48,10 @@ def lib() -> ctypes.CDLL:
             "oracle_fill_normal": [P, S, U64, F, I],
             "oracle_fill_gauss_ref": [P, S, U64, F, I],
             "oracle_fill_int8": [P, S, U64, I],
+            "oracle_fill_gauss_k": [P, S, U64, F, I],
+            "oracle_quant_int4_grouped": [P, S, S, S, P, P],
+            "oracle_gemm_nt_int4_gs": [P, P, P, P, S, S, S, S, I],
+            "oracle_gemm_nt_int8_outlier": [P, P, P, P, P, S, P, S, S, S],
             "oracle_quant_int8": [P, S, S, P, P, I],
             "oracle_f32_to_bf16_n": [P, P, S],
             "oracle_bf16_to_f32_n": [P, P, S],
@@ -58,6 +62,8 @@ def lib() -> ctypes.CDLL:
             fn.restype = None
         L.oracle_emb.argtypes = [P, I, S, S, P, S, P]
         L.oracle_emb.restype = I
+        L.oracle_quant_int8_outliers.argtypes = [P, S, S, F, P, P, P]
+        L.oracle_quant_int8_outliers.restype = S
         L.oracle_max_rel_err.argtypes = [P, P, S]
         L.oracle_max_rel_err.restype = ctypes.c_double
         _lib = L
@@ -216,6 +222,69 @@ def fill_uniform(n, seed, scale, nt=None):
     out = np.empty(n, np.float32)
     lib().oracle_fill_uniform(_p(out), n, seed, scale, _threads(nt))
     return out
+
+
+def fill_gauss_k(n, seed, k, nt=None):
+    """The quantisation benchmark's weights (tests/src/quant.rs:595-602): the reference
+    Box-Muller divided by sqrt(k)."""
+    out = np.empty(n, np.float32)
+    lib().oracle_fill_gauss_k(_p(out), n, seed, float(np.sqrt(np.float32(k), dtype=np.float32)), _threads(nt))
+    return out
+
+
+def quant_weights_with_outlier_channels(n, k):
+    """tests/src/quant.rs:595-609: fill_gauss_k (seed 0xDEADBEEF), then every 64th
+    column (0, 64, ...) times 12."""
+    w = fill_gauss_k(n * k, 0xDEADBEEF, k).reshape(n, k)
+    w[:, ::64] *= np.float32(12.0)
+    return w
+
+
+def quant_int4_grouped(w, group):
+    """tests/src/quant.rs:114-152 -> (packed uint8 [n, (k+1)//2], scale f32 [n, ceil(k/group)])."""
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    packed = np.empty((n, (k + 1) // 2), np.uint8)
+    scale = np.empty((n, (k + group - 1) // group), np.float32)
+    lib().oracle_quant_int4_grouped(_p(w), n, k, group, _p(packed), _p(scale))
+    return packed, scale
+
+
+def gemm_nt_int4_gs(a, packed, scale, k, group, order=0):
+    """tests/src/quant.rs:298-362: order 1 = the AVX2 step as shipped, order 0 = the
+    same arithmetic on the packer's nibble order."""
+    a = np.ascontiguousarray(a, np.float32)
+    m = a.shape[0]
+    n = packed.shape[0]
+    c = np.empty((m, n), np.float32)
+    lib().oracle_gemm_nt_int4_gs(_p(a), _p(np.ascontiguousarray(packed, np.uint8)),
+                                 _p(np.ascontiguousarray(scale, np.float32)), _p(c), m, n, k, group, int(order))
+    return c
+
+
+def quant_int8_outliers(w, thresh):
+    """tests/src/quant.rs:458-515 -> (q int8 [n,k], scale f32 [n], outlier column indices uint32)."""
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    q = np.empty((n, k), np.int8)
+    s = np.empty(n, np.float32)
+    idx = np.empty(max(k, 1), np.uint32)
+    cnt = lib().oracle_quant_int8_outliers(_p(w), n, k, thresh, _p(q), _p(s), _p(idx))
+    assert cnt <= k
+    return q, s, idx[:cnt].copy()
+
+
+def gemm_nt_int8_outlier(a, q, scale, w, idx):
+    """tests/src/quant.rs:524-565: the int8 body times scale, plus a[jj] * w[j][jj] per outlier."""
+    a = np.ascontiguousarray(a, np.float32)
+    m, k = a.shape
+    n = q.shape[0]
+    c = np.empty((m, n), np.float32)
+    idx = np.ascontiguousarray(idx, np.uint32)
+    lib().oracle_gemm_nt_int8_outlier(_p(a), _p(np.ascontiguousarray(q, np.int8)),
+                                      _p(np.ascontiguousarray(scale, np.float32)),
+                                      _p(np.ascontiguousarray(w, np.float32)), _p(idx), idx.size, _p(c), m, n, k)
+    return c
 
 
 def fill_int8(n, seed, nt=None):

@@ -30,6 +30,12 @@
  *   oracle_emb                 core/src/interp.rs:1351-1420 (OP_EMB: index
  *                              checks, then the row widened or copied)
  *   parallel split             ops/src/par.rs:44-62 (chunk = ceil(n/nt) over N)
+ *   oracle_quant_int4_grouped  tests/src/quant.rs:114-152 (int4, a scale per group)
+ *   oracle_gemm_nt_int4_gs     tests/src/quant.rs:298-362 (AVX2 as shipped, or the
+ *                              packed order; see the function)
+ *   oracle_quant_int8_outliers tests/src/quant.rs:458-515 (LLM.int8 outlier columns)
+ *   oracle_gemm_nt_int8_outlier tests/src/quant.rs:524-565
+ *   oracle_fill_gauss_k        tests/src/quant.rs:595-602 (Box-Muller / sqrt(k))
  *
  * The AVX2 bodies use the same intrinsic sequence as the reference, so the
  * summation order is the same; the file must be built with -mavx2 -mfma
@@ -45,6 +51,7 @@
 #include <pthread.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define EXPORT __attribute__((visibility("default")))
@@ -456,6 +463,19 @@ static void *gen_range(void *p) {
             float arg = two_pi * u2;
             o[i] = r * cosf(arg) * g->scale;
         }
+    } else if (g->kind == 4) {
+        /* tests/src/quant.rs:595-602: the same draws, r * cos(2 pi u2) / sqrt(k)
+         * (scale holds sqrt(k); a division, as written). */
+        uint64_t s = lcg_jump(g->seed, 2 * g->lo);
+        float *o = (float *)g->out;
+        const float two_pi = 2.0f * 3.14159265358979323846f;
+        for (size_t i = g->lo; i < g->hi; i++) {
+            float u1 = (lcg_next(&s) + 1.0f) * 0.5f + 1e-9f;
+            float u2 = (lcg_next(&s) + 1.0f) * 0.5f;
+            float r = sqrtf(-2.0f * logf(u1));
+            float arg = two_pi * u2;
+            o[i] = r * cosf(arg) / g->scale;
+        }
     } else if (g->kind == 3) {
         /* Box-Muller on the same lcg, with both uniforms taken from the top 24
          * bits over the full [0,1) range: a true N(0, sigma). */
@@ -527,6 +547,13 @@ EXPORT void oracle_fill_normal(float *out, size_t n, uint64_t seed, float sigma,
     gen_par(g, n, nt);
 }
 
+/* The weight generator of the quantisation benchmark (tests/src/quant.rs:595-602):
+ * the reference Box-Muller divided by sqrt(k) (sqrt_k = sqrtf(k)). */
+EXPORT void oracle_fill_gauss_k(float *out, size_t n, uint64_t seed, float sqrt_k, int nt) {
+    gen_t g = {4, seed, 0, 0, sqrt_k, out};
+    gen_par(g, n, nt);
+}
+
 /* Uniform int8 in [-127,127]: ((s>>33) % 255) - 127 on the lcg stream. */
 EXPORT void oracle_fill_int8(int8_t *out, size_t n, uint64_t seed, int nt) {
     gen_t g = {2, seed, 0, 0, 1.0f, out};
@@ -592,6 +619,187 @@ EXPORT void oracle_quant_int8(const float *w, size_t n, size_t k, int8_t *q, flo
     }
     for (int t = 0; t < started; t++)
         if (th[t]) pthread_join(th[t], NULL);
+}
+
+/* ------------------------------------------------------ variant kernels */
+
+/* tests/src/quant.rs:114-152: per row and group of `group` columns, amax (0 ->
+ * 1e-30), s = amax/7, v = round(w/s) clamped to [-7,7]; two's-complement
+ * nibbles packed two per byte, column j in the low nibble when j is even and
+ * the high nibble when odd; rows of (k+1)/2 bytes; scale [n][ceil(k/group)]. */
+EXPORT void oracle_quant_int4_grouped(const float *w, size_t n, size_t k, size_t group, uint8_t *packed,
+                                      float *scale) {
+    size_t rowbytes = (k + 1) / 2, gpr = (k + group - 1) / group;
+    memset(packed, 0, n * rowbytes);
+    for (size_t i = 0; i < n; i++)
+        for (size_t g = 0; g < gpr; g++) {
+            size_t beg = g * group, end = beg + group < k ? beg + group : k;
+            float amax = 0.0f;
+            for (size_t j = beg; j < end; j++) {
+                float a = fabsf(w[i * k + j]);
+                if (a > amax) amax = a;
+            }
+            if (amax == 0.0f) amax = 1e-30f;
+            float s = amax / 7.0f;
+            scale[i * gpr + g] = s;
+            for (size_t j = beg; j < end; j++) {
+                float r = roundf(w[i * k + j] / s);
+                if (r < -7.0f) r = -7.0f;
+                if (r > 7.0f) r = 7.0f;
+                uint8_t nib = (uint8_t)(int8_t)r & 0x0F;
+                size_t idx = i * rowbytes + j / 2;
+                packed[idx] = (j % 2 == 0) ? (uint8_t)((packed[idx] & 0xF0) | nib)
+                                           : (uint8_t)((packed[idx] & 0x0F) | (nib << 4));
+            }
+        }
+}
+
+static inline int nib_value(uint8_t byte, size_t col) {
+    int nib = (col % 2 == 0) ? (byte & 0x0F) : ((byte >> 4) & 0x0F);
+    return nib > 7 ? nib - 16 : nib;
+}
+
+/* tests/src/quant.rs:298-362, gemm_nt_int4_gs. Per (i, j) and per group
+ * [g0, min(g0+group, k)): 32-wide steps while kk+32 <= gend, each one 16-byte
+ * load at packed + kk/2 and four 8-lane FMAs into one accumulator (lanes kk..+7,
+ * +8..+15, +16..+23, +24..+31), hsum_ps, a scalar tail (mul then add), then
+ * total += s * scale[group] (mul then add).
+ *
+ * order 1 is the AVX2 step as shipped (the same intrinsic sequence as
+ * :316-333): both 128-bit lanes of the widened load hold the same 16 bytes, so
+ * unpacklo/unpackhi repeat bytes 0-3 and 8-11, and the first nibble taken from
+ * each byte is the high one; the weights used at step offsets t = 0..31 are the
+ * nibbles of byte kk/2 + (t & 16) / 2 + (t & 7) / 2, high nibble for even t.
+ * That is not the packer's order (:143-148), which the scalar tail follows.
+ * order 0 runs the same arithmetic on the packer's order: offset t uses column
+ * kk + t. */
+EXPORT void oracle_gemm_nt_int4_gs(const float *a, const uint8_t *packed, const float *scale, float *c,
+                                   size_t m, size_t n, size_t k, size_t group, int order) {
+    size_t rowbytes = (k + 1) / 2, gpr = (k + group - 1) / group;
+    const __m256i lut = _mm256_setr_epi8(0, 1, 2, 3, 4, 5, 6, 7, -8, -7, -6, -5, -4, -3, -2, -1,
+                                         0, 1, 2, 3, 4, 5, 6, 7, -8, -7, -6, -5, -4, -3, -2, -1);
+    const __m256i mask0f = _mm256_set1_epi8(0x0F);
+    for (size_t i = 0; i < m; i++)
+        for (size_t j = 0; j < n; j++) {
+            const float *ar = a + i * k;
+            const uint8_t *pr = packed + j * rowbytes;
+            const float *sc = scale + j * gpr;
+            float total = 0.0f;
+            size_t g0 = 0;
+            while (g0 < k) {
+                size_t gend = g0 + group < k ? g0 + group : k;
+                __m256 acc = _mm256_setzero_ps();
+                size_t kk = g0;
+                while (kk + 32 <= gend) {
+                    __m256i q0, q1, q2, q3;
+                    if (order == 1) {
+                        __m128i raw = _mm_loadu_si128((const __m128i *)(pr + kk / 2));
+                        __m256i v = _mm256_inserti128_si256(_mm256_castsi128_si256(raw), raw, 1);
+                        __m256i lo_nib = _mm256_and_si256(_mm256_srli_epi16(v, 4), mask0f);
+                        __m256i hi_nib = _mm256_and_si256(v, mask0f);
+                        __m256i lo_i8 = _mm256_shuffle_epi8(lut, lo_nib);
+                        __m256i hi_i8 = _mm256_shuffle_epi8(lut, hi_nib);
+                        __m256i inter_lo = _mm256_unpacklo_epi8(lo_i8, hi_i8);
+                        __m256i inter_hi = _mm256_unpackhi_epi8(lo_i8, hi_i8);
+                        q0 = _mm256_cvtepi8_epi32(_mm256_castsi256_si128(inter_lo));
+                        q1 = _mm256_cvtepi8_epi32(_mm256_extracti128_si256(inter_lo, 1));
+                        q2 = _mm256_cvtepi8_epi32(_mm256_castsi256_si128(inter_hi));
+                        q3 = _mm256_cvtepi8_epi32(_mm256_extracti128_si256(inter_hi, 1));
+                    } else {
+                        int8_t t8[32];
+                        for (int t = 0; t < 32; t++) t8[t] = (int8_t)nib_value(pr[(kk + t) / 2], kk + t);
+                        q0 = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i *)(t8 + 0)));
+                        q1 = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i *)(t8 + 8)));
+                        q2 = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i *)(t8 + 16)));
+                        q3 = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i *)(t8 + 24)));
+                    }
+                    acc = _mm256_fmadd_ps(_mm256_loadu_ps(ar + kk), _mm256_cvtepi32_ps(q0), acc);
+                    acc = _mm256_fmadd_ps(_mm256_loadu_ps(ar + kk + 8), _mm256_cvtepi32_ps(q1), acc);
+                    acc = _mm256_fmadd_ps(_mm256_loadu_ps(ar + kk + 16), _mm256_cvtepi32_ps(q2), acc);
+                    acc = _mm256_fmadd_ps(_mm256_loadu_ps(ar + kk + 24), _mm256_cvtepi32_ps(q3), acc);
+                    kk += 32;
+                }
+                float s = hsum_ps(acc);
+                while (kk < gend) {
+                    float prod = ar[kk] * (float)nib_value(pr[kk / 2], kk);
+                    s = s + prod;
+                    kk += 1;
+                }
+                float part = s * sc[g0 / group];
+                total = total + part;
+                g0 = gend;
+            }
+            c[i * n + j] = total;
+        }
+}
+
+/* tests/src/quant.rs:458-515: column RMS in f64 (sum over rows of w^2, / n,
+ * sqrt), mean over columns; a column is an outlier when its RMS exceeds
+ * thresh * mean. Per row amax over the other columns (0 -> 1e-30), s =
+ * amax/127, q = round(w/s) clamped to +-127, outlier columns quantised to 0.
+ * Writes the ascending outlier column indices to idx and returns their count. */
+EXPORT size_t oracle_quant_int8_outliers(const float *w, size_t n, size_t k, float thresh, int8_t *q,
+                                         float *scale, uint32_t *idx) {
+    double tot = 0.0;
+    size_t n_out = 0;
+    double *col = (double *)calloc(k ? k : 1, sizeof(double));
+    if (!col) return (size_t)-1;
+    for (size_t i = 0; i < n; i++)
+        for (size_t j = 0; j < k; j++) col[j] += (double)w[i * k + j] * (double)w[i * k + j];
+    for (size_t j = 0; j < k; j++) {
+        col[j] = sqrt(col[j] / (double)n);
+        tot += col[j];
+    }
+    double mean = tot / (double)k;
+    for (size_t j = 0; j < k; j++)
+        if (col[j] > (double)thresh * mean) idx[n_out++] = (uint32_t)j;
+    for (size_t i = 0; i < n; i++) {
+        float amax = 0.0f;
+        size_t o = 0;
+        for (size_t j = 0; j < k; j++) {
+            if (o < n_out && idx[o] == j) {
+                o++;
+                continue;
+            }
+            float av = fabsf(w[i * k + j]);
+            if (av > amax) amax = av;
+        }
+        if (amax == 0.0f) amax = 1e-30f;
+        float s = amax / 127.0f;
+        scale[i] = s;
+        o = 0;
+        for (size_t j = 0; j < k; j++) {
+            if (o < n_out && idx[o] == j) {
+                o++;
+                q[i * k + j] = 0;
+                continue;
+            }
+            float r = roundf(w[i * k + j] / s);
+            if (r < -127.0f) r = -127.0f;
+            if (r > 127.0f) r = 127.0f;
+            q[i * k + j] = (int8_t)r;
+        }
+    }
+    free(col);
+    return n_out;
+}
+
+/* tests/src/quant.rs:524-565: the int8 body of gemm_nt_int8 (:1256-1287 of the
+ * kernels), v = s * scale[j], then v += a[i][jj] * w[j][jj] (mul then add) for
+ * each listed outlier column in list order. w is the f32 weight [n][k]. */
+EXPORT void oracle_gemm_nt_int8_outlier(const float *a, const int8_t *q, const float *scale, const float *w,
+                                        const uint32_t *idx, size_t n_idx, float *c, size_t m, size_t n,
+                                        size_t k) {
+    gemm_nt_int8_cols(a, q, scale, c, m, n, k, 0, n);
+    for (size_t i = 0; i < m; i++)
+        for (size_t j = 0; j < n; j++) {
+            float v = c[i * n + j];
+            for (size_t t = 0; t < n_idx; t++) {
+                float prod = a[i * k + idx[t]] * w[j * k + idx[t]];
+                v = v + prod;
+            }
+            c[i * n + j] = v;
+        }
 }
 
 /* Reference-convention error: max|got-ref| / max|ref| (tests/src/quant.rs:381-418). */

@@ -1,0 +1,292 @@
+// variants.cuh -- the weight-quantisation variants of the reference's study
+// (tests/src/quant.rs): int4 weights with an f32 scale per group of columns
+// (:114-152, :298-362), and the int8 GEMM whose outlier input columns are
+// added back in f32 (LLM.int8, :458-565). Decode-size GEMMs: CUDA-core kernels
+// that stream the packed weights once.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace vmlm {
+
+constexpr int kDevIdxRange = 103;  // an outlier column index >= k
+
+// ------------------------------------------------------------ int4 grouped
+//
+// Layout (tests/src/quant.rs:114-152): rows of (k+1)/2 bytes, column p in the
+// low nibble of byte p/2 when p is even and the high nibble when odd, two's
+// complement in [-8, 7]; scale [n][gpr], gpr = ceil(k/group).
+//
+// The reference's AVX2 step (:316-333) does not read that order: a 32-column
+// step at column kk loads 16 bytes at kk/2 into both 128-bit halves, so its
+// unpacks repeat bytes 0-3 and 8-11, and it takes each byte's high nibble
+// first. Column kk+t (t < 32) uses the nibble of byte kk/2 + (t&16)/2 +
+// (t&7)/2, high when t is even. Only 32-column steps that fit inside a group
+// do that; the rest of a group (its scalar tail) follows the packed order.
+// `order` 1 reproduces the step as shipped, 0 uses the packed order.
+
+constexpr int kI4Warps = 8;
+constexpr int kI4RowsPerWarp = 2;
+constexpr int kI4RowsPerBlock = kI4Warps * kI4RowsPerWarp;
+constexpr int kI4SmemFloats = 24576;  // 96 KB of staged activations per CTA
+
+// Swap the two nibbles of every byte.
+__device__ __forceinline__ uint32_t nib_swap(uint32_t w) { return ((w >> 4) & 0x0F0F0F0Fu) | ((w & 0x0F0F0F0Fu) << 4); }
+
+// Column class c = p % 8 of a 32-column unit: the nibble sits at bits 4c of its
+// word for c < 3 and at bits 4(c-3) of the word shifted right by 12 for c >= 3,
+// so f = 2^23 + u * 2^(4c') with u = nibble ^ 8 and c' = c < 3 ? c : c - 3, and
+// f - (2^23 + 8 * 2^(4c')) = v * 2^(4c') exactly (v the signed nibble). The
+// staged activations carry the factor 2^-(4c'), so a' * (v 2^(4c')) = a * v
+// with the same rounding (power-of-two scaling is exact).
+__host__ __device__ constexpr int i4_shift(int c) { return c < 3 ? 4 * c : 4 * (c - 3); }
+
+__device__ __forceinline__ float i4_val(uint32_t w, uint32_t w12, int c) {
+  const uint32_t src = c < 3 ? w : w12;
+  const int sh = i4_shift(c);
+  const float f = __uint_as_float(0x4B000000u | (src & (0xFu << sh)));
+  return f - (8388608.0f + 8.0f * static_cast<float>(1 << sh));
+}
+
+// Fast path: k % 32 == 0, group % 32 == 0, 16-byte aligned packed rows (so
+// every 32-column unit lies inside one group and is one reference step).
+// Grid (row-set CTAs, ceil(m / MB)); a warp owns kI4RowsPerWarp weight rows
+// and its lanes take 32-column units lane, lane + 32, ...; the activations of
+// MB token rows are staged in shared memory in chunks of kc columns, float4 f
+// of a row stored at f ^ ((f >> 3) & 7) so a quarter-warp's float4 reads of
+// eight consecutive units hit eight different bank groups.
+template <int MB, int ORDER>
+__global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __restrict__ a,
+                                                               const uint8_t* __restrict__ packed,
+                                                               const float* __restrict__ scale, float* __restrict__ c,
+                                                               int m, int n, int k, int group, int gpr, int kc) {
+  extern __shared__ float4 s_a4[];
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const int m0 = blockIdx.y * MB;
+  const int rows_m = m - m0 < MB ? m - m0 : MB;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const long long rowbytes = k / 2;
+  const int kc4 = kc / 4;
+  const bool one_chunk = kc >= k;
+
+  auto stage = [&](int kc0, int kcn) {
+    // a'[r][p] = a[m0 + r][kc0 + p] * 2^-(i4_shift(p % 8)); rows past m are zero
+    for (int e = static_cast<int>(threadIdx.x); e < MB * kcn; e += blockDim.x) {
+      const int r = e / kcn, p = e - r * kcn;
+      float v = 0.f;
+      if (r < rows_m) v = __ldg(a + static_cast<long long>(m0 + r) * k + kc0 + p);
+      const int sh = i4_shift(p & 7);
+      v *= __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+      const int f = p >> 2;
+      reinterpret_cast<float*>(s_a4)[(r * kc4 + (f ^ ((f >> 3) & 7))) * 4 + (p & 3)] = v;
+    }
+  };
+
+  if (one_chunk) {
+    stage(0, k);
+    __syncthreads();
+  }
+  for (int j0 = blockIdx.x * kI4RowsPerBlock; j0 < n; j0 += gridDim.x * kI4RowsPerBlock) {
+    const int jw = j0 + warp * kI4RowsPerWarp;
+    float tot[kI4RowsPerWarp][MB];
+#pragma unroll
+    for (int r = 0; r < kI4RowsPerWarp; ++r)
+#pragma unroll
+      for (int i = 0; i < MB; ++i) tot[r][i] = 0.f;
+    for (int kc0 = 0; kc0 < k; kc0 += kc) {
+      const int kcn = k - kc0 < kc ? k - kc0 : kc;
+      if (!one_chunk) {
+        __syncthreads();
+        stage(kc0, kcn);
+        __syncthreads();
+      }
+      if (jw < n) {
+        for (int u = lane; u < kcn / 32; u += 32) {
+          const int ug = kc0 / 32 + u;
+          const int g = ug * 32 / group;
+          uint4 wv[kI4RowsPerWarp];
+          float sc[kI4RowsPerWarp];
+#pragma unroll
+          for (int r = 0; r < kI4RowsPerWarp; ++r) {
+            const int j = jw + r < n ? jw + r : n - 1;  // a past-the-end row reads row n-1 and is not stored
+            wv[r] = __ldg(reinterpret_cast<const uint4*>(packed + j * rowbytes) + ug);
+            sc[r] = __ldg(scale + static_cast<long long>(j) * gpr + g);
+            if (ORDER == 1) {
+              const uint32_t x0 = nib_swap(wv[r].x), x2 = nib_swap(wv[r].z);
+              wv[r] = make_uint4(x0, x0, x2, x2);
+            }
+            wv[r].x ^= 0x88888888u;
+            wv[r].y ^= 0x88888888u;
+            wv[r].z ^= 0x88888888u;
+            wv[r].w ^= 0x88888888u;
+          }
+          float part[kI4RowsPerWarp][MB];
+#pragma unroll
+          for (int r = 0; r < kI4RowsPerWarp; ++r)
+#pragma unroll
+            for (int i = 0; i < MB; ++i) part[r][i] = 0.f;
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            float4 av[MB];
+#pragma unroll
+            for (int i = 0; i < MB; ++i) av[i] = s_a4[i * kc4 + u * 8 + (v ^ (u & 7))];
+#pragma unroll
+            for (int r = 0; r < kI4RowsPerWarp; ++r) {
+              const uint32_t w = (v >> 1) == 0 ? wv[r].x : (v >> 1) == 1 ? wv[r].y : (v >> 1) == 2 ? wv[r].z : wv[r].w;
+              const uint32_t w12 = w >> 12;
+              const int c0 = (v & 1) * 4;
+              const float d0 = i4_val(w, w12, c0), d1 = i4_val(w, w12, c0 + 1);
+              const float d2 = i4_val(w, w12, c0 + 2), d3 = i4_val(w, w12, c0 + 3);
+#pragma unroll
+              for (int i = 0; i < MB; ++i) {
+                float s = part[r][i];
+                s = fmaf(av[i].x, d0, s);
+                s = fmaf(av[i].y, d1, s);
+                s = fmaf(av[i].z, d2, s);
+                s = fmaf(av[i].w, d3, s);
+                part[r][i] = s;
+              }
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < kI4RowsPerWarp; ++r)
+#pragma unroll
+            for (int i = 0; i < MB; ++i) tot[r][i] = fmaf(part[r][i], sc[r], tot[r][i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kI4RowsPerWarp; ++r)
+#pragma unroll
+      for (int i = 0; i < MB; ++i) {
+        float s = tot[r][i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0 && jw + r < n && i < rows_m) c[static_cast<long long>(m0 + i) * n + jw + r] = s;
+      }
+  }
+}
+
+// Any shape: a warp per (token row, weight row), lanes over columns. The lane
+// sums its columns of one group, then adds that sum times the group's scale.
+template <int ORDER>
+__global__ void __launch_bounds__(256) int4gs_generic_kernel(const float* __restrict__ a,
+                                                             const uint8_t* __restrict__ packed,
+                                                             const float* __restrict__ scale, float* __restrict__ c,
+                                                             int m, int n, int k, int group, int gpr) {
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const long long wid = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  if (wid >= static_cast<long long>(m) * n) return;
+  const int i = static_cast<int>(wid / n), j = static_cast<int>(wid - static_cast<long long>(i) * n);
+  const uint8_t* pr = packed + static_cast<long long>(j) * ((k + 1) / 2);
+  const float* ar = a + static_cast<long long>(i) * k;
+  float tot = 0.f, part = 0.f;
+  int gcur = -1;
+  for (int p = lane; p < k; p += 32) {
+    const int g = p / group;
+    if (g != gcur) {
+      if (gcur >= 0) tot = fmaf(part, __ldg(scale + static_cast<long long>(j) * gpr + gcur), tot);
+      part = 0.f;
+      gcur = g;
+    }
+    int byte, hi;
+    const int gs = g * group;
+    const int gend = gs + group < k ? gs + group : k;
+    const int bs = gs + (p - gs) / 32 * 32;
+    if (ORDER == 1 && bs + 32 <= gend) {
+      const int t = p - bs;
+      byte = bs / 2 + ((t & 16) >> 1) + ((t & 7) >> 1);
+      hi = (t & 1) == 0;
+    } else {
+      byte = p / 2;
+      hi = p & 1;
+    }
+    const uint32_t bv = __ldg(pr + byte);
+    const int nib = hi ? (bv >> 4) & 15 : bv & 15;
+    part = fmaf(__ldg(ar + p), static_cast<float>(nib > 7 ? nib - 16 : nib), part);
+  }
+  if (gcur >= 0) tot = fmaf(part, __ldg(scale + static_cast<long long>(j) * gpr + gcur), tot);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  if (lane == 0) c[static_cast<long long>(i) * n + j] = tot;
+}
+
+// ------------------------------------------------- int8 + outlier columns
+//
+// After the int8 GEMM has written c (tests/src/quant.rs:524-565 computes the
+// int8 body times scale first), c[i][j] += a[i][idx[t]] * w(j, t) for t in list
+// order, each product rounded and then added, as the reference does. w(j, t)
+// is wo[j * n_idx + t] for the compact outlier matrix, or w[j * k + idx[t]]
+// for the full f32 weight. A thread per weight row j and kOutRows token rows;
+// the listed activation columns are staged in shared memory kOutChunk at a
+// time. An index >= k records kDevIdxRange and adds nothing for that entry.
+constexpr int kOutRows = 8;
+constexpr int kOutChunk = 512;
+
+__global__ void __launch_bounds__(256) outlier_add_kernel(const float* __restrict__ a, const float* __restrict__ w,
+                                                          int compact, const uint32_t* __restrict__ idx, int n_idx,
+                                                          float* __restrict__ c, int m, int n, int k,
+                                                          int* __restrict__ err) {
+  __shared__ float s_a[kOutRows][kOutChunk];
+  __shared__ int s_ok[kOutChunk];
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const int m0 = blockIdx.y * kOutRows;
+  const int rows_m = m - m0 < kOutRows ? m - m0 : kOutRows;
+  const int j = blockIdx.x * blockDim.x + static_cast<int>(threadIdx.x);
+  float v[kOutRows];
+#pragma unroll
+  for (int r = 0; r < kOutRows; ++r) v[r] = (j < n && r < rows_m) ? c[static_cast<long long>(m0 + r) * n + j] : 0.f;
+  for (int t0 = 0; t0 < n_idx; t0 += kOutChunk) {
+    const int tn = n_idx - t0 < kOutChunk ? n_idx - t0 : kOutChunk;
+    __syncthreads();
+    for (int e = static_cast<int>(threadIdx.x); e < tn; e += blockDim.x) {
+      const uint32_t col = __ldg(idx + t0 + e);
+      const int ok = col < static_cast<uint32_t>(k);
+      s_ok[e] = ok;
+      if (!ok && blockIdx.x == 0 && blockIdx.y == 0) atomicCAS(err, 0, kDevIdxRange);
+      for (int r = 0; r < kOutRows; ++r)
+        s_a[r][e] = (ok && r < rows_m) ? __ldg(a + static_cast<long long>(m0 + r) * k + col) : 0.f;
+    }
+    __syncthreads();
+    if (j < n) {
+      for (int t = 0; t < tn; ++t) {
+        if (!s_ok[t]) continue;
+        const float wj = compact ? __ldg(w + static_cast<long long>(j) * n_idx + t0 + t)
+                                 : __ldg(w + static_cast<long long>(j) * k + __ldg(idx + t0 + t));
+#pragma unroll
+        for (int r = 0; r < kOutRows; ++r) v[r] = __fadd_rn(v[r], __fmul_rn(s_a[r][t], wj));
+      }
+    }
+  }
+  if (j < n)
+#pragma unroll
+    for (int r = 0; r < kOutRows; ++r)
+      if (r < rows_m) c[static_cast<long long>(m0 + r) * n + j] = v[r];
+}
+
+// wo[j][t] = w[j][idx[t]]: the compact outlier matrix [n][n_idx], built once per
+// weight. An index >= k records kDevIdxRange and writes 0.
+__global__ void __launch_bounds__(256) gather_columns_kernel(const float* __restrict__ w,
+                                                             const uint32_t* __restrict__ idx, int n_idx,
+                                                             float* __restrict__ wo, int n, int k,
+                                                             int* __restrict__ err) {
+  const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= static_cast<long long>(n) * n_idx) return;
+  const int j = static_cast<int>(e / n_idx), t = static_cast<int>(e - static_cast<long long>(j) * n_idx);
+  const uint32_t col = __ldg(idx + t);
+  if (col >= static_cast<uint32_t>(k)) {
+    atomicCAS(err, 0, kDevIdxRange);
+    wo[e] = 0.f;
+    return;
+  }
+  wo[e] = __ldg(w + static_cast<long long>(j) * k + col);
+}
+
+}  // namespace vmlm

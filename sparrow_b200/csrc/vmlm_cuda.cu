@@ -18,6 +18,7 @@
 #include "decode.cuh"
 #include "tc2_gemm.cuh"
 #include "tc_gemm.cuh"
+#include "variants.cuh"
 #include "vm_ops.cuh"
 
 using namespace vmlm;
@@ -159,6 +160,21 @@ int load_encoder() {
   return VMLM_OK;
 }
 
+template <int MB>
+int set_int4_smem_attr() {
+  const int bytes = kI4SmemFloats * 4;
+  VMLM_CUDA(cudaFuncSetAttribute(int4gs_kernel<MB, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  VMLM_CUDA(cudaFuncSetAttribute(int4gs_kernel<MB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return VMLM_OK;
+}
+
+int set_int4_smem_attrs() {
+  VMLM_TRY(set_int4_smem_attr<1>());
+  VMLM_TRY(set_int4_smem_attr<2>());
+  VMLM_TRY(set_int4_smem_attr<4>());
+  return set_int4_smem_attr<8>();
+}
+
 template <TcMode M>
 int set_smem_attr() {
   VMLM_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
@@ -203,6 +219,7 @@ int get_ctx(int dev, Ctx** out) {
   VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kQ8Swap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  VMLM_TRY(set_int4_smem_attrs());
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
   *out = c;
@@ -1050,16 +1067,19 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
 // ------------------------------------------------------------ host API
 
 // Device address for a host range: registered copy, or a staged upload.
-int resolve(Ctx* c, const void* host, size_t bytes, DevBuf& stage, cudaStream_t st, const void** dptr) {
+// The device copy of [host, host + bytes) when a registered weight covers it.
+bool registered_range(Ctx* c, const void* host, size_t bytes, const void** dptr) {
   auto it = g_reg.upper_bound(reinterpret_cast<uintptr_t>(host));
-  if (it != g_reg.begin()) {
-    --it;
-    const uintptr_t h = reinterpret_cast<uintptr_t>(host);
-    if (it->second.dev == c->dev && h >= it->first && h + bytes <= it->first + it->second.bytes) {
-      *dptr = static_cast<const char*>(it->second.dptr) + (h - it->first);
-      return VMLM_OK;
-    }
-  }
+  if (it == g_reg.begin()) return false;
+  --it;
+  const uintptr_t h = reinterpret_cast<uintptr_t>(host);
+  if (it->second.dev != c->dev || h < it->first || h + bytes > it->first + it->second.bytes) return false;
+  *dptr = static_cast<const char*>(it->second.dptr) + (h - it->first);
+  return true;
+}
+
+int resolve(Ctx* c, const void* host, size_t bytes, DevBuf& stage, cudaStream_t st, const void** dptr) {
+  if (registered_range(c, host, bytes, dptr)) return VMLM_OK;
   VMLM_TRY(ensure(stage, bytes));
   VMLM_CUDA(cudaMemcpyAsync(stage.p, host, bytes, cudaMemcpyHostToDevice, st));
   *dptr = stage.p;
@@ -1131,9 +1151,68 @@ size_t pipeline_chunk(size_t m, size_t in_row, size_t out_row, size_t unit = kPi
 
 // The status for a non-zero device error word: the VM's OP_EMB messages, or a
 // kernel that gave up a bounded wait.
+// ------------------------------------------------------- variant kernels
+
+// int4 grouped GEMM: the tiled kernel when every 32-column unit is one
+// reference step inside one group and the packed rows are 16-byte aligned,
+// else the any-shape kernel. MB = token rows per CTA pass (1, 2, 4 or 8).
+template <int MB>
+int launch_int4gs(Ctx* c, const float* a, const uint8_t* packed, const float* scale, float* out, int m, int n, int k,
+                  int group, int gpr, int order, cudaStream_t st) {
+  const int kc_cap = kI4SmemFloats / MB / 32 * 32;
+  const int kc = k < kc_cap ? k : kc_cap;
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(cdiv(n, kI4RowsPerBlock), 4ll * c->sms)),
+                  static_cast<unsigned>(cdiv(m, MB)));
+  const size_t smem = static_cast<size_t>(MB) * kc * 4;
+  if (order)
+    return launch(int4gs_kernel<MB, 1>, grid, dim3(kI4Warps * 32), smem, st, false, a, packed, scale, out, m, n, k,
+                  group, gpr, kc);
+  return launch(int4gs_kernel<MB, 0>, grid, dim3(kI4Warps * 32), smem, st, false, a, packed, scale, out, m, n, k, group,
+                gpr, kc);
+}
+
+int run_int4gs(Ctx* c, const float* a, const uint8_t* packed, const float* scale, float* out, int m, int n, int k,
+               int group, int order, cudaStream_t st) {
+  if (k == 0) {
+    VMLM_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(m) * n * 4, st));
+    return VMLM_OK;
+  }
+  const int gpr = static_cast<int>(cdiv(k, group));
+  if (k % 32 == 0 && group % 32 == 0 && aligned16(packed)) {
+    const int mm = m < 8 ? m : 8;
+    if (mm == 1) return launch_int4gs<1>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
+    if (mm == 2) return launch_int4gs<2>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
+    if (mm <= 4) return launch_int4gs<4>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
+    return launch_int4gs<8>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
+  }
+  const dim3 grid(static_cast<unsigned>(cdiv(static_cast<long long>(m) * n, 8)));
+  if (order)
+    return launch(int4gs_generic_kernel<1>, grid, dim3(256), 0, st, false, a, packed, scale, out, m, n, k, group, gpr);
+  return launch(int4gs_generic_kernel<0>, grid, dim3(256), 0, st, false, a, packed, scale, out, m, n, k, group, gpr);
+}
+
+int check_int4(size_t m, size_t n, size_t k, size_t group, int order) {
+  VMLM_TRY(check_dims(m, n, k));
+  if (group == 0 || group >= (static_cast<size_t>(1) << 31)) return fail(VMLM_ERR_ARG, "int4: group must be >= 1");
+  if (order != 0 && order != 1) return fail(VMLM_ERR_ARG, "int4: order must be 0 (packed) or 1 (AVX2 as shipped)");
+  if (n * ((k + 1) / 2) >= (static_cast<size_t>(1) << 40)) return fail(VMLM_ERR_SHAPE, "int4: weight too large");
+  return VMLM_OK;
+}
+
+// int8 + outlier columns: the Q8 GEMM of the int8 body, then the f32 outlier
+// terms added in list order.
+int run_outlier(Ctx* c, const float* a, const int8_t* q, const float* scale, const float* w, int compact,
+                const uint32_t* idx, int n_idx, float* out, int m, int n, int k, cudaStream_t st) {
+  VMLM_TRY(run_q8(c, a, q, scale, out, m, n, k, st));
+  if (n_idx == 0) return VMLM_OK;
+  const dim3 grid(static_cast<unsigned>(cdiv(n, 256)), static_cast<unsigned>(cdiv(m, kOutRows)));
+  return launch(outlier_add_kernel, grid, dim3(256), 0, st, true, a, w, compact, idx, n_idx, out, m, n, k, c->err);
+}
+
 int device_error(int code) {
   if (code == kDevEmbRange) return fail(VMLM_ERR_OPERATOR, "EMB: row index out of range");
   if (code == kDevEmbFraction) return fail(VMLM_ERR_OPERATOR, "EMB: row index is not an integer");
+  if (code == kDevIdxRange) return fail(VMLM_ERR_ARG, "an outlier column index is >= k");
   return fail(VMLM_ERR_DEVICE_TIMEOUT, "a kernel gave up a bounded wait (device code %d)", code);
 }
 
@@ -1631,6 +1710,113 @@ int vmlm_emb_dev(const void* table, int dtype, size_t rows, size_t cols, const f
   return launch(emb_kernel, dim3(static_cast<unsigned>(m), static_cast<unsigned>(cdiv(cols, 1024))), dim3(256), 0, st,
                 false, table, dtype, static_cast<long long>(rows), static_cast<int>(cols), idx, static_cast<int>(m),
                 out, ctx->err);
+}
+
+int vmlm_gemm_nt_int4_gs(const float* a, const uint8_t* packed, const float* scale, float* c, size_t m, size_t n,
+                         size_t k, size_t group, int order) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_int4(m, n, k, group, order));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !packed || !scale))) return fail(VMLM_ERR_ARG, "gemm_nt_int4_gs: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *dp = nullptr, *ds = nullptr;
+  if (k > 0) {
+    VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+    VMLM_TRY(resolve(ctx, packed, n * ((k + 1) / 2), ctx->h_w, ctx->stream, &dp));
+    VMLM_TRY(resolve(ctx, scale, n * ((k + group - 1) / group) * 4, ctx->h_s, ctx->stream, &ds));
+  }
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  VMLM_TRY(run_int4gs(ctx, static_cast<const float*>(da), static_cast<const uint8_t*>(dp),
+                      static_cast<const float*>(ds), static_cast<float*>(ctx->h_c.p), static_cast<int>(m),
+                      static_cast<int>(n), static_cast<int>(k), static_cast<int>(group), order, ctx->stream));
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int vmlm_gemm_nt_int4_gs_dev(const float* a, const uint8_t* packed, const float* scale, float* c, size_t m, size_t n,
+                             size_t k, size_t group, int order, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_int4(m, n, k, group, order));
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !packed || !scale))) return fail(VMLM_ERR_ARG, "gemm_nt_int4_gs_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_int4gs(ctx, a, packed, scale, c, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                    static_cast<int>(group), order, st);
+}
+
+int vmlm_gemm_nt_int8_outlier(const float* a, const int8_t* q, const float* scale, const float* w,
+                              const uint32_t* idx, size_t n_idx, float* c, size_t m, size_t n, size_t k) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (n_idx > k) return fail(VMLM_ERR_ARG, "gemm_nt_int8_outlier: more outlier columns than k");
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !q || !scale)) || (n_idx > 0 && (!w || !idx)))
+    return fail(VMLM_ERR_ARG, "gemm_nt_int8_outlier: null pointer");
+  for (size_t t = 0; t < n_idx; ++t)
+    if (idx[t] >= k) return fail(VMLM_ERR_ARG, "gemm_nt_int8_outlier: outlier column index %u >= k", idx[t]);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(host_ctx(&ctx));
+  const void *da = nullptr, *dq = nullptr, *ds = nullptr, *dw = nullptr, *di = nullptr;
+  int compact = 0;
+  if (k > 0) {
+    VMLM_TRY(resolve(ctx, a, m * k * 4, ctx->h_a, ctx->stream, &da));
+    VMLM_TRY(resolve(ctx, q, n * k, ctx->h_w, ctx->stream, &dq));
+    VMLM_TRY(resolve(ctx, scale, n * 4, ctx->h_s, ctx->stream, &ds));
+  }
+  std::vector<float> cols;
+  if (n_idx > 0) {
+    VMLM_TRY(resolve(ctx, idx, n_idx * 4, ctx->h_g, ctx->stream, &di));
+    if (!registered_range(ctx, w, n * k * 4, &dw)) {
+      // only the outlier columns the call reads go to the device, as [n][n_idx]
+      cols.resize(n * n_idx);
+      for (size_t j = 0; j < n; ++j)
+        for (size_t t = 0; t < n_idx; ++t) cols[j * n_idx + t] = w[j * k + idx[t]];
+      VMLM_TRY(ensure(ctx->h_b, cols.size() * 4));
+      VMLM_CUDA(cudaMemcpyAsync(ctx->h_b.p, cols.data(), cols.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+      dw = ctx->h_b.p;
+      compact = 1;
+    }
+  }
+  VMLM_TRY(ensure(ctx->h_c, m * n * 4));
+  VMLM_TRY(run_outlier(ctx, static_cast<const float*>(da), static_cast<const int8_t*>(dq),
+                       static_cast<const float*>(ds), static_cast<const float*>(dw), compact,
+                       static_cast<const uint32_t*>(di), static_cast<int>(n_idx), static_cast<float*>(ctx->h_c.p),
+                       static_cast<int>(m), static_cast<int>(n), static_cast<int>(k), ctx->stream));
+  if (!cols.empty()) VMLM_CUDA(cudaStreamSynchronize(ctx->stream));  // cols is pageable
+  return finish_host_call(ctx, c, m * n * 4, nullptr, 0);
+}
+
+int vmlm_gemm_nt_int8_outlier_dev(const float* a, const int8_t* q, const float* scale, const float* w, int compact,
+                                  const uint32_t* idx, size_t n_idx, float* c, size_t m, size_t n, size_t k,
+                                  void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(m, n, k));
+  if (n_idx > k) return fail(VMLM_ERR_ARG, "gemm_nt_int8_outlier_dev: more outlier columns than k");
+  if (m == 0 || n == 0) return VMLM_OK;
+  if (!c || (k > 0 && (!a || !q || !scale)) || (n_idx > 0 && (!w || !idx)))
+    return fail(VMLM_ERR_ARG, "gemm_nt_int8_outlier_dev: null pointer");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return run_outlier(ctx, a, q, scale, w, compact ? 1 : 0, idx, static_cast<int>(n_idx), c, static_cast<int>(m),
+                     static_cast<int>(n), static_cast<int>(k), st);
+}
+
+int vmlm_gather_columns_dev(const float* w, const uint32_t* idx, size_t n_idx, size_t n, size_t k, float* wo,
+                            void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  VMLM_TRY(check_dims(n_idx, n, k));
+  if (n_idx == 0 || n == 0) return VMLM_OK;
+  if (!w || !idx || !wo) return fail(VMLM_ERR_ARG, "gather_columns_dev: null pointer");
+  if (n * n_idx >= (static_cast<size_t>(1) << 40)) return fail(VMLM_ERR_SHAPE, "gather_columns_dev: too large");
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return launch(gather_columns_kernel, dim3(static_cast<unsigned>(cdiv(static_cast<long long>(n * n_idx), 256))),
+                dim3(256), 0, st, false, w, idx, static_cast<int>(n_idx), wo, static_cast<int>(n),
+                static_cast<int>(k), ctx->err);
 }
 
 int vmlm_op_gemm(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot* b, const vmlm_slot* scale) {

@@ -240,6 +240,55 @@ def gemv_f32_dev(a, b, c, m, k, stream=None) -> None:
                                   _dev_ptr(c, "float32", m, "c"), m, k, _stream_ptr(stream)))
 
 
+def gemm_nt_int4_gs(a, packed, scale, c, m, n, k, group, order=0) -> None:
+    """int4 weights, a scale per group of columns (tests/src/quant.rs:298-362); packed
+    [n, (k+1)//2] uint8, scale [n, ceil(k/group)]; order 1 = the AVX2 step as shipped."""
+    gpr = (k + group - 1) // group if group else 0
+    check(lib().vmlm_gemm_nt_int4_gs(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(packed, np.uint8, n * ((k + 1) // 2), "packed"),
+        _host_ptr(scale, np.float32, n * gpr, "scale"), _host_ptr(c, np.float32, m * n, "c"),
+        m, n, k, group, int(order)))
+
+
+def gemm_nt_int4_gs_dev(a, packed, scale, c, m, n, k, group, order=0, stream=None) -> None:
+    gpr = (k + group - 1) // group if group else 0
+    check(lib().vmlm_gemm_nt_int4_gs_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(packed, "uint8", n * ((k + 1) // 2), "packed"),
+        _dev_ptr(scale, "float32", n * gpr, "scale"), _dev_ptr(c, "float32", m * n, "c"),
+        m, n, k, group, int(order), _stream_ptr(stream)))
+
+
+def _idx_dev_ptr(idx, count):
+    if idx is None or isinstance(idx, int):
+        return _dev_ptr(idx, "int32", count, "idx")
+    return _dev_ptr(idx, "uint32" if str(idx.dtype) == "torch.uint32" else "int32", count, "idx")
+
+
+def gemm_nt_int8_outlier(a, q, scale, w, idx, c, m, n, k) -> None:
+    """int8 plus f32 outlier columns (tests/src/quant.rs:524-565); idx uint32 column indices."""
+    idx = np.ascontiguousarray(idx, np.uint32)
+    check(lib().vmlm_gemm_nt_int8_outlier(
+        _host_ptr(a, np.float32, m * k, "a"), _host_ptr(q, np.int8, n * k, "q"),
+        _host_ptr(scale, np.float32, n, "scale"), _host_ptr(w, np.float32, n * k, "w") if idx.size else None,
+        _host_ptr(idx, np.uint32, idx.size, "idx") if idx.size else None, idx.size,
+        _host_ptr(c, np.float32, m * n, "c"), m, n, k))
+
+
+def gemm_nt_int8_outlier_dev(a, q, scale, w, idx, n_idx, c, m, n, k, compact=False, stream=None) -> None:
+    """w: the f32 weight [n, k] (compact False) or the gathered outlier columns [n, n_idx]."""
+    check(lib().vmlm_gemm_nt_int8_outlier_dev(
+        _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(q, "int8", n * k, "q"), _dev_ptr(scale, "float32", n, "scale"),
+        _dev_ptr(w, "float32", n * (n_idx if compact else k), "w") if n_idx else None, int(bool(compact)),
+        _idx_dev_ptr(idx, n_idx) if n_idx else None, n_idx, _dev_ptr(c, "float32", m * n, "c"), m, n, k,
+        _stream_ptr(stream)))
+
+
+def gather_columns_dev(w, idx, n_idx, n, k, wo, stream=None) -> None:
+    """wo[j, t] = w[j, idx[t]] (device tensors)."""
+    check(lib().vmlm_gather_columns_dev(_dev_ptr(w, "float32", n * k, "w"), _idx_dev_ptr(idx, n_idx), n_idx, n, k,
+                                        _dev_ptr(wo, "float32", n * n_idx, "wo"), _stream_ptr(stream)))
+
+
 def emb(table, idx, out) -> None:
     """OP_EMB (core/src/interp.rs:1351-1420) for every index: out[t] = f32(table[idx[t]]);
     table: a [rows, cols] bf16-bit (uint16) or float32 array, idx: float32 row numbers."""

@@ -1,0 +1,269 @@
+"""The quantisation variants of the reference's study (tests/src/quant.rs): int4
+weights with a scale per group of columns, and int8 with f32 outlier columns
+(LLM.int8).
+
+CPU tests pin the oracle restatements to the numbers the reference printed for
+its benchmark (`vmlm-quant`, quoted in docs/VMLM架构白皮书.md §17.4-17.5):
+relative errors against the f32 GEMM of int8 7.2e-4 (uniform weights, hidden
+512) and 4.0e-2 (weights with outlier channels), int4 per-row 1.105e-1 and
+int4 group-32 1.094e-1 (uniform, hidden 512), int8 + outlier columns 2.742e-3,
+3.499e-3, 3.397e-3 at hidden 256, 512, 1024, with 1.56% outlier columns. The
+int4 numbers come out only with the AVX2 step as shipped (order 1), whose
+nibble order differs from the packer's; the packed order (order 0) gives
+~1e-2. GPU tests compare the kernels with the oracle at the relative bound
+TIGHT (f32 sums in another order) and check the host and device calls agree.
+"""
+import numpy as np
+import pytest
+
+import sparrow_b200.kernels as K
+from sparrow_b200._lib import VmlmError
+
+TIGHT = 1e-5      # f32 sums of exact int4 / int8 products, reordered
+TIGHT_Q8 = 2e-5   # the int8 body runs the Q8 path (activations at 2^-22 relative)
+ARG = 1
+
+
+def _rel(O, got, ref):
+    return np.float32(np.max(np.abs(got - ref))) / np.float32(np.max(np.abs(ref)))
+
+
+def _suite_inputs(O, h):
+    """tests/src/quant.rs:578-609: m = 4, n = k = h."""
+    m, n, k = 4, h, h
+    a = O.fill_uniform(m * k, 0xAA, 0.5).reshape(m, k)
+    wu = O.fill_uniform(n * k, 0xBB, np.float32(1.0) / np.sqrt(np.float32(k))).reshape(n, k)
+    wb = O.quant_weights_with_outlier_channels(n, k)
+    return a, wu, wb
+
+
+def test_oracle_reproduces_the_reference_int4_and_int8_errors(oracle):
+    a, wu, wb = _suite_inputs(oracle, 512)
+    k = 512
+    cf = oracle.gemm_nt_f32(a, wu)
+    q8, s8 = oracle.quant_int8(wu)
+    assert f"{_rel(oracle, oracle.gemm_nt_int8(a, q8, s8), cf):.1e}" == "7.2e-04"
+    q4r, s4r = oracle.quant_int4_grouped(wu, k)
+    q4g, s4g = oracle.quant_int4_grouped(wu, 32)
+    assert f"{_rel(oracle, oracle.gemm_nt_int4_gs(a, q4r, s4r, k, k, order=1), cf):.3e}" == "1.105e-01"
+    assert f"{_rel(oracle, oracle.gemm_nt_int4_gs(a, q4g, s4g, k, 32, order=1), cf):.3e}" == "1.094e-01"
+    # the packer's order: the int4 error the reference's design expected
+    assert _rel(oracle, oracle.gemm_nt_int4_gs(a, q4g, s4g, k, 32, order=0), cf) < 2e-2
+    cb = oracle.gemm_nt_f32(a, wb)
+    q8b, s8b = oracle.quant_int8(wb)
+    assert f"{_rel(oracle, oracle.gemm_nt_int8(a, q8b, s8b), cb):.1e}" == "4.0e-02"
+
+
+@pytest.mark.parametrize("h,want", [(256, "2.742e-03"), (512, "3.499e-03"), (1024, "3.397e-03")])
+def test_oracle_reproduces_the_reference_outlier_errors(oracle, h, want):
+    a, _, wb = _suite_inputs(oracle, h)
+    q, s, idx = oracle.quant_int8_outliers(wb, 3.0)
+    assert idx.size == h // 64 and np.array_equal(idx, np.arange(0, h, 64))
+    assert not q[:, idx].any()
+    got = oracle.gemm_nt_int8_outlier(a, q, s, wb, idx)
+    assert f"{_rel(oracle, got, oracle.gemm_nt_f32(a, wb)):.3e}" == want
+
+
+def _effective_weights(oracle, packed, k, group, order):
+    """The int4 value each column uses: a = identity, scale = 1."""
+    n = packed.shape[0]
+    gpr = (k + group - 1) // group
+    return oracle.gemm_nt_int4_gs(np.eye(k, dtype=np.float32), packed, np.ones((n, gpr), np.float32), k, group,
+                                  order).T
+
+
+def _decode(packed, k, group, order):
+    """The documented column -> nibble map, in numpy."""
+    n = packed.shape[0]
+    out = np.empty((n, k), np.float32)
+    for p in range(k):
+        gs = p // group * group
+        gend = min(gs + group, k)
+        bs = gs + (p - gs) // 32 * 32
+        if order == 1 and bs + 32 <= gend:
+            t = p - bs
+            byte, hi = bs // 2 + (t & 16) // 2 + (t & 7) // 2, t % 2 == 0
+        else:
+            byte, hi = p // 2, p % 2 == 1
+        nib = (packed[:, byte] >> 4) & 15 if hi else packed[:, byte] & 15
+        out[:, p] = np.where(nib > 7, nib.astype(np.int32) - 16, nib)
+    return out
+
+
+@pytest.mark.parametrize("k,group", [(64, 32), (96, 64), (100, 100), (70, 33), (33, 8)])
+def test_oracle_int4_nibble_orders(oracle, k, group):
+    rng = np.random.default_rng(k + group)
+    packed = rng.integers(0, 256, (5, (k + 1) // 2), dtype=np.uint8)
+    for order in (0, 1):
+        assert np.array_equal(_effective_weights(oracle, packed, k, group, order), _decode(packed, k, group, order))
+
+
+def test_oracle_int4_quantiser_round_trip(oracle):
+    w = oracle.fill_normal(6 * 70, 3, 1.0).reshape(6, 70)
+    packed, s = oracle.quant_int4_grouped(w, 16)
+    v = _decode(packed, 70, 16, 0)
+    deq = v * np.repeat(s, 16, axis=1)[:, :70]
+    assert np.abs(v).max() <= 7
+    assert np.all(np.abs(deq - w) <= np.repeat(s, 16, axis=1)[:, :70] * 0.5 + 1e-7)
+
+
+def test_variant_argument_guards():
+    a = np.zeros((2, 64), np.float32)
+    c = np.empty((2, 3), np.float32)
+    with pytest.raises(VmlmError) as e:
+        K.gemm_nt_int4_gs(a, np.zeros((3, 32), np.uint8), np.zeros(6, np.float32), c, 2, 3, 64, 0)
+    assert e.value.status == ARG
+    with pytest.raises(VmlmError) as e:
+        K.gemm_nt_int4_gs(a, np.zeros((3, 32), np.uint8), np.zeros(6, np.float32), c, 2, 3, 64, 32, order=2)
+    assert e.value.status == ARG
+    q = np.zeros((3, 64), np.int8)
+    with pytest.raises(VmlmError) as e:
+        K.gemm_nt_int8_outlier(a, q, np.ones(3, np.float32), np.zeros((3, 64), np.float32),
+                               np.array([3, 64], np.uint32), c, 2, 3, 64)
+    assert e.value.status == ARG and "index" in str(e.value)
+
+
+# --------------------------------------------------------------------- GPU
+
+def _int4_case(O, m, n, k, group, seed, outliers=False):
+    a = O.fill_normal(m * k, seed, 1.0).reshape(m, k)
+    w = O.quant_weights_with_outlier_channels(n, k) if outliers else O.fill_normal(n * k, seed + 1, 0.02).reshape(n, k)
+    packed, s = O.quant_int4_grouped(w, group)
+    return a, packed, s
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,group", [
+    (4, 256, 256, 32), (4, 512, 512, 512), (4, 1024, 1024, 32),     # the reference's shapes
+    (1, 5760, 2304, 32), (8, 2304, 2304, 64), (3, 1000, 4096, 128),  # decode layers
+    (16, 777, 640, 32), (2, 333, 96, 96), (5, 4096, 4096, 4096),     # two token-row passes; K staged in two chunks
+])
+@pytest.mark.parametrize("order", [0, 1])
+def test_int4_gs_tiled(kernels, oracle, m, n, k, group, order):
+    a, packed, s = _int4_case(oracle, m, n, k, group, seed=m + n)
+    c = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int4_gs(a, packed, s, c, m, n, k, group, order)
+    assert oracle.max_rel_err(c, oracle.gemm_nt_int4_gs(a, packed, s, k, group, order)) <= TIGHT
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,group", [(4, 100, 100, 100), (3, 77, 70, 33), (2, 50, 33, 8), (9, 40, 1000, 48),
+                                         (1, 1, 1, 1), (4, 64, 96, 16), (17, 31, 65, 65)])
+@pytest.mark.parametrize("order", [0, 1])
+def test_int4_gs_any_shape(kernels, oracle, m, n, k, group, order):
+    a, packed, s = _int4_case(oracle, m, n, k, group, seed=k)
+    c = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int4_gs(a, packed, s, c, m, n, k, group, order)
+    assert oracle.max_rel_err(c, oracle.gemm_nt_int4_gs(a, packed, s, k, group, order)) <= TIGHT
+
+
+@pytest.mark.gpu
+def test_int4_gs_device_calls(kernels, oracle):
+    import torch
+    m, n, k, group = 8, 2304, 2304, 32
+    a, packed, s = _int4_case(oracle, m, n, k, group, seed=5, outliers=True)
+    host = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int4_gs(a, packed, s, host, m, n, k, group, 1)
+    st = torch.cuda.current_stream()
+    da, ds = torch.from_numpy(a).cuda(), torch.from_numpy(s).cuda()
+    dp = torch.from_numpy(packed).cuda()
+    dc = torch.empty((m, n), device="cuda")
+    kernels.gemm_nt_int4_gs_dev(da, dp, ds, dc, m, n, k, group, 1, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(dc.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    # a weight that is not 16-byte aligned takes the any-shape kernel
+    buf = torch.empty(packed.size + 1, dtype=torch.uint8, device="cuda")
+    buf[1:].copy_(dp.reshape(-1))
+    kernels.gemm_nt_int4_gs_dev(da, buf[1:], ds, dc, m, n, k, group, 1, stream=st)
+    kernels.sync(st)
+    assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int4_gs(a, packed, s, k, group, 1)) <= TIGHT
+
+
+@pytest.mark.gpu
+def test_int4_gs_nonfinite_and_empty(kernels, oracle):
+    m, n, k, group = 3, 300, 256, 32
+    a, packed, s = _int4_case(oracle, m, n, k, group, seed=9)
+    a[0, 5] = np.inf
+    a[1, 70] = np.nan
+    c = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int4_gs(a, packed, s, c, m, n, k, group, 0)
+    ref = oracle.gemm_nt_int4_gs(a, packed, s, k, group, 0)
+    assert np.array_equal(np.isnan(c), np.isnan(ref)) and np.array_equal(np.isinf(c), np.isinf(ref))
+    assert oracle.max_rel_err(c[2:], ref[2:]) <= TIGHT
+    z = np.full((2, 5), 7.0, np.float32)
+    kernels.gemm_nt_int4_gs(np.zeros((2, 0), np.float32), np.zeros((5, 0), np.uint8), np.zeros((5, 0), np.float32),
+                            z, 2, 5, 0, 32)
+    assert not z.any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("h", [256, 512, 1024])
+def test_int8_outlier_reference_shapes(kernels, oracle, h):
+    a, _, wb = _suite_inputs(oracle, h)
+    q, s, idx = oracle.quant_int8_outliers(wb, 3.0)
+    c = np.empty((4, h), np.float32)
+    kernels.gemm_nt_int8_outlier(a, q, s, wb, idx, c, 4, h, h)
+    assert oracle.max_rel_err(c, oracle.gemm_nt_int8_outlier(a, q, s, wb, idx)) <= TIGHT_Q8
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k", [(1, 5760, 2304), (8, 2304, 2304), (33, 1000, 520), (300, 2304, 2304)])
+def test_int8_outlier_device_paths(kernels, oracle, m, n, k):
+    import torch
+    a = oracle.fill_normal(m * k, m, 1.0).reshape(m, k)
+    w = oracle.quant_weights_with_outlier_channels(n, k)
+    q, s, idx = oracle.quant_int8_outliers(w, 3.0)
+    ref = oracle.gemm_nt_int8_outlier(a, q, s, w, idx)
+    host = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int8_outlier(a, q, s, w, idx, host, m, n, k)
+    assert oracle.max_rel_err(host, ref) <= TIGHT_Q8
+    st = torch.cuda.current_stream()
+    da, dq, ds, dw = (torch.from_numpy(v).cuda() for v in (a, q, s, w))
+    di = torch.from_numpy(idx.astype(np.int32)).cuda()
+    full = torch.empty((m, n), device="cuda")
+    kernels.gemm_nt_int8_outlier_dev(da, dq, ds, dw, di, idx.size, full, m, n, k, compact=False, stream=st)
+    wo = torch.empty((n, idx.size), device="cuda")
+    kernels.gather_columns_dev(dw, di, idx.size, n, k, wo, stream=st)
+    comp = torch.empty((m, n), device="cuda")
+    kernels.gemm_nt_int8_outlier_dev(da, dq, ds, wo, di, idx.size, comp, m, n, k, compact=True, stream=st)
+    kernels.sync(st)
+    assert np.array_equal(full.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    assert np.array_equal(comp.cpu().numpy().view(np.uint32), host.view(np.uint32))
+    # a registered weight is read in place (full matrix, same bits)
+    kernels.register_weight(w)
+    try:
+        again = np.empty((m, n), np.float32)
+        kernels.gemm_nt_int8_outlier(a, q, s, w, idx, again, m, n, k)
+    finally:
+        kernels.unregister_all()
+    assert np.array_equal(again.view(np.uint32), host.view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_int8_outlier_without_outliers_is_q8(kernels, oracle):
+    m, n, k = 4, 700, 384
+    a = oracle.fill_normal(m * k, 1, 1.0).reshape(m, k)
+    q, s = oracle.quant_int8(oracle.fill_normal(n * k, 2, 0.02).reshape(n, k))
+    c = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int8_outlier(a, q, s, np.zeros((n, k), np.float32), np.zeros(0, np.uint32), c, m, n, k)
+    assert np.array_equal(c.view(np.uint32), kernels.q8_linear(a, q, s).view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_int8_outlier_device_index_check(kernels, oracle):
+    import torch
+    m, n, k = 2, 64, 128
+    a = torch.ones((m, k), device="cuda")
+    q = torch.zeros((n, k), dtype=torch.int8, device="cuda")
+    s = torch.ones(n, device="cuda")
+    wo = torch.ones((n, 2), device="cuda")
+    bad = torch.tensor([5, 128], dtype=torch.int32, device="cuda")  # 128 >= k: recorded, not read
+    c = torch.empty((m, n), device="cuda")
+    st = torch.cuda.current_stream()
+    kernels.gemm_nt_int8_outlier_dev(a, q, s, wo, bad, 2, c, m, n, k, compact=True, stream=st)
+    with pytest.raises(VmlmError) as e:
+        kernels.sync(st)
+    assert e.value.status == ARG
+    kernels.gemm_nt_int8_outlier_dev(a, q, s, wo, bad[:1], 1, c, m, n, k, compact=True, stream=st)
+    kernels.sync(st)
+    assert torch.all(c == 1.0)
