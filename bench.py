@@ -263,6 +263,35 @@ def quantise_rows(w):
     return q.contiguous(), s.contiguous()
 
 
+def quantise_int4_groups(w, group):
+    """tests/src/quant.rs:114-152 on the GPU (input preparation only): absmax/7 per
+    group of columns, round half away from zero, clamp to [-7, 7], two's-complement
+    nibbles, column p in the low nibble of byte p/2 when p is even."""
+    import torch
+    n, k = w.shape
+    gpr = (k + group - 1) // group
+    wp = torch.nn.functional.pad(w, (0, gpr * group - k)).view(n, gpr, group)
+    amax = wp.abs().amax(dim=2)
+    amax = torch.where(amax == 0, torch.full_like(amax, 1e-30), amax)
+    s = (amax / 7.0).float()
+    v = wp / s[:, :, None]
+    q = (torch.sign(v) * torch.floor(v.abs() + 0.5)).clamp_(-7, 7).to(torch.int32).view(n, gpr * group)[:, :k]
+    nib = torch.nn.functional.pad(q & 15, (0, k % 2))
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).to(torch.uint8)
+    return packed.contiguous(), s.contiguous()
+
+
+def quantise_int8_outliers(w, thresh):
+    """tests/src/quant.rs:458-515 on the GPU (input preparation only): columns whose
+    RMS exceeds thresh x the mean column RMS are outliers; the others are quantised
+    per row, the outliers to 0. Returns q, scale and the outlier columns (int32)."""
+    import torch
+    col = (w.double() ** 2).mean(0).sqrt()
+    outl = col > thresh * col.mean()
+    q, s = quantise_rows(w.masked_fill(outl[None, :], 0.0))
+    return q, s, torch.nonzero(outl).flatten().to(torch.int32).contiguous()
+
+
 def gen(shape, seed, sigma):
     import torch
     g = torch.Generator(device="cuda")
@@ -526,7 +555,55 @@ def bench_configs(K, dist, rank, world, flush, pk):
                                    "sample": "one full run of the restated gemm_nt_scalar (ops/src/kernels.rs:947-967)"}
         res[name] = entry
         del a, b
+    # quantisation variants (tests/src/quant.rs): int4 with a scale per 32
+    # columns, and int8 with f32 outlier columns, on weights with outlier
+    # channels (every 64th column x 12, :595-609); the reference's benchmark
+    # shape (m = 4, n = k = 512) and decode-layer shapes
+    for m, n, k in ((4, 512, 512), (1, 5760, 2304), (8, 5760, 2304)):
+        w = gen((n, k), 11, 1.0 / float(np.sqrt(k)))
+        w[:, ::64] *= 12.0
+        a = gen((m, k), 12, 0.5)
+        c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        packed, s4 = quantise_int4_groups(w, 32)
+        step = lambda: K.gemm_nt_int4_gs_dev(a, packed, s4, c, m, n, k, 32, 0, stream=st)  # noqa: E731
+        t = time_steps(step, 50, 5, flush, dist)
+        nbytes = packed.numel() + 4 * s4.numel() + 4 * m * k + 4 * m * n
+        entry = {"bytes": nbytes, "step_us": t * 1e3, "GBps": nbytes / t / 1e6, "frac_hbm": nbytes / t / 1e6 / hbm,
+                 "GFLOPS": 2 * m * n * k / t / 1e6, "launches": 1}
+        if rank == 0 and world == 1 and m == 4:
+            from oracle import oracle as O
+            an, pn, sn = a.cpu().numpy(), packed.cpu().numpy(), s4.cpu().numpy()
+            best = min(timed_call(lambda: O.gemm_nt_int4_gs(an, pn, sn, k, 32, order=1)) for _ in range(20))
+            entry["cpu_oracle"] = {"value": 2 * m * n * k / best / 1e9, "unit": "GFLOP/s", "cores": 1, "kind": "port",
+                                   "sample": "best of 20 runs of the restated AVX2 gemm_nt_int4_gs "
+                                             "(tests/src/quant.rs:298-362), single thread as shipped"}
+        res[f"V_int4_g32_{m}x{n}x{k}"] = entry
+        q, s, idx = quantise_int8_outliers(w, 3.0)
+        wo = torch.empty((n, idx.numel()), dtype=torch.float32, device="cuda")
+        K.gather_columns_dev(w, idx, idx.numel(), n, k, wo, stream=st)
+        step = lambda: K.gemm_nt_int8_outlier_dev(a, q, s, wo, idx, idx.numel(), c, m, n, k,  # noqa: E731
+                                                  compact=True, stream=st)
+        t = time_steps(step, 50, 5, flush, dist)
+        nbytes = n * k + 4 * n + 4 * wo.numel() + 4 * idx.numel() + 4 * m * k + 4 * m * n
+        entry = {"bytes": nbytes, "outlier_columns": idx.numel(), "step_us": t * 1e3, "GBps": nbytes / t / 1e6,
+                 "frac_hbm": nbytes / t / 1e6 / hbm, "GFLOPS": 2 * m * n * k / t / 1e6}
+        if rank == 0 and world == 1 and m == 4:
+            from oracle import oracle as O
+            an, qn, sn, wn, idn = (v.cpu().numpy() for v in (a, q, s, w, idx))
+            idn = idn.astype(np.uint32)
+            best = min(timed_call(lambda: O.gemm_nt_int8_outlier(an, qn, sn, wn, idn)) for _ in range(20))
+            entry["cpu_oracle"] = {"value": 2 * m * n * k / best / 1e9, "unit": "GFLOP/s", "cores": 1, "kind": "port",
+                                   "sample": "best of 20 runs of the restated gemm_nt_int8_outlier "
+                                             "(tests/src/quant.rs:524-565), single thread as shipped"}
+        res[f"V_int8_outlier_{m}x{n}x{k}"] = entry
+        del w, a, c, packed, s4, q, s, idx, wo
     return res
+
+
+def timed_call(fn):
+    t0 = time.perf_counter()
+    fn()
+    return time.perf_counter() - t0
 
 
 def run_ours(args):

@@ -67,6 +67,7 @@ SIGNATURES = {
     "vmlm_gemv_f32_dev": (I, [P, P, P, S, S, P]),
     "vmlm_emb": (I, [P, I, S, S, P, S, P]),
     "vmlm_emb_dev": (I, [P, I, S, S, P, S, P, P]),
+    "vmlm_set_host_pipeline": (I, [I]),
     "vmlm_gemm_nt_int4_gs": (I, [P, P, P, P, S, S, S, S, I]),
     "vmlm_gemm_nt_int4_gs_dev": (I, [P, P, P, P, S, S, S, S, I, P]),
     "vmlm_gemm_nt_int8_outlier": (I, [P, P, P, P, P, S, P, S, S, S]),

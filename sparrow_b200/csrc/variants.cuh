@@ -29,35 +29,39 @@ constexpr int kDevIdxRange = 103;  // an outlier column index >= k
 // `order` 1 reproduces the step as shipped, 0 uses the packed order.
 
 constexpr int kI4Warps = 8;
-constexpr int kI4RowsPerWarp = 2;
-constexpr int kI4RowsPerBlock = kI4Warps * kI4RowsPerWarp;
 constexpr int kI4SmemFloats = 24576;  // 96 KB of staged activations per CTA
+constexpr int kI4LanesPerRow = 8;     // a weight row's 32-column units go to 8 lanes
+constexpr int kI4RowsPerBlock = kI4Warps * 32 / kI4LanesPerRow;
 
 // Swap the two nibbles of every byte.
 __device__ __forceinline__ uint32_t nib_swap(uint32_t w) { return ((w >> 4) & 0x0F0F0F0Fu) | ((w & 0x0F0F0F0Fu) << 4); }
 
-// Column class c = p % 8 of a 32-column unit: the nibble sits at bits 4c of its
-// word for c < 3 and at bits 4(c-3) of the word shifted right by 12 for c >= 3,
-// so f = 2^23 + u * 2^(4c') with u = nibble ^ 8 and c' = c < 3 ? c : c - 3, and
-// f - (2^23 + 8 * 2^(4c')) = v * 2^(4c') exactly (v the signed nibble). The
-// staged activations carry the factor 2^-(4c'), so a' * (v 2^(4c')) = a * v
-// with the same rounding (power-of-two scaling is exact).
-__host__ __device__ constexpr int i4_shift(int c) { return c < 3 ? 4 * c : 4 * (c - 3); }
+// Column class c = p % 8 of a 32-column unit: its nibble sits at bits sh = 4c
+// of the word for c < 5 and at bits sh = 4c - 12 of the word shifted right by
+// 12 for c >= 5 (sh <= 16). One LOP3 per column, (src & (0xF << sh)) ^
+// (0x4B000000 | 8 << sh), gives the float f = 2^23 + (nibble ^ 8) * 2^sh, and
+// f - (2^23 + 8 * 2^sh) = v * 2^sh exactly (v the signed nibble). The staged
+// activations carry the factor 2^-sh, so a' * (v 2^sh) = a * v with the same
+// rounding (power-of-two scaling is exact).
+__host__ __device__ constexpr int i4_shift(int c) { return c < 5 ? 4 * c : 4 * c - 12; }
 
 __device__ __forceinline__ float i4_val(uint32_t w, uint32_t w12, int c) {
-  const uint32_t src = c < 3 ? w : w12;
+  const uint32_t src = c < 5 ? w : w12;
   const int sh = i4_shift(c);
-  const float f = __uint_as_float(0x4B000000u | (src & (0xFu << sh)));
+  const float f = __uint_as_float((src & (0xFu << sh)) ^ (0x4B000000u | (0x8u << sh)));
   return f - (8388608.0f + 8.0f * static_cast<float>(1 << sh));
 }
 
-// Fast path: k % 32 == 0, group % 32 == 0, 16-byte aligned packed rows (so
-// every 32-column unit lies inside one group and is one reference step).
-// Grid (row-set CTAs, ceil(m / MB)); a warp owns kI4RowsPerWarp weight rows
-// and its lanes take 32-column units lane, lane + 32, ...; the activations of
-// MB token rows are staged in shared memory in chunks of kc columns, float4 f
-// of a row stored at f ^ ((f >> 3) & 7) so a quarter-warp's float4 reads of
-// eight consecutive units hit eight different bank groups.
+// Fast path: k % 32 == 0, group % 32 == 0, 16-byte aligned rows (so every
+// 32-column unit lies inside one group and is one reference step). Grid
+// (row-set CTAs, ceil(m / MB)); lane l of a warp works on weight row
+// 4 * warp + l / 8 of the CTA's row set and takes its units l % 8, l % 8 + 8,
+// ..., the next unit's weights loaded before the current one is computed. The
+// activations of MB token rows are staged in shared memory in chunks of kc
+// columns, a unit's eight float4 at a stride of nine float4 per unit: the
+// eight units a warp reads at once hit eight different bank groups, the four
+// lanes on the same unit (one per weight row) read the same words
+// (broadcast), and a unit's reads are one base address plus constants.
 template <int MB, int ORDER>
 __global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __restrict__ a,
                                                                const uint8_t* __restrict__ packed,
@@ -69,20 +73,39 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __re
   const int m0 = blockIdx.y * MB;
   const int rows_m = m - m0 < MB ? m - m0 : MB;
   const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const int u0 = lane % kI4LanesPerRow;
   const long long rowbytes = k / 2;
-  const int kc4 = kc / 4;
+  const int rs = kc / 32 * 9;  // float4 per staged token row
   const bool one_chunk = kc >= k;
 
   auto stage = [&](int kc0, int kcn) {
-    // a'[r][p] = a[m0 + r][kc0 + p] * 2^-(i4_shift(p % 8)); rows past m are zero
-    for (int e = static_cast<int>(threadIdx.x); e < MB * kcn; e += blockDim.x) {
-      const int r = e / kcn, p = e - r * kcn;
-      float v = 0.f;
-      if (r < rows_m) v = __ldg(a + static_cast<long long>(m0 + r) * k + kc0 + p);
-      const int sh = i4_shift(p & 7);
-      v *= __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-      const int f = p >> 2;
-      reinterpret_cast<float*>(s_a4)[(r * kc4 + (f ^ ((f >> 3) & 7))) * 4 + (p & 3)] = v;
+    // a'[r][p] = a[m0 + r][kc0 + p] * 2^-(i4_shift(p % 8)); rows past m are zero.
+    // float4 f covers columns 4f .. 4f+3 (classes 0-3 or 4-7 of its unit).
+    const int kcn4 = kcn / 4;
+    constexpr int kUnroll = 4;
+    for (int e0 = static_cast<int>(threadIdx.x); e0 < MB * kcn4; e0 += kUnroll * blockDim.x) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int q = 0; q < kUnroll; ++q) {
+        const int e = e0 + q * static_cast<int>(blockDim.x);
+        const int r = e / kcn4, f = e - r * kcn4;
+        v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < MB * kcn4 && r < rows_m)
+          v[q] = __ldg(reinterpret_cast<const float4*>(a + static_cast<long long>(m0 + r) * k + kc0) + f);
+      }
+#pragma unroll
+      for (int q = 0; q < kUnroll; ++q) {
+        const int e = e0 + q * static_cast<int>(blockDim.x);
+        if (e >= MB * kcn4) break;
+        const int r = e / kcn4, f = e - r * kcn4;
+        const int c0 = (f & 1) * 4;  // column class of the float4's first column
+        float4 x = v[q];
+        x.x *= __uint_as_float(static_cast<uint32_t>(127 - i4_shift(c0)) << 23);
+        x.y *= __uint_as_float(static_cast<uint32_t>(127 - i4_shift(c0 + 1)) << 23);
+        x.z *= __uint_as_float(static_cast<uint32_t>(127 - i4_shift(c0 + 2)) << 23);
+        x.w *= __uint_as_float(static_cast<uint32_t>(127 - i4_shift(c0 + 3)) << 23);
+        s_a4[r * rs + (f >> 3) * 9 + (f & 7)] = x;
+      }
     }
   };
 
@@ -91,12 +114,12 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __re
     __syncthreads();
   }
   for (int j0 = blockIdx.x * kI4RowsPerBlock; j0 < n; j0 += gridDim.x * kI4RowsPerBlock) {
-    const int jw = j0 + warp * kI4RowsPerWarp;
-    float tot[kI4RowsPerWarp][MB];
+    const int jwarp = j0 + warp * (32 / kI4LanesPerRow);
+    const int j = jwarp + lane / kI4LanesPerRow;
+    const int jr = j < n ? j : n - 1;  // a past-the-end row reads row n-1 and is not stored
+    float tot[MB];
 #pragma unroll
-    for (int r = 0; r < kI4RowsPerWarp; ++r)
-#pragma unroll
-      for (int i = 0; i < MB; ++i) tot[r][i] = 0.f;
+    for (int i = 0; i < MB; ++i) tot[i] = 0.f;
     for (int kc0 = 0; kc0 < k; kc0 += kc) {
       const int kcn = k - kc0 < kc ? k - kc0 : kc;
       if (!one_chunk) {
@@ -104,70 +127,59 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __re
         stage(kc0, kcn);
         __syncthreads();
       }
-      if (jw < n) {
-        for (int u = lane; u < kcn / 32; u += 32) {
-          const int ug = kc0 / 32 + u;
-          const int g = ug * 32 / group;
-          uint4 wv[kI4RowsPerWarp];
-          float sc[kI4RowsPerWarp];
-#pragma unroll
-          for (int r = 0; r < kI4RowsPerWarp; ++r) {
-            const int j = jw + r < n ? jw + r : n - 1;  // a past-the-end row reads row n-1 and is not stored
-            wv[r] = __ldg(reinterpret_cast<const uint4*>(packed + j * rowbytes) + ug);
-            sc[r] = __ldg(scale + static_cast<long long>(j) * gpr + g);
-            if (ORDER == 1) {
-              const uint32_t x0 = nib_swap(wv[r].x), x2 = nib_swap(wv[r].z);
-              wv[r] = make_uint4(x0, x0, x2, x2);
-            }
-            wv[r].x ^= 0x88888888u;
-            wv[r].y ^= 0x88888888u;
-            wv[r].z ^= 0x88888888u;
-            wv[r].w ^= 0x88888888u;
+      const int units = kcn / 32;
+      if (jwarp < n && u0 < units) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(packed + jr * rowbytes) + kc0 / 32;
+        const float* srow = scale + static_cast<long long>(jr) * gpr;
+        uint4 wv = __ldg(wrow + u0);
+        float sc = __ldg(srow + (kc0 + u0 * 32) / group);
+        for (int u = u0; u < units; u += kI4LanesPerRow) {
+          uint4 wn = wv;
+          float sn = sc;
+          if (u + kI4LanesPerRow < units) {
+            wn = __ldg(wrow + u + kI4LanesPerRow);
+            sn = __ldg(srow + (kc0 + (u + kI4LanesPerRow) * 32) / group);
           }
-          float part[kI4RowsPerWarp][MB];
+          if (ORDER == 1) {
+            const uint32_t x0 = nib_swap(wv.x), x2 = nib_swap(wv.z);
+            wv = make_uint4(x0, x0, x2, x2);
+          }
+          const float4* sa = s_a4 + u * 9;
+          float part[MB];
 #pragma unroll
-          for (int r = 0; r < kI4RowsPerWarp; ++r)
-#pragma unroll
-            for (int i = 0; i < MB; ++i) part[r][i] = 0.f;
+          for (int i = 0; i < MB; ++i) part[i] = 0.f;
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
-            float4 av[MB];
+            const uint32_t w = (v >> 1) == 0 ? wv.x : (v >> 1) == 1 ? wv.y : (v >> 1) == 2 ? wv.z : wv.w;
+            const uint32_t w12 = w >> 12;
+            const int c0 = (v & 1) * 4;
+            const float d0 = i4_val(w, w12, c0), d1 = i4_val(w, w12, c0 + 1);
+            const float d2 = i4_val(w, w12, c0 + 2), d3 = i4_val(w, w12, c0 + 3);
 #pragma unroll
-            for (int i = 0; i < MB; ++i) av[i] = s_a4[i * kc4 + u * 8 + (v ^ (u & 7))];
-#pragma unroll
-            for (int r = 0; r < kI4RowsPerWarp; ++r) {
-              const uint32_t w = (v >> 1) == 0 ? wv[r].x : (v >> 1) == 1 ? wv[r].y : (v >> 1) == 2 ? wv[r].z : wv[r].w;
-              const uint32_t w12 = w >> 12;
-              const int c0 = (v & 1) * 4;
-              const float d0 = i4_val(w, w12, c0), d1 = i4_val(w, w12, c0 + 1);
-              const float d2 = i4_val(w, w12, c0 + 2), d3 = i4_val(w, w12, c0 + 3);
-#pragma unroll
-              for (int i = 0; i < MB; ++i) {
-                float s = part[r][i];
-                s = fmaf(av[i].x, d0, s);
-                s = fmaf(av[i].y, d1, s);
-                s = fmaf(av[i].z, d2, s);
-                s = fmaf(av[i].w, d3, s);
-                part[r][i] = s;
-              }
+            for (int i = 0; i < MB; ++i) {
+              const float4 av = sa[i * rs + v];
+              float s = part[i];
+              s = fmaf(av.x, d0, s);
+              s = fmaf(av.y, d1, s);
+              s = fmaf(av.z, d2, s);
+              s = fmaf(av.w, d3, s);
+              part[i] = s;
             }
           }
 #pragma unroll
-          for (int r = 0; r < kI4RowsPerWarp; ++r)
-#pragma unroll
-            for (int i = 0; i < MB; ++i) tot[r][i] = fmaf(part[r][i], sc[r], tot[r][i]);
+          for (int i = 0; i < MB; ++i) tot[i] = fmaf(part[i], sc, tot[i]);
+          wv = wn;
+          sc = sn;
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < kI4RowsPerWarp; ++r)
+    for (int i = 0; i < MB; ++i) {
+      float s = tot[i];
 #pragma unroll
-      for (int i = 0; i < MB; ++i) {
-        float s = tot[r][i];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0 && jw + r < n && i < rows_m) c[static_cast<long long>(m0 + i) * n + jw + r] = s;
-      }
+      for (int o = kI4LanesPerRow / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (u0 == 0 && j < n && i < rows_m) c[static_cast<long long>(m0 + i) * n + j] = s;
+    }
   }
 }
 

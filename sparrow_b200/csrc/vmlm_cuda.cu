@@ -1097,6 +1097,7 @@ int finish_host_call(Ctx* c, float* host_c, size_t c_bytes, int32_t* host_acc, s
 
 constexpr size_t kPipeChunkRows = 128;  // rows per chunk of a pipelined host call (a multiple)
 constexpr size_t kPipeMaxChunks = 8;
+std::atomic<int> g_pipe_chunks{4};      // most chunks per pipelined call (vmlm_set_host_pipeline)
 
 template <class F>
 int host_pipeline(Ctx* c, size_t m, size_t chunk, const void* host_in, void* din, size_t in_row, void* host_out,
@@ -1143,9 +1144,10 @@ int host_pipeline(Ctx* c, size_t m, size_t chunk, const void* host_in, void* din
 
 // Rows per chunk of a pipelined host call, 0 for a call too small to gain.
 size_t pipeline_chunk(size_t m, size_t in_row, size_t out_row, size_t unit = kPipeChunkRows) {
-  if (m < 256 || m * (in_row + out_row) < (static_cast<size_t>(2) << 20)) return 0;
+  const size_t most = static_cast<size_t>(g_pipe_chunks.load());
+  if (most < 2 || m < 2 * unit || m * (in_row + out_row) < (static_cast<size_t>(2) << 20)) return 0;
   size_t chunk = unit;
-  while (m / chunk > kPipeMaxChunks) chunk += unit;
+  while (m / chunk > most) chunk += unit;
   return chunk;
 }
 
@@ -1154,16 +1156,17 @@ size_t pipeline_chunk(size_t m, size_t in_row, size_t out_row, size_t unit = kPi
 // ------------------------------------------------------- variant kernels
 
 // int4 grouped GEMM: the tiled kernel when every 32-column unit is one
-// reference step inside one group and the packed rows are 16-byte aligned,
-// else the any-shape kernel. MB = token rows per CTA pass (1, 2, 4 or 8).
+// reference step inside one group and the packed and activation rows are
+// 16-byte aligned, else the any-shape kernel. MB = token rows per CTA pass (1, 2, 4 or 8).
 template <int MB>
 int launch_int4gs(Ctx* c, const float* a, const uint8_t* packed, const float* scale, float* out, int m, int n, int k,
                   int group, int gpr, int order, cudaStream_t st) {
-  const int kc_cap = kI4SmemFloats / MB / 32 * 32;
+  // a staged token row takes 9 float4 (144 bytes) per 32-column unit
+  const int kc_cap = kI4SmemFloats * 4 / (MB * 144) * 32;
   const int kc = k < kc_cap ? k : kc_cap;
-  const dim3 grid(static_cast<unsigned>(std::min<long long>(cdiv(n, kI4RowsPerBlock), 4ll * c->sms)),
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(cdiv(n, kI4RowsPerBlock), 8ll * c->sms)),
                   static_cast<unsigned>(cdiv(m, MB)));
-  const size_t smem = static_cast<size_t>(MB) * kc * 4;
+  const size_t smem = static_cast<size_t>(MB) * (kc / 32) * 144;
   if (order)
     return launch(int4gs_kernel<MB, 1>, grid, dim3(kI4Warps * 32), smem, st, false, a, packed, scale, out, m, n, k,
                   group, gpr, kc);
@@ -1178,7 +1181,7 @@ int run_int4gs(Ctx* c, const float* a, const uint8_t* packed, const float* scale
     return VMLM_OK;
   }
   const int gpr = static_cast<int>(cdiv(k, group));
-  if (k % 32 == 0 && group % 32 == 0 && aligned16(packed)) {
+  if (k % 32 == 0 && group % 32 == 0 && aligned16(packed) && aligned16(a)) {
     const int mm = m < 8 ? m : 8;
     if (mm == 1) return launch_int4gs<1>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
     if (mm == 2) return launch_int4gs<2>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);
@@ -1985,6 +1988,13 @@ int vmlm_sharded_gemm_i8i8_dev(const int8_t* x, const int8_t* w_shard, const flo
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return run_i8i8(ctx, x, w_shard, scale_shard, nullptr, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                   static_cast<int>(k), st, &sh);
+}
+
+int vmlm_set_host_pipeline(int max_chunks) {
+  if (max_chunks < 0 || max_chunks > static_cast<int>(kPipeMaxChunks))
+    return fail(VMLM_ERR_ARG, "set_host_pipeline: max_chunks must be in [0, %d]", static_cast<int>(kPipeMaxChunks));
+  g_pipe_chunks.store(max_chunks == 0 ? 4 : max_chunks);
+  return VMLM_OK;
 }
 
 int vmlm_sync(void* stream) {

@@ -240,6 +240,11 @@ def gemv_f32_dev(a, b, c, m, k, stream=None) -> None:
                                   _dev_ptr(c, "float32", m, "c"), m, k, _stream_ptr(stream)))
 
 
+def set_host_pipeline(max_chunks: int) -> None:
+    """Most row chunks a large host-pointer call is pipelined in (1 = off, 0 = default)."""
+    check(lib().vmlm_set_host_pipeline(int(max_chunks)))
+
+
 def gemm_nt_int4_gs(a, packed, scale, c, m, n, k, group, order=0) -> None:
     """int4 weights, a scale per group of columns (tests/src/quant.rs:298-362); packed
     [n, (k+1)//2] uint8, scale [n, ceil(k/group)]; order 1 = the AVX2 step as shipped."""
