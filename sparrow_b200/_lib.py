@@ -68,6 +68,16 @@ SIGNATURES = {
     "vmlm_emb": (I, [P, I, S, S, P, S, P]),
     "vmlm_emb_dev": (I, [P, I, S, S, P, S, P, P]),
     "vmlm_set_host_pipeline": (I, [I]),
+    "vmlm_pool_load": (I, [P, S, P, S, P]),
+    "vmlm_pool_free": (I, [P]),
+    "vmlm_pool_info": (I, [P, P, P, P]),
+    "vmlm_pool_region": (I, [P, I, P]),
+    "vmlm_pool_slot": (I, [P, S, P, P]),
+    "vmlm_pool_layerb": (I, [P, ctypes.c_float]),
+    "vmlm_pool_layer_base": (I, [P, P]),
+    "vmlm_pool_find_const": (I, [P, ctypes.c_char_p, P]),
+    "vmlm_pool_find_slot": (I, [P, ctypes.c_char_p, P]),
+    "vmlm_pool_gemm": (I, [P, P, P]),
     "vmlm_gemm_nt_int4_gs": (I, [P, P, P, P, S, S, S, S, I]),
     "vmlm_gemm_nt_int4_gs_dev": (I, [P, P, P, P, S, S, S, S, I, P]),
     "vmlm_gemm_nt_int8_outlier": (I, [P, P, P, P, P, S, P, S, S, S]),

@@ -19,6 +19,7 @@
 #include "tc2_gemm.cuh"
 #include "tc_gemm.cuh"
 #include "variants.cuh"
+#include "vmb_pool.cuh"
 #include "vm_ops.cuh"
 
 using namespace vmlm;
@@ -1325,7 +1326,186 @@ int op_gemm(unsigned fl, const vmlm_slot* d, const vmlm_slot* a, const vmlm_slot
 
 // =================================================================== C ABI
 
+// A .vmb program's constant pool and scratch regions in device memory, with its
+// slot table (Vm::load, core/src/interp.rs:123-220) and the OP_LAYERB base.
+struct vmlm_pool {
+  int dev = -1;
+  vmlm::VmbLayout L;
+  void* region[4] = {nullptr, nullptr, nullptr, nullptr};  // const, act, state, grad
+  uint64_t layer_base = 0;
+};
+
+namespace {
+
+void pool_release(vmlm_pool* p) {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (p->dev >= 0) cudaSetDevice(p->dev);
+  for (void*& r : p->region)
+    if (r) {
+      cudaFree(r);
+      r = nullptr;
+    }
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+// The device slot i of the pool, with the layer base applied to CONSTANT slots
+// and bound-checked as const_ptr_based does (core/src/interp.rs:453-479).
+int pool_slot(const vmlm_pool* p, size_t i, vmlm_slot* out, int* kind) {
+  if (i >= p->L.slots.size()) return fail(VMLM_ERR_ARG, "pool: slot %zu past the slot table (%zu slots)", i,
+                                          p->L.slots.size());
+  const vmlm::VmbSlot& s = p->L.slots[i];
+  const bool cst = s.kind == vmlm::kVmbSlotConst || s.kind == vmlm::kVmbSlotParam;
+  const int r = cst ? 0 : s.kind == vmlm::kVmbSlotState ? 2 : s.kind == vmlm::kVmbSlotGrad ? 3 : 1;
+  uint64_t off = s.off;
+  if (s.kind == vmlm::kVmbSlotConst && p->layer_base != 0) {
+    const uint64_t bytes = static_cast<uint64_t>(s.rows) * s.cols * vmlm::vmb_dtype_size(s.dtype);
+    if (off + p->layer_base < off || off + p->layer_base + bytes > p->L.const_len)
+      return fail(VMLM_ERR_OPERATOR, "layer base walks past the constant pool: off=%llu base=%llu bytes=%llu limit=%llu",
+                  static_cast<unsigned long long>(off), static_cast<unsigned long long>(p->layer_base),
+                  static_cast<unsigned long long>(bytes), static_cast<unsigned long long>(p->L.const_len));
+    off += p->layer_base;
+  }
+  if (out) {
+    out->ptr = static_cast<char*>(p->region[r]) + off;
+    out->rows = s.rows;
+    out->cols = s.cols;
+    out->dtype = s.dtype;
+  }
+  if (kind) *kind = static_cast<int>(s.kind);
+  return VMLM_OK;
+}
+
+}  // namespace
+
 extern "C" {
+
+int vmlm_pool_load(const void* vmb, size_t len, const void* weights, size_t weights_len, vmlm_pool** out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!out) return fail(VMLM_ERR_ARG, "pool_load: null out");
+  *out = nullptr;
+  if (!vmb) return fail(VMLM_ERR_ARG, "pool_load: null image");
+  vmlm::VmbLayout L;
+  const char* msg = "";
+  const int rc = vmlm::vmb_parse(static_cast<const uint8_t*>(vmb), len, weights != nullptr, weights_len, &L, &msg);
+  if (rc) return fail(rc, "%s", msg);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  vmlm_pool* p = new vmlm_pool();
+  p->dev = ctx->dev;
+  p->L = std::move(L);
+  const uint64_t sizes[4] = {p->L.const_len, p->L.act_bytes, p->L.state_bytes, p->L.grad_bytes};
+  for (int r = 0; r < 4; ++r) {
+    const size_t bytes = sizes[r] + vmlm::kVmbRegionPad;
+    if (cudaMalloc(&p->region[r], bytes) != cudaSuccess) {
+      cudaGetLastError();
+      pool_release(p);
+      delete p;
+      return fail(VMLM_ERR_OOM, "pool_load: cudaMalloc of %zu bytes failed", bytes);
+    }
+    // the VM zeroes its scratch regions (interp.rs:165-187); the pool's slack too
+    cudaError_t e = cudaMemset(p->region[r], 0, bytes);
+    if (e == cudaSuccess && r == 0 && sizes[0] > 0) {
+      const void* src = weights ? weights : static_cast<const char*>(vmb) + p->L.const_off;
+      e = cudaMemcpy(p->region[0], src, sizes[0], cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+      pool_release(p);
+      delete p;
+      return fail(VMLM_ERR_CUDA, "pool_load: %s", cudaGetErrorString(e));
+    }
+  }
+  *out = p;
+  return VMLM_OK;
+}
+
+int vmlm_pool_free(vmlm_pool* pool) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!pool) return VMLM_OK;
+  pool_release(pool);
+  delete pool;
+  return VMLM_OK;
+}
+
+int vmlm_pool_info(const vmlm_pool* pool, size_t* n_const, size_t* n_slots, size_t* region_bytes) {
+  if (!pool) return fail(VMLM_ERR_ARG, "pool_info: null pool");
+  if (n_const) *n_const = pool->L.consts.size();
+  if (n_slots) *n_slots = pool->L.slots.size();
+  if (region_bytes) {
+    region_bytes[0] = pool->L.const_len;
+    region_bytes[1] = pool->L.act_bytes;
+    region_bytes[2] = pool->L.state_bytes;
+    region_bytes[3] = pool->L.grad_bytes;
+  }
+  return VMLM_OK;
+}
+
+int vmlm_pool_region(const vmlm_pool* pool, int region, void** base) {
+  if (!pool || !base) return fail(VMLM_ERR_ARG, "pool_region: null argument");
+  if (region < 0 || region > 3) return fail(VMLM_ERR_ARG, "pool_region: region must be 0 (const) .. 3 (grad)");
+  *base = pool->region[region];
+  return VMLM_OK;
+}
+
+int vmlm_pool_slot(const vmlm_pool* pool, size_t slot, vmlm_slot* out, int* kind) {
+  if (!pool) return fail(VMLM_ERR_ARG, "pool_slot: null pool");
+  return pool_slot(pool, slot, out, kind);
+}
+
+int vmlm_pool_layerb(vmlm_pool* pool, float delta) {
+  if (!pool) return fail(VMLM_ERR_ARG, "pool_layerb: null pool");
+  pool->layer_base = vmlm::vmb_layerb(pool->layer_base, delta);
+  return VMLM_OK;
+}
+
+int vmlm_pool_layer_base(const vmlm_pool* pool, size_t* base) {
+  if (!pool || !base) return fail(VMLM_ERR_ARG, "pool_layer_base: null argument");
+  *base = static_cast<size_t>(pool->layer_base);
+  return VMLM_OK;
+}
+
+int vmlm_pool_find_const(const vmlm_pool* pool, const char* name, size_t* idx) {
+  if (!pool || !name || !idx) return fail(VMLM_ERR_ARG, "pool_find_const: null argument");
+  const uint32_t h = vmlm::vmb_hash32(name);
+  for (size_t i = 0; i < pool->L.consts.size(); ++i)
+    if (pool->L.consts[i].hash == h) {
+      *idx = i;
+      return VMLM_OK;
+    }
+  return fail(VMLM_ERR_ARG, "const not found");
+}
+
+int vmlm_pool_find_slot(const vmlm_pool* pool, const char* name, size_t* idx) {
+  if (!pool || !name || !idx) return fail(VMLM_ERR_ARG, "pool_find_slot: null argument");
+  const uint32_t h = vmlm::vmb_hash32(name);
+  for (size_t i = 0; i < pool->L.slots.size(); ++i)
+    if (pool->L.slots[i].name == h) {
+      *idx = i;
+      return VMLM_OK;
+    }
+  return fail(VMLM_ERR_ARG, "slot not found");
+}
+
+int vmlm_pool_gemm(vmlm_pool* pool, const void* ins, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!pool || !ins) return fail(VMLM_ERR_ARG, "pool_gemm: null argument");
+  const uint8_t* b = static_cast<const uint8_t*>(ins);
+  if (b[0] != vmlm::kVmbOpGemm) return fail(VMLM_ERR_ARG, "pool_gemm: opcode %u is not OP_GEMM", b[0]);
+  uint16_t dt;
+  std::memcpy(&dt, b + 2, 2);
+  const uint32_t d = vmlm::vmb_u32(b + 4), a = vmlm::vmb_u32(b + 8), bs = vmlm::vmb_u32(b + 12);
+  int dev = -1;
+  VMLM_CUDA(cudaGetDevice(&dev));
+  if (dev != pool->dev) return fail(VMLM_ERR_STATE, "pool_gemm: the pool lives on device %d, current is %d", pool->dev, dev);
+  vmlm_slot sd, sa, sb, ss;
+  VMLM_TRY(pool_slot(pool, d, &sd, nullptr));
+  VMLM_TRY(pool_slot(pool, a, &sa, nullptr));
+  VMLM_TRY(pool_slot(pool, bs, &sb, nullptr));
+  const bool has_scale = dt < pool->L.slots.size();
+  if (has_scale) VMLM_TRY(pool_slot(pool, dt, &ss, nullptr));
+  return op_gemm(b[1], &sd, &sa, &sb, has_scale ? &ss : nullptr, true, stream);
+}
+
 
 int vmlm_version(void) { return 100; }
 

@@ -19,7 +19,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import check, lib
+from ._lib import Slot, check, lib
 
 
 def _host_ptr(x, dtype, count, name):
@@ -238,6 +238,69 @@ def gemv_f32(a, b, c, m, k) -> None:
 def gemv_f32_dev(a, b, c, m, k, stream=None) -> None:
     check(lib().vmlm_gemv_f32_dev(_dev_ptr(a, "float32", m * k, "a"), _dev_ptr(b, "float32", k, "b"),
                                   _dev_ptr(c, "float32", m, "c"), m, k, _stream_ptr(stream)))
+
+
+class Pool:
+    """A .vmb program's constant pool, scratch regions and slot table in device
+    memory (vmlm_pool_*; Vm::load, core/src/interp.rs:123-220)."""
+
+    def __init__(self, image: bytes, weights: bytes = None):
+        self._h = ctypes.c_void_p()
+        img = bytes(image)
+        w = bytes(weights) if weights is not None else None
+        check(lib().vmlm_pool_load(img, len(img), w, len(w) if w is not None else 0, ctypes.byref(self._h)))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().vmlm_pool_free(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def info(self):
+        """-> (n_const, n_slots, [const, act, state, grad] bytes)."""
+        nc, ns = ctypes.c_size_t(), ctypes.c_size_t()
+        rb = (ctypes.c_size_t * 4)()
+        check(lib().vmlm_pool_info(self._h, ctypes.byref(nc), ctypes.byref(ns), rb))
+        return nc.value, ns.value, list(rb)
+
+    def region(self, r: int) -> int:
+        p = ctypes.c_void_p()
+        check(lib().vmlm_pool_region(self._h, r, ctypes.byref(p)))
+        return p.value or 0
+
+    def slot(self, i: int):
+        """-> (device address, rows, cols, dtype, kind)."""
+        s, kind = Slot(), ctypes.c_int()
+        check(lib().vmlm_pool_slot(self._h, i, ctypes.byref(s), ctypes.byref(kind)))
+        return s.ptr or 0, s.rows, s.cols, s.dtype, kind.value
+
+    def layerb(self, delta: float) -> None:
+        check(lib().vmlm_pool_layerb(self._h, ctypes.c_float(delta)))
+
+    def layer_base(self) -> int:
+        b = ctypes.c_size_t()
+        check(lib().vmlm_pool_layer_base(self._h, ctypes.byref(b)))
+        return b.value
+
+    def find_const(self, name: str) -> int:
+        i = ctypes.c_size_t()
+        check(lib().vmlm_pool_find_const(self._h, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def find_slot(self, name: str) -> int:
+        i = ctypes.c_size_t()
+        check(lib().vmlm_pool_find_slot(self._h, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def gemm(self, ins: bytes, stream=None) -> None:
+        """Run one 16-byte OP_GEMM instruction on the pool's slots."""
+        assert len(ins) == 16
+        check(lib().vmlm_pool_gemm(self._h, ins, _stream_ptr(stream)))
 
 
 def set_host_pipeline(max_chunks: int) -> None:

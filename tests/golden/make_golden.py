@@ -15,6 +15,8 @@ Sources (paths inside the shouzugzs-AI/Sparrow tree):
   sparrow/examples/int8_bad_bins/           same set with a_scale[0] += 2^-6 (gen_int8.py:96-100)
   sparrow/examples/int8_naive_bins/         scale = max|row|/127 (gen_int8.py:84-93)
   sparrow/examples/bf16_bins_{bf16,f32}/    written by sparrow/tools/gen_bf16.py
+  sparrow/examples/e2e_bins/e2e_tiny.vmb    a whole .vmb program (7 f32 constants, 11 slots, an OP_GEMM),
+                                            with its constants' .bin files and the .args manifest
 Recorded outputs: sparrow/REPORT_V015.md:443-446 (criteria 1-4 of
 sparrow/tools/int8_ab.ps1), printed with the engine's truncating print_f32
 (core/src/interp.rs:2416-2473).
@@ -33,6 +35,9 @@ COPY = {
     "int8_naive_bins": ("sparrow/examples/int8_naive_bins", None),
     "bf16_bins_bf16": ("sparrow/examples/bf16_bins_bf16", ["LINEAR_W.bin", "EMBED_E.bin"]),
     "bf16_bins_f32": ("sparrow/examples/bf16_bins_f32", ["LINEAR_W.bin", "EMBED_E.bin"]),
+    "e2e_tiny": ("sparrow/examples/e2e_bins", ["e2e_tiny.vmb", "e2e_tiny.args", "tiny_in.bin", "EMBED_E.bin",
+                                               "SPARSE_off.bin", "SPARSE_src.bin", "SPARSE_W.bin", "LINEAR_W.bin",
+                                               "LINEAR_b.bin"]),
 }
 
 GOLDEN = {
