@@ -412,10 +412,12 @@ def bench_configs(K, dist, rank, world, flush, pk):
     res = {}
     hbm = pk["hbm_gbs"]
 
-    def q8_layer(m, n, k, seed):
+    def q8_layer(m, n, k, seed, calls=None):
         x = gen((m, k), seed, 1.0)
         q, s = quantise_rows(gen((n, k), seed + 1, 0.02))
         c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        if calls is not None:
+            calls.append((x, q, s, c, m, n, k))
         step = lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)  # noqa: E731
         return step, n * k + 4 * n + 4 * m * k + 4 * m * n
 
@@ -431,10 +433,12 @@ def bench_configs(K, dist, rank, world, flush, pk):
     # C3: the per-layer Q8 set (q, k, v, o, gate, up, down). A step is the
     # seven calls back to back on one stream, as a decoder layer issues them
     # (L2 flushed once per step); the sum of the calls timed one by one, each
-    # after its own flush, is reported beside it.
+    # after its own flush, is reported beside it; and the seven as one batch of
+    # independent calls (vmlm_gemm_nt_int8_batch_dev: one grouped launch).
     shapes = [(2304, 2304)] * 4 + [(5760, 2304)] * 2 + [(2304, 5760)]
     for m in (1, 8, 32):
-        steps = [q8_layer(m, n, k, 10 * i + m) for i, (n, k) in enumerate(shapes)]
+        calls = []
+        steps = [q8_layer(m, n, k, 10 * i + m, calls) for i, (n, k) in enumerate(shapes)]
         nbytes = sum(b for _, b in steps)
 
         def layer():
@@ -445,8 +449,14 @@ def bench_configs(K, dist, rank, world, flush, pk):
         entry = hbm_entry(nbytes, t, tg)
         entry["single_calls_us"] = sum(time_steps(s, 10, 3, flush, dist) for s, _ in steps) * 1e3
         entry["step"] = "7 calls back to back, L2 flushed once per step"
+        tb = time_steps(lambda: K.gemm_nt_int8_batch_dev(calls, stream=st), 20, 3, flush, dist)
+        n0 = K.launch_count()
+        K.gemm_nt_int8_batch_dev(calls, stream=st)
+        entry["batch"] = {"step_us": tb * 1e3, "GBps": nbytes / tb / 1e6, "frac_hbm": nbytes / tb / 1e6 / hbm,
+                          "launches": K.launch_count() - n0,
+                          "step": "the 7 calls as one vmlm_gemm_nt_int8_batch_dev call, L2 flushed once per step"}
         res[f"C3_q8_layer_set_M{m}"] = entry
-        del steps
+        del steps, calls
     # C4: Q8 LM head, vocab rows sharded over the ranks, all-gather of logits
     n4, k4 = 122753, 2304
     rows = (n4 + world - 1) // world

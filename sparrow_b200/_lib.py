@@ -68,6 +68,7 @@ SIGNATURES = {
     "vmlm_emb": (I, [P, I, S, S, P, S, P]),
     "vmlm_emb_dev": (I, [P, I, S, S, P, S, P, P]),
     "vmlm_set_host_pipeline": (I, [I]),
+    "vmlm_gemm_nt_int8_batch_dev": (I, [P, S, P]),
     "vmlm_pool_load": (I, [P, S, P, S, P]),
     "vmlm_pool_free": (I, [P]),
     "vmlm_pool_info": (I, [P, P, P, P]),

@@ -70,6 +70,30 @@ struct DecParams {
   unsigned long long* trace;  // optional, kTraceSlots values per CTA
 };
 
+// Grouped launches: independent Q8 calls with the same token count m run as one
+// grid, a CTA per 128-row tile and no cluster. Each problem carries its own
+// weight tensor map, pointers and sizes; tile0 is its first CTA (problems are
+// listed by descending k, so the longest tiles start first).
+struct DecProblem {
+  CUtensorMap map;  // W [n][k] int8, box 128 x 128
+  const float* x;
+  const int8_t* w;
+  const float* scale;
+  float* out;
+  long long ldx, ldo;
+  int n, k, kb, tile0, vec_x;
+};
+constexpr int kDecMaxGroup = 16;
+struct DecNoGroup {
+  static constexpr int kMax = 0;
+  int count;
+};
+struct DecGroup {
+  static constexpr int kMax = kDecMaxGroup;
+  DecProblem prob[kDecMaxGroup];
+  int count;
+};
+
 // Rows of a tile finished by one CTA of the cluster.
 __host__ __device__ inline int dec_rows_per_cta(int c) { return (kTileRows + c - 1) / c; }
 
@@ -124,9 +148,11 @@ __device__ __forceinline__ float dec_nonfinite_dot(const DecParams& p, int t, in
                           __ldg(p.scale + n));
 }
 
+template <class G>
 __global__ void __launch_bounds__(kDecThreads, 1)
     q8_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmP,
-                     const DecParams p) {
+                     const DecParams p_in, const __grid_constant__ G grp) {
+  DecParams p = p_in;  // a grouped launch replaces the per-problem fields below
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
@@ -147,9 +173,28 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const CUtensorMap* map_w = &tmW;
   const int c = p.cluster;
   const int rank = c > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int tile = blockIdx.x / c;
+  int tile = blockIdx.x / c;
+  if constexpr (G::kMax > 0) {
+    // this CTA's problem (c == 1): the last one whose first tile is at or before it
+    int g = 0;
+    while (g + 1 < grp.count && grp.prob[g + 1].tile0 <= static_cast<int>(blockIdx.x)) ++g;
+    const DecProblem& pr = grp.prob[g];
+    p.x = pr.x;
+    p.ldx = pr.ldx;
+    p.w = pr.w;
+    p.scale = pr.scale;
+    p.out = pr.out;
+    p.ldo = pr.ldo;
+    p.n = pr.n;
+    p.k = pr.k;
+    p.kb = pr.kb;
+    p.vec_x = pr.vec_x;
+    map_w = &pr.map;
+    tile = static_cast<int>(blockIdx.x) - pr.tile0;
+  }
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb / c);
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * p.kb / c);
   const int nkb = kb1 - kb0;
@@ -183,7 +228,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(map_w);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + kDecMaxTok) {
     s_max[threadIdx.x - 64] = 0;
@@ -207,7 +252,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       for (int j = 0; j < nkb; ++j) {
         if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
         mbar_arrive_expect_tx(full_bar + stage, kDecStageBytes);
-        tma_load_2d(smem + stage * kDecStageBytes, &tmW, full_bar + stage, (kb0 + j) * kBlockBytes,
+        tma_load_2d(smem + stage * kDecStageBytes, map_w, full_bar + stage, (kb0 + j) * kBlockBytes,
                     tile * kTileRows, pol);
         issued_mask |= 1u << stage;
         last_phase = (last_phase & ~(1u << stage)) | (phase << stage);

@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -219,7 +220,8 @@ int get_ctx(int dev, Ctx** out) {
                                  kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(tc2_gemm_kernel<TcMode::kQ8Swap>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMaxSmem));
-  VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel<DecNoGroup>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel<DecGroup>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   VMLM_TRY(set_int4_smem_attrs());
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
@@ -565,7 +567,7 @@ int max_active_clusters(Ctx* ctx, int cl, uint32_t smem, int* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  VMLM_CUDA(cudaOccupancyMaxActiveClusters(&n, q8_decode_kernel, &cfg));
+  VMLM_CUDA(cudaOccupancyMaxActiveClusters(&n, q8_decode_kernel<DecNoGroup>, &cfg));
   ctx->dec_clusters[key] = n;
   *out = n;
   return VMLM_OK;
@@ -637,9 +639,81 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
     mp = mw;  // unused
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
-  VMLM_TRY(launch_ex(q8_decode_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), plan.smem, st, true,
-                     plan.c, mw, mp, p));
+  VMLM_TRY(launch_ex(q8_decode_kernel<DecNoGroup>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), plan.smem,
+                     st, true, plan.c, mw, mp, p, DecNoGroup{0}));
   if (g_profile) VMLM_TRY(prof_end(st, pp));
+  return VMLM_OK;
+}
+
+// Independent Q8 calls with the same m as one grouped decode launch: a CTA per
+// 128-row tile of every call (no cluster: each CTA runs its tile's whole K),
+// problems ordered by descending K so the longest tiles start first. Returns
+// VMLM_OK with *done = false when the calls do not fit (the caller then runs
+// them one by one).
+struct Q8Call {
+  const float* a;
+  const int8_t* q;
+  const float* scale;
+  float* c;
+  int m, n, k;
+};
+
+int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, bool* done) {
+  *done = false;
+  if (count < 2 || count > kDecMaxGroup) return VMLM_OK;
+  const int M = calls[0].m;
+  if (M < 1 || M > kDecMaxTok) return VMLM_OK;
+  int kb_max = 0;
+  for (int i = 0; i < count; ++i) {
+    const Q8Call& q = calls[i];
+    if (q.m != M || q.n < 1 || q.k < 16 || q.k % 16 || q.k > 131072 || !aligned16(q.q)) return VMLM_OK;
+    kb_max = std::max(kb_max, static_cast<int>(cdiv(q.k, kBlockBytes)));
+  }
+  const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
+  int stages = kb_max < 16 ? kb_max : 16;
+  while (stages >= 1 && dec_smem_layout(stages, rows_b, kb_max, M, 1).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  if (stages < 1 || (stages < 2 && kb_max > 1)) return VMLM_OK;
+  int order[kDecMaxGroup];
+  for (int i = 0; i < count; ++i) order[i] = i;
+  std::stable_sort(order, order + count, [&](int x, int y) { return calls[x].k > calls[y].k; });
+  DecGroup grp;
+  std::memset(&grp, 0, sizeof(grp));
+  grp.count = count;
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const Q8Call& q = calls[order[i]];
+    DecProblem& pr = grp.prob[i];
+    VMLM_TRY(make_map(&pr.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.q, q.k, q.n, q.k, 128, kTileRows));
+    pr.x = q.a;
+    pr.w = q.q;
+    pr.scale = q.scale;
+    pr.out = q.c;
+    pr.ldx = q.k;
+    pr.ldo = q.n;
+    pr.n = q.n;
+    pr.k = q.k;
+    pr.kb = static_cast<int>(cdiv(q.k, kBlockBytes));
+    pr.tile0 = tiles;
+    pr.vec_x = (q.k % 4 == 0) && aligned16(q.a);
+    tiles += static_cast<int>(cdiv(q.n, kTileRows));
+  }
+  DecParams p = {};
+  p.m = M;
+  p.cluster = 1;
+  p.rows_b = rows_b;
+  p.kbr_max = kb_max;
+  p.stages = stages;
+  p.tmem_cols = pow2_at_least(rows_b);
+  p.err = ctx->err;
+  p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(tiles) <= g_trace_ctas) ? g_trace : nullptr;
+  const uint32_t smem = dec_smem_layout(stages, rows_b, kb_max, M, 1).total;
+  ProfPair pp;
+  if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
+  // the tensor-map arguments of the ungrouped form are unused here
+  VMLM_TRY(launch_ex(q8_decode_kernel<DecGroup>, dim3(static_cast<unsigned>(tiles)), dim3(kDecThreads), smem, st,
+                     true, 1, grp.prob[0].map, grp.prob[0].map, p, grp));
+  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  *done = true;
   return VMLM_OK;
 }
 
@@ -1893,6 +1967,37 @@ int vmlm_emb_dev(const void* table, int dtype, size_t rows, size_t cols, const f
   return launch(emb_kernel, dim3(static_cast<unsigned>(m), static_cast<unsigned>(cdiv(cols, 1024))), dim3(256), 0, st,
                 false, table, dtype, static_cast<long long>(rows), static_cast<int>(cols), idx, static_cast<int>(m),
                 out, ctx->err);
+}
+
+int vmlm_gemm_nt_int8_batch_dev(const vmlm_q8_call* calls, size_t count, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (count == 0) return VMLM_OK;
+  if (!calls) return fail(VMLM_ERR_ARG, "gemm_nt_int8_batch_dev: null call list");
+  for (size_t i = 0; i < count; ++i) {
+    const vmlm_q8_call& q = calls[i];
+    VMLM_TRY(check_dims(q.m, q.n, q.k));
+    if (q.m > 0 && q.n > 0 && (!q.c || !q.scale || (q.k > 0 && (!q.a || !q.q))))
+      return fail(VMLM_ERR_ARG, "gemm_nt_int8_batch_dev: null pointer in call %zu", i);
+  }
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  std::vector<Q8Call> qc;
+  for (size_t i = 0; i < count; ++i)
+    if (calls[i].m > 0 && calls[i].n > 0)
+      qc.push_back(Q8Call{calls[i].a, calls[i].q, calls[i].scale, calls[i].c, static_cast<int>(calls[i].m),
+                          static_cast<int>(calls[i].n), static_cast<int>(calls[i].k)});
+  for (size_t i0 = 0; i0 < qc.size(); i0 += kDecMaxGroup) {
+    const int cnt = static_cast<int>(std::min<size_t>(kDecMaxGroup, qc.size() - i0));
+    bool done = false;
+    VMLM_TRY(run_decode_group(ctx, qc.data() + i0, cnt, st, &done));
+    if (done) continue;
+    for (int i = 0; i < cnt; ++i) {
+      const Q8Call& q = qc[i0 + i];
+      VMLM_TRY(run_q8(ctx, q.a, q.q, q.scale, q.c, q.m, q.n, q.k, st));
+    }
+  }
+  return VMLM_OK;
 }
 
 int vmlm_gemm_nt_int4_gs(const float* a, const uint8_t* packed, const float* scale, float* c, size_t m, size_t n,

@@ -303,6 +303,21 @@ class Pool:
         check(lib().vmlm_pool_gemm(self._h, ins, _stream_ptr(stream)))
 
 
+class Q8Call(ctypes.Structure):
+    """vmlm_q8_call: one Q8 call of a batch (device pointers)."""
+    _fields_ = [("a", ctypes.c_void_p), ("q", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("c", ctypes.c_void_p),
+                ("m", ctypes.c_size_t), ("n", ctypes.c_size_t), ("k", ctypes.c_size_t)]
+
+
+def gemm_nt_int8_batch_dev(calls, stream=None) -> None:
+    """Independent Q8 calls [(a, q, scale, c, m, n, k), ...] on CUDA tensors, as one grouped launch where they fit."""
+    arr = (Q8Call * len(calls))()
+    for i, (a, q, s, c, m, n, k) in enumerate(calls):
+        arr[i] = Q8Call(_dev_ptr(a, "float32", m * k, "a"), _dev_ptr(q, "int8", n * k, "q"),
+                        _dev_ptr(s, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"), m, n, k)
+    check(lib().vmlm_gemm_nt_int8_batch_dev(arr, len(calls), _stream_ptr(stream)))
+
+
 def set_host_pipeline(max_chunks: int) -> None:
     """Most row chunks a large host-pointer call is pipelined in (1 = off, 0 = default)."""
     check(lib().vmlm_set_host_pipeline(int(max_chunks)))

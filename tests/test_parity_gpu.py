@@ -454,3 +454,60 @@ def test_bf16_prefill_k_split_shapes(kernels, oracle, m, n, k, exact):
     # exchanged through distributed shared memory), general and bf16-valued X
     x, w = bf16_case(oracle, m, n, k, seed=m + k, exact_x=exact)
     check_bf16(kernels, oracle, x, w)
+
+
+# ------------------------------------------------- batches of independent calls
+
+C3_SHAPES = [(2304, 2304)] * 4 + [(5760, 2304)] * 2 + [(2304, 5760)]
+
+
+def _batch(oracle, m, shapes, seed):
+    import torch
+    calls, host = [], []
+    for i, (n, k) in enumerate(shapes):
+        x, q, s = q8_case(oracle, m, n, k, seed=seed + i)
+        dx, dq, ds = (torch.from_numpy(v).cuda() for v in (x, q, s))
+        calls.append((dx, dq, ds, torch.empty((m, n), device="cuda"), m, n, k))
+        host.append((x, q, s))
+    return calls, host
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 32])
+def test_q8_batch_matches_single_calls(kernels, oracle, m):
+    """A decoder layer's seven Q8 linears as one batch: the same bits as seven calls."""
+    import torch
+    calls, host = _batch(oracle, m, C3_SHAPES, seed=40 + m)
+    st = torch.cuda.current_stream()
+    kernels.gemm_nt_int8_batch_dev(calls, stream=st)
+    kernels.sync(st)
+    for (dx, dq, ds, dc, m_, n, k), (x, q, s) in zip(calls, host):
+        single = torch.empty_like(dc)
+        kernels.gemm_nt_int8_dev(dx, dq, ds, single, m_, n, k, stream=st)
+        kernels.sync(st)
+        assert torch.equal(dc.view(torch.int32), single.view(torch.int32)), (n, k)
+        assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int8(x, q, s, nt=NT)) <= TIGHT_Q8
+
+
+def test_q8_batch_mixed_and_edge_calls(kernels, oracle):
+    """Calls that do not share m, a K that is not a multiple of 16, a ragged N, a
+    non-finite token, and more calls than one grouped launch takes."""
+    import torch
+    st = torch.cuda.current_stream()
+    shapes = [(300, 1024), (129, 64), (1000, 2304)] * 7  # 21 calls: two grouped launches
+    calls, host = _batch(oracle, 2, shapes, seed=90)
+    host[4][0][1, 7] = np.inf
+    calls[4][0].copy_(torch.from_numpy(host[4][0]))
+    kernels.gemm_nt_int8_batch_dev(calls, stream=st)
+    kernels.sync(st)
+    for (dx, dq, ds, dc, m_, n, k), (x, q, s) in zip(calls, host):
+        ref = oracle.gemm_nt_int8(x, q, s)
+        got = dc.cpu().numpy()
+        assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref))
+        fin = np.isfinite(ref).all(axis=1)
+        assert oracle.max_rel_err(np.ascontiguousarray(got[fin]), np.ascontiguousarray(ref[fin])) <= TIGHT_Q8
+    mixed, mhost = _batch(oracle, 1, [(640, 2304)], seed=7)
+    more, more_host = _batch(oracle, 4, [(640, 100)], seed=8)  # K % 16 != 0 and another m: one by one
+    kernels.gemm_nt_int8_batch_dev(mixed + more, stream=st)
+    kernels.sync(st)
+    for (dx, dq, ds, dc, m_, n, k), (x, q, s) in zip(mixed + more, mhost + more_host):
+        assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int8(x, q, s)) <= TIGHT_Q8
