@@ -474,7 +474,11 @@ def _batch(oracle, m, shapes, seed):
 
 @pytest.mark.parametrize("m", [1, 3, 8, 32])
 def test_q8_batch_matches_single_calls(kernels, oracle, m):
-    """A decoder layer's seven Q8 linears as one batch: the same bits as seven calls."""
+    """A decoder layer's seven Q8 linears as one batch, against the oracle and the
+    seven calls one by one. Not bit-identical to them: in a grouped launch a CTA
+    forms a token's digit planes over the whole K (one exponent), a single call
+    split over a cluster over each CTA's K range (an exponent per range), so the
+    activations are rounded on different 22-bit grids."""
     import torch
     calls, host = _batch(oracle, m, C3_SHAPES, seed=40 + m)
     st = torch.cuda.current_stream()
@@ -484,8 +488,9 @@ def test_q8_batch_matches_single_calls(kernels, oracle, m):
         single = torch.empty_like(dc)
         kernels.gemm_nt_int8_dev(dx, dq, ds, single, m_, n, k, stream=st)
         kernels.sync(st)
-        assert torch.equal(dc.view(torch.int32), single.view(torch.int32)), (n, k)
-        assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int8(x, q, s, nt=NT)) <= TIGHT_Q8
+        ref = oracle.gemm_nt_int8(x, q, s, nt=NT)
+        assert oracle.max_rel_err(dc.cpu().numpy(), ref) <= TIGHT_Q8, (n, k)
+        assert oracle.max_rel_err(dc.cpu().numpy(), single.cpu().numpy()) <= TIGHT_Q8, (n, k)
 
 
 def test_q8_batch_mixed_and_edge_calls(kernels, oracle):
