@@ -71,9 +71,9 @@ struct DecParams {
 };
 
 // Grouped launches: independent Q8 calls with the same token count m run as one
-// grid, a CTA per 128-row tile and no cluster. Each problem carries its own
-// weight tensor map, pointers and sizes; tile0 is its first CTA (problems are
-// listed by descending k, so the longest tiles start first).
+// grid, a cluster of `cluster` CTAs per 128-row tile. Each problem carries its
+// own weight tensor map, pointers and sizes; tile0 is its first tile (problems
+// are listed by descending k, so the longest tiles start first).
 struct DecProblem {
   CUtensorMap map;  // W [n][k] int8, box 128 x 128
   const float* x;
@@ -178,9 +178,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int rank = c > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   int tile = blockIdx.x / c;
   if constexpr (G::kMax > 0) {
-    // this CTA's problem (c == 1): the last one whose first tile is at or before it
+    // this cluster's problem: the last one whose first tile is at or before it
     int g = 0;
-    while (g + 1 < grp.count && grp.prob[g + 1].tile0 <= static_cast<int>(blockIdx.x)) ++g;
+    while (g + 1 < grp.count && grp.prob[g + 1].tile0 <= tile) ++g;
     const DecProblem& pr = grp.prob[g];
     p.x = pr.x;
     p.ldx = pr.ldx;
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     p.kb = pr.kb;
     p.vec_x = pr.vec_x;
     map_w = &pr.map;
-    tile = static_cast<int>(blockIdx.x) - pr.tile0;
+    tile -= pr.tile0;
   }
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb / c);
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * p.kb / c);

@@ -646,8 +646,8 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
 }
 
 // Independent Q8 calls with the same m as one grouped decode launch: a CTA per
-// 128-row tile of every call (no cluster: each CTA runs its tile's whole K),
-// problems ordered by descending K so the longest tiles start first. Returns
+// 128-row tile of every call over the tile's whole K, problems ordered by
+// descending K so the longest tiles start first. Returns
 // VMLM_OK with *done = false when the calls do not fit (the caller then runs
 // them one by one).
 struct Q8Call {
@@ -667,12 +667,21 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   for (int i = 0; i < count; ++i) {
     const Q8Call& q = calls[i];
     if (q.m != M || q.n < 1 || q.k < 16 || q.k % 16 || q.k > 131072 || !aligned16(q.q)) return VMLM_OK;
-    kb_max = std::max(kb_max, static_cast<int>(cdiv(q.k, kBlockBytes)));
+    const int kb = static_cast<int>(cdiv(q.k, kBlockBytes));
+    kb_max = std::max(kb_max, kb);
   }
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
-  int stages = kb_max < 16 ? kb_max : 16;
-  while (stages >= 1 && dec_smem_layout(stages, rows_b, kb_max, M, 1).total > static_cast<uint32_t>(kMaxSmem)) --stages;
-  if (stages < 1 || (stages < 2 && kb_max > 1)) return VMLM_OK;
+  // Whole-K CTAs, and only when a CTA's x slice fits one register batch of the
+  // plane warps (the rule plan_decode applies): grouped launches that split K
+  // over clusters (ten waves of 8-CTA clusters for the C3 set at m = 8), or
+  // that make the planes in several batches, measured slower than the calls
+  // one by one, so those batches run call by call.
+  const int c = 1, kbr = kb_max;
+  if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
+    return VMLM_OK;
+  int stages = kbr < 16 ? kbr : 16;
+  while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  if (stages < 1 || (stages < 2 && kbr > 1)) return VMLM_OK;
   int order[kDecMaxGroup];
   for (int i = 0; i < count; ++i) order[i] = i;
   std::stable_sort(order, order + count, [&](int x, int y) { return calls[x].k > calls[y].k; });
@@ -699,19 +708,20 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   }
   DecParams p = {};
   p.m = M;
-  p.cluster = 1;
+  p.cluster = c;
   p.rows_b = rows_b;
-  p.kbr_max = kb_max;
+  p.kbr_max = kbr;
   p.stages = stages;
   p.tmem_cols = pow2_at_least(rows_b);
   p.err = ctx->err;
-  p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(tiles) <= g_trace_ctas) ? g_trace : nullptr;
-  const uint32_t smem = dec_smem_layout(stages, rows_b, kb_max, M, 1).total;
+  const long long grid = static_cast<long long>(tiles) * c;
+  p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
+  const uint32_t smem = dec_smem_layout(stages, rows_b, kbr, M, c).total;
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   // the tensor-map arguments of the ungrouped form are unused here
-  VMLM_TRY(launch_ex(q8_decode_kernel<DecGroup>, dim3(static_cast<unsigned>(tiles)), dim3(kDecThreads), smem, st,
-                     true, 1, grp.prob[0].map, grp.prob[0].map, p, grp));
+  VMLM_TRY(launch_ex(q8_decode_kernel<DecGroup>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st,
+                     true, c, grp.prob[0].map, grp.prob[0].map, p, grp));
   if (g_profile) VMLM_TRY(prof_end(st, pp));
   *done = true;
   return VMLM_OK;
