@@ -75,7 +75,10 @@ struct DecParams {
 // own weight tensor map, pointers and sizes; tile0 is its first tile (problems
 // are listed by descending k, so the longest tiles start first).
 struct DecProblem {
-  CUtensorMap map;  // W [n][k] int8, box 128 x 128
+  CUtensorMap map;    // W [n][k] int8, box 128 x 128
+  CUtensorMap map_p;  // planes mode: the problem's planes [3m][kp], box 128 x rows_b
+  const int* exps;
+  const int* nonfinite;
   const float* x;
   const int8_t* w;
   const float* scale;
@@ -174,6 +177,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const CUtensorMap* map_w = &tmW;
+  const CUtensorMap* map_p = &tmP;
   const int c = p.cluster;
   const int rank = c > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   int tile = blockIdx.x / c;
@@ -192,7 +196,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     p.k = pr.k;
     p.kb = pr.kb;
     p.vec_x = pr.vec_x;
+    p.exps = pr.exps;
+    p.nonfinite = pr.nonfinite;
     map_w = &pr.map;
+    map_p = &pr.map_p;
     tile -= pr.tile0;
   }
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb / c);
@@ -317,7 +324,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       if (et == 0) {
         mbar_arrive_expect_tx(planes_bar, static_cast<uint32_t>(nkb * p.rows_b * kBlockBytes));
         for (int j = 0; j < nkb; ++j)
-          tma_load_2d(smem + L.b_off + j * p.rows_b * kBlockBytes, &tmP, planes_bar, (kb0 + j) * kBlockBytes, 0,
+          tma_load_2d(smem + L.b_off + j * p.rows_b * kBlockBytes, map_p, planes_bar, (kb0 + j) * kBlockBytes, 0,
                       policy_evict_last());
         if (trace) trace[1] = globaltimer();
       }

@@ -90,14 +90,10 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 
 // One CTA per token. planes: [3*M][kp] int8, row 3t+p. Columns [K, kp) are 0.
 // Requires kp % 16 == 0.
-__global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __restrict__ x, long long ldx, int M,
-                                                                 int K, int kp, int8_t* __restrict__ planes,
-                                                                 int* __restrict__ exps, int* __restrict__ nonfinite) {
-  pdl_launch_dependents();
-  __shared__ float redf[32];
-  __shared__ int redi[32];
-  const int t = blockIdx.x;
-  if (t >= M) return;
+// The planes, exponent and non-finite flag of token row t (one CTA).
+__device__ __forceinline__ void q8_planes_row(const float* __restrict__ x, long long ldx, int K, int kp,
+                                              int8_t* __restrict__ planes, int* __restrict__ exps,
+                                              int* __restrict__ nonfinite, int t, float* redf, int* redi) {
   const float* xr = x + static_cast<long long>(t) * ldx;
   const bool vec = ((K & 3) == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
   const int nchunk = (kp + 3) >> 2;  // 4-element chunks covering [0, kp)
@@ -171,6 +167,41 @@ __global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __
     exps[t] = e;
     nonfinite[t] = bad;
   }
+}
+
+__global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __restrict__ x, long long ldx, int M,
+                                                                 int K, int kp, int8_t* __restrict__ planes,
+                                                                 int* __restrict__ exps, int* __restrict__ nonfinite) {
+  pdl_launch_dependents();
+  __shared__ float redf[32];
+  __shared__ int redi[32];
+  const int t = blockIdx.x;
+  if (t >= M) return;
+  q8_planes_row(x, ldx, K, kp, planes, exps, nonfinite, t, redf, redi);
+}
+
+// The planes of several independent activation matrices with the same token
+// count in one launch: grid (M, count), problem blockIdx.y.
+constexpr int kPlanesMaxGroup = 16;
+struct PlanesProblem {
+  const float* x;
+  int8_t* planes;
+  int* exps;
+  int* nonfinite;
+  int k, kp;
+};
+struct PlanesGroup {
+  PlanesProblem prob[kPlanesMaxGroup];
+  int count, m;
+};
+
+__global__ void __launch_bounds__(kPrepThreads) q8_planes_group_kernel(const __grid_constant__ PlanesGroup g) {
+  pdl_launch_dependents();
+  __shared__ float redf[32];
+  __shared__ int redi[32];
+  if (static_cast<int>(blockIdx.y) >= g.count || static_cast<int>(blockIdx.x) >= g.m) return;
+  const PlanesProblem& pr = g.prob[blockIdx.y];
+  q8_planes_row(pr.x, pr.k, pr.k, pr.kp, pr.planes, pr.exps, pr.nonfinite, blockIdx.x, redf, redi);
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {

@@ -109,6 +109,7 @@ struct Ctx {
   int* err_host = nullptr;  // pinned copy read after host-API calls
   DevBuf h_a, h_c, h_w, h_s, h_acc, h_b, h_g;  // host-API staging
   DevBuf xn;  // RMSNorm-fused Q8 calls: the normalised activations [M][K]
+  DevBuf grp_planes;  // grouped Q8 batches in planes mode: every problem's planes, exponents and flags
   // host-pointer calls pipelined by row chunks: copies in and out on streams of
   // their own, ordered against the compute stream by events
   cudaStream_t s_in = nullptr, s_out = nullptr;
@@ -671,14 +672,16 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
     kb_max = std::max(kb_max, kb);
   }
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
-  // Whole-K CTAs, and only when a CTA's x slice fits one register batch of the
-  // plane warps (the rule plan_decode applies): grouped launches that split K
-  // over clusters (ten waves of 8-CTA clusters for the C3 set at m = 8), or
-  // that make the planes in several batches, measured slower than the calls
-  // one by one, so those batches run call by call.
+  // Whole-K CTAs. When a CTA's x slice fits one register batch of the plane
+  // warps (the rule plan_decode applies) the kernel makes the planes itself;
+  // otherwise one q8_planes_group_kernel launch makes every problem's planes
+  // first and the kernel loads them (planes mode). Grouped launches that split
+  // K over clusters (ten waves of 8-CTA clusters for the C3 set at m = 8), or
+  // that make the planes in several batches in the kernel, measured slower than
+  // the calls one by one.
   const int c = 1, kbr = kb_max;
-  if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
-    return VMLM_OK;
+  const bool planes_mode =
+      static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
   int stages = kbr < 16 ? kbr : 16;
   while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   if (stages < 1 || (stages < 2 && kbr > 1)) return VMLM_OK;
@@ -688,6 +691,19 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   DecGroup grp;
   std::memset(&grp, 0, sizeof(grp));
   grp.count = count;
+  PlanesGroup pg;
+  std::memset(&pg, 0, sizeof(pg));
+  if (planes_mode) {
+    // every problem's planes [3M][kp] (kp = K rounded up to 16; each region
+    // 128-byte aligned), then its exponents and flags [M] each
+    size_t bytes = 0;
+    for (int i = 0; i < count; ++i)
+      bytes += (static_cast<size_t>(3) * M * cdiv(calls[i].k, 16) * 16 + 127) / 128 * 128 + 8ull * M + 128;
+    VMLM_TRY(ensure(ctx->grp_planes, bytes));
+    pg.count = count;
+    pg.m = M;
+  }
+  char* ws = static_cast<char*>(ctx->grp_planes.p);
   int tiles = 0;
   for (int i = 0; i < count; ++i) {
     const Q8Call& q = calls[order[i]];
@@ -705,10 +721,26 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
     pr.tile0 = tiles;
     pr.vec_x = (q.k % 4 == 0) && aligned16(q.a);
     tiles += static_cast<int>(cdiv(q.n, kTileRows));
+    if (planes_mode) {
+      const int kp = static_cast<int>(cdiv(q.k, 16) * 16);
+      int8_t* planes = reinterpret_cast<int8_t*>(ws);
+      ws += (static_cast<size_t>(3) * M * kp + 127) / 128 * 128;
+      int* exps = reinterpret_cast<int*>(ws);
+      ws += (8ull * M + 127) / 128 * 128;
+      pr.exps = exps;
+      pr.nonfinite = exps + M;
+      VMLM_TRY(make_map(&pr.map_p, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, q.k, 3ull * M, kp, 128,
+                        static_cast<uint32_t>(rows_b)));
+      pg.prob[i] = PlanesProblem{q.a, planes, exps, exps + M, q.k, kp};
+    }
   }
+  if (planes_mode)
+    VMLM_TRY(launch(q8_planes_group_kernel, dim3(static_cast<unsigned>(M), static_cast<unsigned>(count)),
+                    dim3(kPrepThreads), 0, st, false, pg));
   DecParams p = {};
   p.m = M;
   p.cluster = c;
+  p.planes_mode = planes_mode ? 1 : 0;
   p.rows_b = rows_b;
   p.kbr_max = kbr;
   p.stages = stages;
@@ -1630,7 +1662,8 @@ int vmlm_shutdown(void) {
     cudaStreamSynchronize(c->stream);
     for (DevBuf* b : {&c->act, &c->small, &c->slots, &c->counters, &c->shard_done, &c->sync, &c->norm_terms,
                       &c->norm_dirty, &c->norm_flags, &c->f32_ta, &c->f32_tb, &c->f32_da, &c->f32_db, &c->f32_nfa,
-                      &c->f32_nfb, &c->f32_nft, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b, &c->h_g, &c->xn})
+                      &c->f32_nfb, &c->f32_nft, &c->f32_flags, &c->h_a, &c->h_c, &c->h_w, &c->h_s, &c->h_acc, &c->h_b, &c->h_g, &c->xn,
+                      &c->grp_planes})
       if (b->p) cudaFree(b->p);
     cudaFree(c->err);
     cudaFreeHost(c->err_host);
