@@ -664,27 +664,37 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   if (count < 2 || count > kDecMaxGroup) return VMLM_OK;
   const int M = calls[0].m;
   if (M < 1 || M > kDecMaxTok) return VMLM_OK;
-  int kb_max = 0;
+  int kb_max = 0, kb_min = 1 << 30;
   for (int i = 0; i < count; ++i) {
     const Q8Call& q = calls[i];
     if (q.m != M || q.n < 1 || q.k < 16 || q.k % 16 || q.k > 131072 || !aligned16(q.q)) return VMLM_OK;
     const int kb = static_cast<int>(cdiv(q.k, kBlockBytes));
     kb_max = std::max(kb_max, kb);
+    kb_min = std::min(kb_min, kb);
   }
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
-  // Whole-K CTAs. When a CTA's x slice fits one register batch of the plane
-  // warps (the rule plan_decode applies) the kernel makes the planes itself;
-  // otherwise one q8_planes_group_kernel launch makes every problem's planes
-  // first and the kernel loads them (planes mode). Grouped launches that split
-  // K over clusters (ten waves of 8-CTA clusters for the C3 set at m = 8), or
-  // that make the planes in several batches in the kernel, measured slower than
-  // the calls one by one.
-  const int c = 1, kbr = kb_max;
+  // When a CTA's x slice over the whole K fits one register batch of the plane
+  // warps (the rule plan_decode applies), whole-K CTAs make the planes
+  // themselves. Otherwise one q8_planes_group_kernel launch makes every
+  // problem's planes first and the kernel loads them (planes mode), on whole-K
+  // CTAs where the planes tile fits shared memory, else on the smallest cluster
+  // that fits. Splitting K over clusters while the kernel makes the planes in
+  // several batches (ten waves of 8-CTA clusters for the C3 set at m = 8)
+  // measured slower than the calls one by one.
   const bool planes_mode =
-      static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
-  int stages = kbr < 16 ? kbr : 16;
-  while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
-  if (stages < 1 || (stages < 2 && kbr > 1)) return VMLM_OK;
+      static_cast<long long>(M) * kb_max * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
+  int c = 0, kbr = 0, stages = 0;
+  for (int cc = 1; cc <= (planes_mode ? kDecMaxCluster : 1) && cc <= kb_min; cc *= 2) {
+    const int r = static_cast<int>(cdiv(kb_max, cc));
+    int s = r < 16 ? r : 16;
+    while (s >= 1 && dec_smem_layout(s, rows_b, r, M, cc).total > static_cast<uint32_t>(kMaxSmem)) --s;
+    if (s < 1 || (s < 2 && r > 1)) continue;
+    c = cc;
+    kbr = r;
+    stages = s;
+    break;
+  }
+  if (c == 0) return VMLM_OK;
   int order[kDecMaxGroup];
   for (int i = 0; i < count; ++i) order[i] = i;
   std::stable_sort(order, order + count, [&](int x, int y) { return calls[x].k > calls[y].k; });
