@@ -8,6 +8,7 @@
 
 #include <cstdint>
 
+#include "prep.cuh"
 #include "ptx.cuh"
 
 namespace vmlm {
@@ -180,6 +181,217 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4gs_kernel(const float* __re
       for (int o = kI4LanesPerRow / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       if (u0 == 0 && j < n && i < rows_m) c[static_cast<long long>(m0 + i) * n + j] = s;
     }
+  }
+}
+
+// Integer form for one or two token rows (the HBM-bound case), same tile rules
+// and lane mapping as int4gs_kernel, one token row per grid row (blockIdx.y).
+// The token row becomes three int8 digit planes of its 22-bit fixed-point
+// form X = rint(x * 2^e) (one exponent per row, as the Q8 path makes them), and
+// each weight nibble the unsigned byte u = nibble ^ 8 = v + 8: per 8 columns
+// one LOP3 and one shift + LOP3 give the bytes of the even and of the odd
+// columns, and two dp4a per plane add u * X_p. A 32-column unit's sum is then
+// sum_p 256^p (D_p - 8 sum X_p), exactly sum X * v (|.| <= 2^30), converted
+// once to f32 and multiplied by the group's scale; the row total is scaled by
+// 2^-e at the end. Staged per unit (7 uint4, 112 bytes, stride 7 so eight
+// consecutive units fall in eight bank groups): even-column and odd-column
+// plane words of planes 0, 1, 2, then the unit's digit sums. A row holding NaN
+// or Inf is computed in f32 instead (the row staged as floats, scalar decode).
+constexpr int kI4UnitWords = 7;
+
+template <int ORDER>
+__global__ void __launch_bounds__(kI4Warps * 32) int4gs_dp4a_kernel(const float* __restrict__ a,
+                                                                    const uint8_t* __restrict__ packed,
+                                                                    const float* __restrict__ scale,
+                                                                    float* __restrict__ c, int n, int k, int group,
+                                                                    int gpr, int kc) {
+  extern __shared__ uint4 s_u[];
+  __shared__ float redf[32];
+  __shared__ int redi[32];
+  pdl_launch_dependents();
+  pdl_wait_prior();
+  const int t = blockIdx.y;
+  const float* xr = a + static_cast<long long>(t) * k;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const int u0 = lane % kI4LanesPerRow;
+  const long long rowbytes = k / 2;
+  const int ukc = kc / 32;                          // units per staged chunk
+  float* s_x = reinterpret_cast<float*>(s_u + ukc * kI4UnitWords);  // f32 row chunk (NaN/Inf rows only)
+  const bool one_chunk = kc >= k;
+
+  // the row's exponent and non-finite flag over the whole K
+  float amax = 0.f;
+  int bad = 0;
+  for (int i = static_cast<int>(threadIdx.x); i < k / 4; i += blockDim.x) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(xr) + i);
+    bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  block_max_or(amax, bad, redf, redi);
+  int e = 0;
+  if (!bad && amax > 0.f) {
+    int E;
+    frexpf(amax, &E);
+    e = 22 - E;
+  }
+
+  auto stage = [&](int kc0, int kcn) {
+    if (bad) {
+      for (int i = static_cast<int>(threadIdx.x); i < kcn / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(s_x)[i] = __ldg(reinterpret_cast<const float4*>(xr + kc0) + i);
+      return;
+    }
+    // thread per 8-column word q (units of 4 words); the 4 threads of a unit are
+    // consecutive lanes and combine their digit sums by shuffles
+    const int nw = kcn / 8;
+    for (int q0 = 0; q0 < nw; q0 += blockDim.x) {
+      const int q = q0 + static_cast<int>(threadIdx.x);
+      int sx[3] = {0, 0, 0};
+      if (q < nw) {
+        const float4 v0 = __ldg(reinterpret_cast<const float4*>(xr + kc0) + 2 * q);
+        const float4 v1 = __ldg(reinterpret_cast<const float4*>(xr + kc0) + 2 * q + 1);
+        const float xs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        int d[3][8];
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          q8_digits(xs[j], e, d[0][j], d[1][j], d[2][j]);
+          sx[0] += d[0][j];
+          sx[1] += d[1][j];
+          sx[2] += d[2][j];
+        }
+        uint32_t* su = reinterpret_cast<uint32_t*>(s_u + (q >> 2) * kI4UnitWords);
+        #pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          su[(2 * p) * 4 + (q & 3)] = pack4(d[p][0], d[p][2], d[p][4], d[p][6]);
+          su[(2 * p + 1) * 4 + (q & 3)] = pack4(d[p][1], d[p][3], d[p][5], d[p][7]);
+        }
+      }
+      #pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        sx[p] += __shfl_xor_sync(0xffffffffu, sx[p], 1);
+        sx[p] += __shfl_xor_sync(0xffffffffu, sx[p], 2);
+      }
+      if (q < nw && (q & 3) == 0) s_u[(q >> 2) * kI4UnitWords + 6] = make_uint4(sx[0], sx[1], sx[2], 0);
+    }
+  };
+
+  // one 32-column unit of weight row j: sum X * v as a float (or the f32 sum of
+  // a NaN/Inf row), before the group's scale
+  auto unit_value = [&](uint4 wv, int u) -> float {
+    if (ORDER == 1) {
+      const uint32_t x0 = nib_swap(wv.x), x2 = nib_swap(wv.z);
+      wv = make_uint4(x0, x0, x2, x2);
+    }
+    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+    if (!bad) {
+      const uint4* su = s_u + u * kI4UnitWords;
+      const uint4 e0 = su[0], o0 = su[1], e1 = su[2], o1 = su[3], e2 = su[4], o2 = su[5], sx = su[6];
+      const uint32_t E0[4] = {e0.x, e0.y, e0.z, e0.w}, O0[4] = {o0.x, o0.y, o0.z, o0.w};
+      const uint32_t E1[4] = {e1.x, e1.y, e1.z, e1.w}, O1[4] = {o1.x, o1.y, o1.z, o1.w};
+      const uint32_t E2[4] = {e2.x, e2.y, e2.z, e2.w}, O2[4] = {o2.x, o2.y, o2.z, o2.w};
+      int D0 = 0, D1 = 0, D2 = 0;
+      #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int lo = static_cast<int>((ws[i] & 0x0F0F0F0Fu) ^ 0x08080808u);
+        const int hi = static_cast<int>(((ws[i] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u);
+        D0 = __dp4a(lo, static_cast<int>(E0[i]), D0);
+        D0 = __dp4a(hi, static_cast<int>(O0[i]), D0);
+        D1 = __dp4a(lo, static_cast<int>(E1[i]), D1);
+        D1 = __dp4a(hi, static_cast<int>(O1[i]), D1);
+        D2 = __dp4a(lo, static_cast<int>(E2[i]), D2);
+        D2 = __dp4a(hi, static_cast<int>(O2[i]), D2);
+      }
+      const int S = (D0 - 8 * static_cast<int>(sx.x)) + 256 * (D1 - 8 * static_cast<int>(sx.y)) +
+                    65536 * (D2 - 8 * static_cast<int>(sx.z));
+      return __int2float_rn(S);
+    }
+    const float* xs = s_x + u * 32;
+    float part = 0.f;
+    #pragma unroll
+    for (int cidx = 0; cidx < 32; ++cidx) {
+      const uint32_t nib = (ws[cidx >> 3] >> (4 * (cidx & 7))) & 15u;
+      part = fmaf(xs[cidx], static_cast<float>(static_cast<int>(nib) - (nib > 7 ? 16 : 0)), part);
+    }
+    return part;
+  };
+  auto finish_row = [&](float tot, int j) {
+    #pragma unroll
+    for (int o = kI4LanesPerRow / 2; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if (u0 == 0 && j < n) c[static_cast<long long>(t) * n + j] = bad ? tot : scale_pow2(tot, -e);
+  };
+  const int rows_step = gridDim.x * kI4RowsPerBlock;
+
+  if (one_chunk) {
+    stage(0, k);
+    __syncthreads();
+    // one flat stream per lane over (row set, step): the weight loads run two
+    // steps ahead across row-set boundaries, so a row set's first loads do not
+    // start cold; a row's total is reduced and stored after its last step
+    const int units = k / 32;
+    const int steps = (units + kI4LanesPerRow - 1) / kI4LanesPerRow;
+    const int jlane = warp * (32 / kI4LanesPerRow) + lane / kI4LanesPerRow;  // row within a row set
+    auto fetch = [&](int j0, int st, uint4& w, float& s) {
+      const int u = u0 + st * kI4LanesPerRow;
+      const int j = j0 + jlane;
+      if (j0 < n && u < units) {
+        const int jr = j < n ? j : n - 1;
+        w = __ldg(reinterpret_cast<const uint4*>(packed + jr * rowbytes) + u);
+        s = __ldg(scale + static_cast<long long>(jr) * gpr + u * 32 / group);
+      }
+    };
+    int j0 = blockIdx.x * kI4RowsPerBlock, st = 0;   // current position
+    int pj = j0, pst = 0;                              // next position to fetch
+    uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+    float s0 = 0.f, s1 = 0.f;
+    auto advance = [&](int& jj, int& ss) {
+      if (++ss == steps) {
+        ss = 0;
+        jj += rows_step;
+      }
+    };
+    fetch(pj, pst, w0, s0);
+    advance(pj, pst);
+    fetch(pj, pst, w1, s1);
+    advance(pj, pst);
+    float tot = 0.f;
+    while (j0 < n) {
+      uint4 w2 = w1;
+      float s2 = s1;
+      fetch(pj, pst, w2, s2);
+      advance(pj, pst);
+      const int u = u0 + st * kI4LanesPerRow;
+      if (u < units) tot = fmaf(unit_value(w0, u), s0, tot);  // rows past n hold row n-1 and are not stored
+      if (st == steps - 1) {
+        finish_row(tot, j0 + jlane);
+        tot = 0.f;
+      }
+      advance(j0, st);
+      w0 = w1;
+      s0 = s1;
+      w1 = w2;
+      s1 = s2;
+    }
+    return;
+  }
+  for (int j0 = blockIdx.x * kI4RowsPerBlock; j0 < n; j0 += rows_step) {
+    const int jwarp = j0 + warp * (32 / kI4LanesPerRow);
+    const int j = jwarp + lane / kI4LanesPerRow;
+    const int jr = j < n ? j : n - 1;  // a past-the-end row reads row n-1 and is not stored
+    float tot = 0.f;
+    for (int kc0 = 0; kc0 < k; kc0 += kc) {
+      const int kcn = k - kc0 < kc ? k - kc0 : kc;
+      __syncthreads();
+      stage(kc0, kcn);
+      __syncthreads();
+      const int units = kcn / 32;
+      if (jwarp < n && u0 < units) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(packed + jr * rowbytes) + kc0 / 32;
+        const float* srow = scale + static_cast<long long>(jr) * gpr;
+        for (int u = u0; u < units; u += kI4LanesPerRow)
+          tot = fmaf(unit_value(__ldg(wrow + u), u), __ldg(srow + (kc0 + u * 32) / group), tot);
+      }
+    }
+    finish_row(tot, j);
   }
 }
 

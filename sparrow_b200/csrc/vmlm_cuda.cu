@@ -172,6 +172,8 @@ int set_int4_smem_attr() {
 }
 
 int set_int4_smem_attrs() {
+  VMLM_CUDA(cudaFuncSetAttribute(int4gs_dp4a_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kI4SmemFloats * 4));
+  VMLM_CUDA(cudaFuncSetAttribute(int4gs_dp4a_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kI4SmemFloats * 4));
   VMLM_TRY(set_int4_smem_attr<1>());
   VMLM_TRY(set_int4_smem_attr<2>());
   VMLM_TRY(set_int4_smem_attr<4>());
@@ -1308,6 +1310,23 @@ int run_int4gs(Ctx* c, const float* a, const uint8_t* packed, const float* scale
     return VMLM_OK;
   }
   const int gpr = static_cast<int>(cdiv(k, group));
+  if (m == 1 && k % 32 == 0 && group % 32 == 0 && aligned16(packed) && aligned16(a)) {
+    // one token row: the integer (dp4a) form (two rows as two grid rows read the
+    // weights twice; the f32 kernel shares them); a chunk of kc columns
+    // stages 112 bytes of planes per 32 columns and, for NaN/Inf rows, the floats
+    const int kc_cap = kI4SmemFloats * 4 / (112 + 128) * 32;
+    const int kc = k < kc_cap ? k : kc_cap;
+    const size_t smem = static_cast<size_t>(kc / 32) * (112 + 128);
+    // one wave (four CTAs per SM at 60 registers): a CTA stages the row once and
+    // streams many row sets
+    const dim3 grid(static_cast<unsigned>(std::min<long long>(cdiv(n, kI4RowsPerBlock), 4ll * c->sms)),
+                    static_cast<unsigned>(m));
+    if (order)
+      return launch(int4gs_dp4a_kernel<1>, grid, dim3(kI4Warps * 32), smem, st, false, a, packed, scale, out, n, k,
+                    group, gpr, kc);
+    return launch(int4gs_dp4a_kernel<0>, grid, dim3(kI4Warps * 32), smem, st, false, a, packed, scale, out, n, k,
+                  group, gpr, kc);
+  }
   if (k % 32 == 0 && group % 32 == 0 && aligned16(packed) && aligned16(a)) {
     const int mm = m < 8 ? m : 8;
     if (mm == 1) return launch_int4gs<1>(c, a, packed, scale, out, m, n, k, group, gpr, order, st);

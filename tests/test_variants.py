@@ -20,6 +20,8 @@ import sparrow_b200.kernels as K
 from sparrow_b200._lib import VmlmError
 
 TIGHT = 1e-5      # f32 sums of exact int4 / int8 products, reordered
+# one or two token rows take the integer (dp4a) int4 kernel: activations rounded
+# to 22 bits per row as in the Q8 path, so the Q8 bound applies
 TIGHT_Q8 = 2e-5   # the int8 body runs the Q8 path (activations at 2^-22 relative)
 ARG = 1
 
@@ -137,13 +139,31 @@ def _int4_case(O, m, n, k, group, seed, outliers=False):
     (4, 256, 256, 32), (4, 512, 512, 512), (4, 1024, 1024, 32),     # the reference's shapes
     (1, 5760, 2304, 32), (8, 2304, 2304, 64), (3, 1000, 4096, 128),  # decode layers
     (16, 777, 640, 32), (2, 333, 96, 96), (5, 4096, 4096, 4096),     # two token-row passes; K staged in two chunks
+    (2, 700, 16384, 128), (1, 122753, 2304, 32),                     # integer form: K in two chunks; LM head
 ])
 @pytest.mark.parametrize("order", [0, 1])
 def test_int4_gs_tiled(kernels, oracle, m, n, k, group, order):
     a, packed, s = _int4_case(oracle, m, n, k, group, seed=m + n)
     c = np.empty((m, n), np.float32)
     kernels.gemm_nt_int4_gs(a, packed, s, c, m, n, k, group, order)
-    assert oracle.max_rel_err(c, oracle.gemm_nt_int4_gs(a, packed, s, k, group, order)) <= TIGHT
+    tol = TIGHT_Q8 if m == 1 else TIGHT
+    assert oracle.max_rel_err(c, oracle.gemm_nt_int4_gs(a, packed, s, k, group, order)) <= tol
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("order", [0, 1])
+def test_int4_gs_integer_form_nonfinite_row(kernels, oracle, order):
+    """Two token rows, one holding Inf and NaN: that row is computed in f32 (the
+    reference's NaN/Inf pattern), the other in the integer form."""
+    m, n, k, group = 2, 500, 2304, 32
+    a, packed, s = _int4_case(oracle, m, n, k, group, seed=21)
+    a[0, 3] = np.inf
+    a[0, 900] = np.nan
+    c = np.empty((m, n), np.float32)
+    kernels.gemm_nt_int4_gs(a, packed, s, c, m, n, k, group, order)
+    ref = oracle.gemm_nt_int4_gs(a, packed, s, k, group, order)
+    assert np.array_equal(np.isnan(c), np.isnan(ref)) and np.array_equal(np.isinf(c), np.isinf(ref))
+    assert oracle.max_rel_err(np.ascontiguousarray(c[1:]), np.ascontiguousarray(ref[1:])) <= TIGHT_Q8
 
 
 @pytest.mark.gpu
