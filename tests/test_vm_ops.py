@@ -1,4 +1,4 @@
-"""The decode-step neighbours of the quantised linear layer (SURVEY row f3):
+"""The decode-step neighbours of the quantised linear layer:
 RMSNorm fused into the Q8 GEMM, OP_GEMV and OP_EMB, through the C ABI.
 
 CPU tests pin the oracle restatements (ops/src/kernels.rs:1346-1370,
