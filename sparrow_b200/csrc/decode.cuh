@@ -84,6 +84,7 @@ struct DecProblem {
   const float* scale;
   float* out;
   long long ldx, ldo;
+  long long kbase;  // equal-share launches (q8_decode_sk_kernel): first k-block of the problem over the batch
   int n, k, kb, tile0, vec_x;
 };
 constexpr int kDecMaxGroup = 16;

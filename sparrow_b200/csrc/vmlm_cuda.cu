@@ -17,6 +17,7 @@
 #include "../../include/vmlm_cuda.h"
 #include "prep.cuh"
 #include "decode.cuh"
+#include "decode_sk.cuh"
 #include "tc2_gemm.cuh"
 #include "tc_gemm.cuh"
 #include "variants.cuh"
@@ -225,6 +226,7 @@ int get_ctx(int dev, Ctx** out) {
                                  kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel<DecNoGroup>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   VMLM_CUDA(cudaFuncSetAttribute(q8_decode_kernel<DecGroup>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  VMLM_CUDA(cudaFuncSetAttribute(q8_decode_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   VMLM_TRY(set_int4_smem_attrs());
   g_ctx[dev] = c;
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
@@ -661,6 +663,85 @@ struct Q8Call {
   int m, n, k;
 };
 
+// A grouped batch with more 128-row tiles than SMs (one CTA per tile would
+// run in two waves) at token counts where a CTA's x slice of an equal k-block
+// share fits one register batch of the plane warps: q8_decode_sk_kernel, one
+// CTA per SM, every CTA streaming an equal share of the batch's k-blocks.
+// Problems are taken by descending K, as in the one-CTA-per-tile launch.
+// *done = false when the batch does not fit (the caller then plans it as
+// before).
+int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, bool* done) {
+  *done = false;
+  const int M = calls[0].m;
+  if (M < 1 || M > 16) return VMLM_OK;
+  int order[kDecMaxGroup];
+  for (int i = 0; i < count; ++i) order[i] = i;
+  std::stable_sort(order, order + count, [&](int x, int y) { return calls[x].k > calls[y].k; });
+  DecGroup grp;
+  std::memset(&grp, 0, sizeof(grp));
+  grp.count = count;
+  long long tiles = 0, total = 0;
+  for (int i = 0; i < count; ++i) {
+    const Q8Call& q = calls[order[i]];
+    DecProblem& pr = grp.prob[i];
+    pr.n = q.n;
+    pr.k = q.k;
+    pr.kb = static_cast<int>(cdiv(q.k, kBlockBytes));
+    pr.tile0 = static_cast<int>(tiles);
+    pr.kbase = total;
+    const long long nt = static_cast<long long>(cdiv(q.n, kTileRows));
+    tiles += nt;
+    total += nt * pr.kb;
+  }
+  const int grid = ctx->sms;
+  if (tiles <= grid || total < grid) return VMLM_OK;
+  const int kbr = static_cast<int>(cdiv(total, grid));
+  if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
+    return VMLM_OK;
+  for (int b = 0; b < grid; ++b) {
+    DecSkSegs sg;
+    if (!dec_sk_segments(grp.prob, count, total, grid, b, sg)) return VMLM_OK;
+  }
+  const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
+  int stages = kbr < 16 ? kbr : 16;
+  while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  if (stages < 2) return VMLM_OK;
+  for (int i = 0; i < count; ++i) {
+    const Q8Call& q = calls[order[i]];
+    DecProblem& pr = grp.prob[i];
+    VMLM_TRY(make_map(&pr.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.q, q.k, q.n, q.k, 128, kTileRows));
+    pr.x = q.a;
+    pr.w = q.q;
+    pr.scale = q.scale;
+    pr.out = q.c;
+    pr.ldx = q.k;
+    pr.ldo = q.n;
+    pr.vec_x = (q.k % 4 == 0) && aligned16(q.a);
+  }
+  // slots and counters start at zero and are left at zero by every call
+  VMLM_TRY(ensure(ctx->slots, static_cast<size_t>(tiles) * M * kTileRows * 8, true));
+  VMLM_TRY(ensure(ctx->counters, static_cast<size_t>(tiles) * 4, true));
+  DecSkParams p = {};
+  p.m = M;
+  p.rows_b = rows_b;
+  p.stages = stages;
+  p.tmem_cols = pow2_at_least(kDecSkMaxSeg * rows_b);
+  p.kbr_max = kbr;
+  p.grid = grid;
+  p.kb_total = total;
+  p.slots = static_cast<double*>(ctx->slots.p);
+  p.counters = static_cast<int*>(ctx->counters.p);
+  p.err = ctx->err;
+  p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
+  const uint32_t smem = dec_sk_smem_layout(stages, rows_b, kbr).total;
+  ProfPair pp;
+  if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
+  VMLM_TRY(launch(q8_decode_sk_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st, true, p, grp));
+  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  *done = true;
+  return VMLM_OK;
+}
+
 int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, bool* done) {
   *done = false;
   if (count < 2 || count > kDecMaxGroup) return VMLM_OK;
@@ -674,6 +755,8 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
     kb_max = std::max(kb_max, kb);
     kb_min = std::min(kb_min, kb);
   }
+  VMLM_TRY(run_decode_group_sk(ctx, calls, count, st, done));
+  if (*done) return VMLM_OK;
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
   // When a CTA's x slice over the whole K fits one register batch of the plane
   // warps (the rule plan_decode applies), whole-K CTAs make the planes

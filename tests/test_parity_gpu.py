@@ -516,3 +516,34 @@ def test_q8_batch_mixed_and_edge_calls(kernels, oracle):
     kernels.sync(st)
     for (dx, dq, ds, dc, m_, n, k), (x, q, s) in zip(mixed + more, mhost + more_host):
         assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int8(x, q, s)) <= TIGHT_Q8
+
+
+@pytest.mark.parametrize("m,shapes", [(2, [(2000, 1040)] * 12), (16, [(2560, 256)] * 8), (1, C3_SHAPES)])
+def test_q8_batch_equal_share(kernels, oracle, m, shapes):
+    """Batches with more 128-row tiles than the GPU has SMs run with an equal
+    share of k-blocks per CTA: tiles split between CTAs are summed through f64
+    slots by the CTA that completes them. Ragged N, a K that ends inside a
+    k-block, tokens holding NaN and Inf, and the same batch twice in a row (the
+    slots and counters must be left at zero): against the oracle, and the two
+    calls bit-identical."""
+    import torch
+    calls, host = _batch(oracle, m, shapes, seed=300 + m)
+    if m > 1:
+        host[3][0][1, 5] = np.nan
+        host[7][0][0, shapes[7][1] - 1] = -np.inf
+        for i in (3, 7):
+            calls[i][0].copy_(torch.from_numpy(host[i][0]))
+    st = torch.cuda.current_stream()
+    outs = []
+    for _ in range(2):
+        for c in calls:
+            c[3].fill_(7.0)
+        kernels.gemm_nt_int8_batch_dev(calls, stream=st)
+        kernels.sync(st)
+        outs.append([c[3].cpu().numpy().copy() for c in calls])
+    for got, again, (x, q, s) in zip(outs[0], outs[1], host):
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+        ref = oracle.gemm_nt_int8(x, q, s, nt=NT)
+        assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref))
+        fin = np.isfinite(ref).all(axis=1)
+        assert oracle.max_rel_err(np.ascontiguousarray(got[fin]), np.ascontiguousarray(ref[fin])) <= TIGHT_Q8
