@@ -30,6 +30,12 @@
 // adds a NaN partial; the finishing CTA recomputes its outputs by sequential
 // f32 dot products, as the other kernels do.
 //
+// Trace (vmlm_trace_enable): slots 0-7 as in the other kernels (start, planes
+// ready, last W load issued, first stage consumed, last commit, first
+// accumulator, epilogue done, TMEM released); slots 8-10 hold timestamps:
+// first W load issued, plane warps past the wait for the previous kernel, and
+// the CTA-wide set-up barrier passed.
+//
 // The partials of one output are integers times powers of two; their sum is
 // exact in f64 (and so independent of the order of the atomic adds) while the
 // segments' exponents of a token lie within 2^10 of each other, which holds
