@@ -94,12 +94,16 @@ def parse():
     return ap.parse_args()
 
 
-# Single workloads for profiling: name -> (kind, m, n, k)
+# The Q8 linears of one 2304-hidden decoder layer (q, k, v, o, gate, up, down): (n, k)
+C3_SHAPES = [(2304, 2304)] * 4 + [(5760, 2304)] * 2 + [(2304, 5760)]
+
+# Single workloads for profiling: name -> (kind, m, n, k); "q8batch" runs the
+# C3 layer set as one vmlm_gemm_nt_int8_batch_dev call at m tokens
 CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf16f", M2, N2, K2),
          "c3q_m8": ("q8", 8, 2304, 2304), "c4m1": ("q8", 1, 122753, 2304), "c4m64": ("q8", 64, 122753, 2304),
          "c5": ("i8", 4096, 28672, 8192), "c5small": ("i8", 1024, 4096, 8192),
          "c4m64small": ("q8", 64, 16384, 2304), "c3q_m32": ("q8", 32, 2304, 2304), "c3d_m32": ("q8", 32, 2304, 5760),
-         "c3g_m32": ("q8", 32, 5760, 2304),
+         "c3g_m32": ("q8", 32, 5760, 2304), "c3b_m1": ("q8batch", 1, 0, 0), "c3b_m2": ("q8batch", 2, 0, 0),
          "f32nt": ("f32nt", M2, N2, K2), "f32nn": ("f32nn", M2, N2, K2)}
 
 
@@ -116,6 +120,15 @@ def run_case(args):
         x = gen((m, k), 0, 1.0)
         q, s = quantise_rows(gen((n, k), 1, 0.02))
         step = lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)  # noqa: E731
+    elif kind == "q8batch":
+        # the C3 layer set (q, k, v, o, gate, up, down) as one batch of independent calls
+        calls = []
+        for i, (n_i, k_i) in enumerate(C3_SHAPES):
+            x = gen((m, k_i), 10 * i + m, 1.0)
+            q, s = quantise_rows(gen((n_i, k_i), 10 * i + 1 + m, 0.02))
+            calls.append((x, q, s, torch.empty((m, n_i), dtype=torch.float32, device="cuda"), m, n_i, k_i))
+        n, k = sum(n_i for n_i, _ in C3_SHAPES), 0
+        step = lambda: K.gemm_nt_int8_batch_dev(calls, stream=st)  # noqa: E731
     elif kind in ("bf16", "bf16f"):
         x = gen((m, k), 0, 1.0)
         if kind == "bf16":
@@ -435,7 +448,7 @@ def bench_configs(K, dist, rank, world, flush, pk):
     # (L2 flushed once per step); the sum of the calls timed one by one, each
     # after its own flush, is reported beside it; and the seven as one batch of
     # independent calls (vmlm_gemm_nt_int8_batch_dev: one grouped launch).
-    shapes = [(2304, 2304)] * 4 + [(5760, 2304)] * 2 + [(2304, 5760)]
+    shapes = C3_SHAPES
     for m in (1, 8, 32):
         calls = []
         steps = [q8_layer(m, n, k, 10 * i + m, calls) for i, (n, k) in enumerate(shapes)]
