@@ -17,7 +17,9 @@
 //   warp 0      streams the range's W k-blocks (TMA, one tensor map per
 //               problem) through a stage ring, segment after segment.
 //   warps 2..9  make the digit planes of every segment (one register batch of
-//               x chunks), then run the segments' epilogues in order.
+//               x chunks), or in planes mode load them from the planes
+//               kernel's output (one exponent per token over the problem's
+//               whole K), then run the segments' epilogues in order.
 //   warp 1      owns TMEM; tcgen05.mma kind::i8 per k-block into the
 //               segment's accumulator; a commit per segment.
 //
@@ -56,6 +58,10 @@ constexpr int kDecSkMaxSeg = 4;
 
 struct DecSkParams {
   int m;
+  // planes mode: the digit planes, exponents and non-finite flags come from
+  // q8_planes_group_kernel (each problem's map_p, exps, nonfinite: one
+  // exponent per token over the problem's whole K) instead of being made here
+  int planes_mode;
   int rows_b;          // UMMA N: plane rows, 16 * ceil(3m / 16)
   int stages;          // W stage ring depth
   int tmem_cols;       // kDecSkMaxSeg accumulators of rows_b columns, rounded up to a power of two
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     pdl_wait_prior();
     if (trace && et == 0) trace[9] = globaltimer();
     #pragma unroll
-    for (int r = 0; r < kDecRegChunks; ++r) {
+    for (int r = 0; r < (p.planes_mode ? 0 : kDecRegChunks); ++r) {
       const int qi = et + r * kDecEpiThreads;
       keep[r] = (r < nsteps && qi < nq) ? dec_sk_load(sg, sx, qi, qpt) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -379,68 +385,91 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
   } else {
     // ----------------------------------- digit planes, then the epilogues
-    // pass 1: per segment and token, max |x| and the non-finite flag (32
-    // consecutive chunks are one k-block of one token: one segment)
-    #pragma unroll
-    for (int r = 0; r < kDecRegChunks; ++r) {
-      const int qi = et + r * kDecEpiThreads;
-      if (r >= nsteps || qi - lane >= nq) break;  // warp-uniform
-      const float4 v = keep[r];
-      float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-      int bad = !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
-      mx = warp_max(mx);
-      bad = warp_or(bad);
-      if (lane == 0) {
-        const int t = (qi - lane) / qpt;
-        const int s = dec_sk_seg_of(sg, ((qi - lane) - t * qpt) >> 5);
-        atomicMax(s_max + s * kDecMaxTok + t, __float_as_int(mx));
-        if (bad) atomicOr(s_bad + s * kDecMaxTok + t, 1);
+    if (p.planes_mode) {
+      // one TMA load per k-block of the range from its problem's planes
+      // (rows past 3m read as zero), and the problems' exponents and flags
+      if (et == 0) {
+        mbar_arrive_expect_tx(planes_bar, static_cast<uint32_t>(nkb * p.rows_b * kBlockBytes));
+        for (int j = 0; j < nkb; ++j) {
+          const int s = dec_sk_seg_of(sg, j);
+          tma_load_2d(smem + L.b_off + j * p.rows_b * kBlockBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, planes_bar,
+                      (dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s)) * kBlockBytes, 0, policy_evict_last());
+        }
+        if (trace) trace[1] = globaltimer();
       }
-    }
-    named_bar_sync(1, kDecEpiThreads);
-    if (et < kDecSkMaxSeg * kDecMaxTok) {
-      int e = 0;
-      const float amax = __int_as_float(s_max[et]);
-      if (!s_bad[et] && amax > 0.f) {
-        int E;
-        frexpf(amax, &E);
-        e = 22 - E;
+      if (et < kDecSkMaxSeg * kDecMaxTok) {
+        const int s = et / kDecMaxTok, t = et - s * kDecMaxTok;
+        if (s < sg.n && t < p.m) {
+          const DecProblem& pr = grp.prob[dec_sk_pick(sg.g, s)];
+          s_exp[et] = __ldg(pr.exps + t);
+          s_bad[et] = __ldg(pr.nonfinite + t);
+        }
       }
-      s_exp[et] = e;
-    }
-    named_bar_sync(1, kDecEpiThreads);
-    // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte
-    // rows) of the chunk's local k-block
-    uint8_t* planes = smem + L.b_off;
-    #pragma unroll
-    for (int r = 0; r < kDecRegChunks; ++r) {
-      const int qi = et + r * kDecEpiThreads;
-      if (r >= nsteps || qi >= nq) break;
-      const int t = qi / qpt;
-      const int cc = qi - t * qpt;
-      const int j = cc >> 5;
-      const int si = dec_sk_seg_of(sg, j) * kDecMaxTok + t;
-      const float4 v = s_bad[si] ? make_float4(0.f, 0.f, 0.f, 0.f) : keep[r];
-      const int e = s_exp[si];
-      int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
-      q8_digits(v.x, e, a0, a1, a2);
-      q8_digits(v.y, e, b0, b1, b2);
-      q8_digits(v.z, e, c0, c1, c2);
-      q8_digits(v.w, e, f0, f1, f2);
-      const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
-      const int b = (cc & 31) * 4;
-      uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+      named_bar_sync(1, kDecEpiThreads);
+    } else {
+      // pass 1: per segment and token, max |x| and the non-finite flag (32
+      // consecutive chunks are one k-block of one token: one segment)
       #pragma unroll
-      for (int pl = 0; pl < 3; ++pl) {
-        const int row = 3 * t + pl;
-        *reinterpret_cast<uint32_t*>(blk + row * kBlockBytes + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))) = w3[pl];
+      for (int r = 0; r < kDecRegChunks; ++r) {
+        const int qi = et + r * kDecEpiThreads;
+        if (r >= nsteps || qi - lane >= nq) break;  // warp-uniform
+        const float4 v = keep[r];
+        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        int bad = !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+        mx = warp_max(mx);
+        bad = warp_or(bad);
+        if (lane == 0) {
+          const int t = (qi - lane) / qpt;
+          const int s = dec_sk_seg_of(sg, ((qi - lane) - t * qpt) >> 5);
+          atomicMax(s_max + s * kDecMaxTok + t, __float_as_int(mx));
+          if (bad) atomicOr(s_bad + s * kDecMaxTok + t, 1);
+        }
       }
-    }
-    fence_proxy_async_smem();
-    named_bar_sync(1, kDecEpiThreads);
-    if (et == 0) {
-      mbar_arrive(planes_bar);
-      if (trace) trace[1] = globaltimer();
+      named_bar_sync(1, kDecEpiThreads);
+      if (et < kDecSkMaxSeg * kDecMaxTok) {
+        int e = 0;
+        const float amax = __int_as_float(s_max[et]);
+        if (!s_bad[et] && amax > 0.f) {
+          int E;
+          frexpf(amax, &E);
+          e = 22 - E;
+        }
+        s_exp[et] = e;
+      }
+      named_bar_sync(1, kDecEpiThreads);
+      // pass 2: digits into the swizzled B tiles (row 3t+p, K-major, 128-byte
+      // rows) of the chunk's local k-block
+      uint8_t* planes = smem + L.b_off;
+      #pragma unroll
+      for (int r = 0; r < kDecRegChunks; ++r) {
+        const int qi = et + r * kDecEpiThreads;
+        if (r >= nsteps || qi >= nq) break;
+        const int t = qi / qpt;
+        const int cc = qi - t * qpt;
+        const int j = cc >> 5;
+        const int si = dec_sk_seg_of(sg, j) * kDecMaxTok + t;
+        const float4 v = s_bad[si] ? make_float4(0.f, 0.f, 0.f, 0.f) : keep[r];
+        const int e = s_exp[si];
+        int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
+        q8_digits(v.x, e, a0, a1, a2);
+        q8_digits(v.y, e, b0, b1, b2);
+        q8_digits(v.z, e, c0, c1, c2);
+        q8_digits(v.w, e, f0, f1, f2);
+        const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
+        const int b = (cc & 31) * 4;
+        uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
+        #pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+          const int row = 3 * t + pl;
+          *reinterpret_cast<uint32_t*>(blk + row * kBlockBytes + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))) = w3[pl];
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, kDecEpiThreads);
+      if (et == 0) {
+        mbar_arrive(planes_bar);
+        if (trace) trace[1] = globaltimer();
+      }
     }
 
     // ------------------------------------------------------------ epilogues
@@ -562,6 +591,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (et == 0) p.counters[gt] = 0;
       }
     }
+    // planes mode after an abort: the planes copy must land before this
+    // CTA's shared memory is released
+    if (p.planes_mode && et == 0 && *abort_flag) mbar_wait(planes_bar, 0, nullptr, abort_flag, kDevTimeoutDrain, false);
     __syncwarp();
     if (lane == 0) mbar_arrive(done_bar);  // TMEM reads of this warp are complete
     if (trace && et == 0) trace[6] = globaltimer();

@@ -663,10 +663,11 @@ struct Q8Call {
   int m, n, k;
 };
 
-// A grouped batch with more 128-row tiles than SMs (one CTA per tile would
-// run in two waves) at token counts where a CTA's x slice of an equal k-block
-// share fits one register batch of the plane warps: q8_decode_sk_kernel, one
-// CTA per SM, every CTA streaming an equal share of the batch's k-blocks.
+// A grouped batch of up to 16 tokens with more 128-row tiles than SMs (one
+// CTA per tile would run in two waves): q8_decode_sk_kernel, one CTA per SM,
+// every CTA streaming an equal share of the batch's k-blocks. The kernel
+// makes the digit planes itself where a CTA's x slice fits one register batch
+// of the plane warps, else loads those of one q8_planes_group_kernel launch.
 // Problems are taken by descending K, as in the one-CTA-per-tile launch.
 // *done = false when the batch does not fit (the caller then plans it as
 // before).
@@ -696,8 +697,11 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   const int grid = ctx->sms;
   if (tiles <= grid || total < grid) return VMLM_OK;
   const int kbr = static_cast<int>(cdiv(total, grid));
-  if (static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
-    return VMLM_OK;
+  // A CTA's x slice of its share must fit one register batch of the plane
+  // warps for the kernel to make the planes itself; otherwise one
+  // q8_planes_group_kernel launch makes every problem's planes first.
+  const bool planes_mode =
+      static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
   for (int b = 0; b < grid; ++b) {
     DecSkSegs sg;
     if (!dec_sk_segments(grp.prob, count, total, grid, b, sg)) return VMLM_OK;
@@ -706,6 +710,20 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   int stages = kbr < 16 ? kbr : 16;
   while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   if (stages < 2) return VMLM_OK;
+  PlanesGroup pg;
+  std::memset(&pg, 0, sizeof(pg));
+  char* ws = nullptr;
+  if (planes_mode) {
+    // every problem's planes [3M][kp] (kp = K rounded up to 16; each region
+    // 128-byte aligned), then its exponents and flags [M] each
+    size_t bytes = 0;
+    for (int i = 0; i < count; ++i)
+      bytes += (static_cast<size_t>(3) * M * cdiv(calls[i].k, 16) * 16 + 127) / 128 * 128 + 8ull * M + 128;
+    VMLM_TRY(ensure(ctx->grp_planes, bytes));
+    ws = static_cast<char*>(ctx->grp_planes.p);
+    pg.count = count;
+    pg.m = M;
+  }
   for (int i = 0; i < count; ++i) {
     const Q8Call& q = calls[order[i]];
     DecProblem& pr = grp.prob[i];
@@ -717,12 +735,28 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
     pr.ldx = q.k;
     pr.ldo = q.n;
     pr.vec_x = (q.k % 4 == 0) && aligned16(q.a);
+    if (planes_mode) {
+      const int kp = static_cast<int>(cdiv(q.k, 16) * 16);
+      int8_t* planes = reinterpret_cast<int8_t*>(ws);
+      ws += (static_cast<size_t>(3) * M * kp + 127) / 128 * 128;
+      int* exps = reinterpret_cast<int*>(ws);
+      ws += (8ull * M + 127) / 128 * 128;
+      pr.exps = exps;
+      pr.nonfinite = exps + M;
+      VMLM_TRY(make_map(&pr.map_p, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, q.k, 3ull * M, kp, 128,
+                        static_cast<uint32_t>(rows_b)));
+      pg.prob[i] = PlanesProblem{q.a, planes, exps, exps + M, q.k, kp};
+    }
   }
+  if (planes_mode)
+    VMLM_TRY(launch(q8_planes_group_kernel, dim3(static_cast<unsigned>(M), static_cast<unsigned>(count)),
+                    dim3(kPrepThreads), 0, st, false, pg));
   // slots and counters start at zero and are left at zero by every call
   VMLM_TRY(ensure(ctx->slots, static_cast<size_t>(tiles) * M * kTileRows * 8, true));
   VMLM_TRY(ensure(ctx->counters, static_cast<size_t>(tiles) * 4, true));
   DecSkParams p = {};
   p.m = M;
+  p.planes_mode = planes_mode ? 1 : 0;
   p.rows_b = rows_b;
   p.stages = stages;
   p.tmem_cols = pow2_at_least(kDecSkMaxSeg * rows_b);

@@ -518,11 +518,14 @@ def test_q8_batch_mixed_and_edge_calls(kernels, oracle):
         assert oracle.max_rel_err(dc.cpu().numpy(), oracle.gemm_nt_int8(x, q, s)) <= TIGHT_Q8
 
 
-@pytest.mark.parametrize("m,shapes", [(2, [(2000, 1040)] * 12), (16, [(2560, 256)] * 8), (1, C3_SHAPES)])
+@pytest.mark.parametrize("m,shapes", [(2, [(2000, 1040)] * 12), (16, [(2560, 256)] * 8), (1, C3_SHAPES),
+                                     (8, [(2000, 1040)] * 12), (16, [(1200, 2304)] * 16)])
 def test_q8_batch_equal_share(kernels, oracle, m, shapes):
     """Batches with more 128-row tiles than the GPU has SMs run with an equal
     share of k-blocks per CTA: tiles split between CTAs are summed through f64
-    slots by the CTA that completes them. Ragged N, a K that ends inside a
+    slots by the CTA that completes them. The kernel makes the digit planes
+    itself (m = 1, 2 and the short-K m = 16 case) or loads those of the planes
+    kernel (m = 8, and m = 16 at K = 2304). Ragged N, a K that ends inside a
     k-block, tokens holding NaN and Inf, and the same batch twice in a row (the
     slots and counters must be left at zero): against the oracle, and the two
     calls bit-identical."""
