@@ -666,8 +666,8 @@ struct Q8Call {
 // A grouped batch of up to 16 tokens with more 128-row tiles than SMs (one
 // CTA per tile would run in two waves): q8_decode_sk_kernel, one CTA per SM,
 // every CTA streaming an equal share of the batch's k-blocks. The kernel
-// makes the digit planes itself where a CTA's x slice fits one register batch
-// of the plane warps, else loads those of one q8_planes_group_kernel launch.
+// makes the digit planes itself for one token, else loads those of one
+// q8_planes_group_kernel launch.
 // Problems are taken by descending K, as in the one-CTA-per-tile launch.
 // *done = false when the batch does not fit (the caller then plans it as
 // before).
@@ -697,10 +697,13 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   const int grid = ctx->sms;
   if (tiles <= grid || total < grid) return VMLM_OK;
   const int kbr = static_cast<int>(cdiv(total, grid));
-  // A CTA's x slice of its share must fit one register batch of the plane
-  // warps for the kernel to make the planes itself; otherwise one
-  // q8_planes_group_kernel launch makes every problem's planes first.
+  // The kernel makes the planes itself for one token whose x slice of a share
+  // fits one register batch of the plane warps. Otherwise one
+  // q8_planes_group_kernel launch makes every problem's planes first: from
+  // two tokens on, the in-kernel digit pass delays the first MMA more than
+  // the extra launch costs (C3 set at m = 2: 25.6 vs 26.8 us).
   const bool planes_mode =
+      M > 1 ||
       static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
   for (int b = 0; b < grid; ++b) {
     DecSkSegs sg;

@@ -524,18 +524,17 @@ def test_q8_batch_equal_share(kernels, oracle, m, shapes):
     """Batches with more 128-row tiles than the GPU has SMs run with an equal
     share of k-blocks per CTA: tiles split between CTAs are summed through f64
     slots by the CTA that completes them. The kernel makes the digit planes
-    itself (m = 1, 2 and the short-K m = 16 case) or loads those of the planes
-    kernel (m = 8, and m = 16 at K = 2304). Ragged N, a K that ends inside a
+    itself (m = 1) or loads those of the planes kernel (m = 2, 8, 16). Ragged N, a K that ends inside a
     k-block, tokens holding NaN and Inf, and the same batch twice in a row (the
     slots and counters must be left at zero): against the oracle, and the two
     calls bit-identical."""
     import torch
     calls, host = _batch(oracle, m, shapes, seed=300 + m)
-    if m > 1:
-        host[3][0][1, 5] = np.nan
-        host[7][0][0, shapes[7][1] - 1] = -np.inf
-        for i in (3, 7):
-            calls[i][0].copy_(torch.from_numpy(host[i][0]))
+    a, b = 1, len(shapes) - 2
+    host[a][0][m - 1, 5] = np.nan
+    host[b][0][0, shapes[b][1] - 1] = -np.inf
+    for i in (a, b):
+        calls[i][0].copy_(torch.from_numpy(host[i][0]))
     st = torch.cuda.current_stream()
     outs = []
     for _ in range(2):
