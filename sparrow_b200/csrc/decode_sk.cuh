@@ -58,9 +58,12 @@ constexpr int kDecSkMaxSeg = 4;
 
 struct DecSkParams {
   int m;
-  // planes mode: the digit planes, exponents and non-finite flags come from
-  // q8_planes_group_kernel (each problem's map_p, exps, nonfinite: one
-  // exponent per token over the problem's whole K) instead of being made here
+  // 0: the kernel makes the digit planes. 1, 2 (planes mode): the planes,
+  // exponents and non-finite flags come from q8_planes_group_kernel (each
+  // problem's map_p, exps, nonfinite: one exponent per token over the
+  // problem's whole K); 1 loads the range's planes once into a resident
+  // region, 2 loads each k-block's planes into the ring stage of its W box
+  // (for ranges whose planes do not fit shared memory beside a ring)
   int planes_mode;
   int rows_b;          // UMMA N: plane rows, 16 * ceil(3m / 16)
   int stages;          // W stage ring depth
@@ -75,13 +78,15 @@ struct DecSkParams {
 };
 
 struct DecSkSmem {
-  uint32_t b_off, bar_off, meta_off, total;
+  uint32_t stage, b_off, bar_off, meta_off, total;
 };
 
-__host__ __device__ inline DecSkSmem dec_sk_smem_layout(int stages, int rows_b, int kbr) {
+__host__ __device__ inline DecSkSmem dec_sk_smem_layout(int stages, int rows_b, int kbr, int planes_mode) {
   DecSkSmem s;
-  s.b_off = static_cast<uint32_t>(stages) * kDecStageBytes;  // W stages first, from offset 0
-  s.bar_off = s.b_off + static_cast<uint32_t>(kbr) * rows_b * kBlockBytes;
+  // a ring stage: the W box, then in planes mode 2 the k-block's planes
+  s.stage = kDecStageBytes + (planes_mode == 2 ? static_cast<uint32_t>(rows_b) * kBlockBytes : 0u);
+  s.b_off = static_cast<uint32_t>(stages) * s.stage;  // the ring first, from offset 0
+  s.bar_off = s.b_off + (planes_mode == 2 ? 0u : static_cast<uint32_t>(kbr) * rows_b * kBlockBytes);
   // full[stages], empty[stages], planes, tfull[kDecSkMaxSeg], done, drain; then the TMEM address and an abort word
   s.meta_off = s.bar_off + (2 * stages + 3 + kDecSkMaxSeg) * 8 + 16;
   // per segment and token: max |x| bits, non-finite flag, exponent; per segment: the finishing flag
@@ -223,7 +228,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  const DecSkSmem L = dec_sk_smem_layout(p.stages, p.rows_b, p.kbr_max);
+  const DecSkSmem L = dec_sk_smem_layout(p.stages, p.rows_b, p.kbr_max, p.planes_mode);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty_bar = full_bar + p.stages;
   uint64_t* planes_bar = empty_bar + p.stages;
@@ -278,12 +283,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const uint64_t pol = policy_evict_first();
   int pstage = 0, pj = 0;
   uint32_t pphase = 0, issued_mask = 0, last_phase = 0;
+  bool planes_ok = false;  // planes mode 2: the planes kernel has finished (loads may read its planes)
   auto issue = [&](int j) {
     const int s = dec_sk_seg_of(sg, j);
     const int kb = dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s);
-    mbar_arrive_expect_tx(full_bar + pstage, kDecStageBytes);
-    tma_load_2d(smem + pstage * kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map, full_bar + pstage,
-                kb * kBlockBytes, dec_sk_pick(sg.tile, s) * kTileRows, pol);
+    mbar_arrive_expect_tx(full_bar + pstage, L.stage);
+    tma_load_2d(smem + pstage * L.stage, &grp.prob[dec_sk_pick(sg.g, s)].map, full_bar + pstage, kb * kBlockBytes,
+                dec_sk_pick(sg.tile, s) * kTileRows, pol);
+    if (p.planes_mode == 2 && planes_ok)
+      tma_load_2d(smem + pstage * L.stage + kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, full_bar + pstage,
+                  kb * kBlockBytes, 0, policy_evict_last());
     if (trace && issued_mask == 0) trace[8] = globaltimer();
     issued_mask |= 1u << pstage;
     last_phase = (last_phase & ~(1u << pstage)) | (pphase << pstage);
@@ -326,6 +335,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------ W producer
     if (lane == 0) {
+      if (p.planes_mode == 2) {
+        // the planes of the first ring, whose W boxes went out before the
+        // wait for the planes kernel (same stages, same full barriers)
+        pdl_wait_prior();
+        planes_ok = true;
+        for (int j = 0; j < pj; ++j) {
+          const int s = dec_sk_seg_of(sg, j);
+          tma_load_2d(smem + j * L.stage + kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, full_bar + j,
+                      (dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s)) * kBlockBytes, 0, policy_evict_last());
+        }
+      }
       for (; pj < nkb; ++pj) {
         if (!mbar_wait(empty_bar + pstage, pphase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
         issue(pj);
@@ -360,8 +380,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             tc_fence_after();
             if (trace && !issued) trace[3] = globaltimer();
-            const uint32_t a_addr = smem_u32(smem + stage * kDecStageBytes);
-            const uint32_t b_addr = smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
+            const uint32_t a_addr = smem_u32(smem + stage * L.stage);
+            const uint32_t b_addr = p.planes_mode == 2 ? a_addr + kDecStageBytes
+                                                       : smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
             #pragma unroll
             for (uint32_t u = 0; u < 4; ++u)
               umma_i8(acc, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
@@ -386,9 +407,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   } else {
     // ----------------------------------- digit planes, then the epilogues
     if (p.planes_mode) {
-      // one TMA load per k-block of the range from its problem's planes
-      // (rows past 3m read as zero), and the problems' exponents and flags
-      if (et == 0) {
+      // mode 1: one TMA load per k-block of the range from its problem's
+      // planes (rows past 3m read as zero); mode 2: the producer loads them
+      // with the W boxes. Then the problems' exponents and flags.
+      if (et == 0 && p.planes_mode == 2) mbar_arrive(planes_bar);
+      if (et == 0 && p.planes_mode == 1) {
         mbar_arrive_expect_tx(planes_bar, static_cast<uint32_t>(nkb * p.rows_b * kBlockBytes));
         for (int j = 0; j < nkb; ++j) {
           const int s = dec_sk_seg_of(sg, j);

@@ -663,7 +663,7 @@ struct Q8Call {
   int m, n, k;
 };
 
-// A grouped batch of up to 16 tokens with more 128-row tiles than SMs (one
+// A grouped batch of up to 32 tokens with more 128-row tiles than SMs (one
 // CTA per tile would run in two waves): q8_decode_sk_kernel, one CTA per SM,
 // every CTA streaming an equal share of the batch's k-blocks. The kernel
 // makes the digit planes itself for one token, else loads those of one
@@ -674,7 +674,7 @@ struct Q8Call {
 int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, bool* done) {
   *done = false;
   const int M = calls[0].m;
-  if (M < 1 || M > 16) return VMLM_OK;
+  if (M < 1 || M > kDecMaxTok) return VMLM_OK;
   int order[kDecMaxGroup];
   for (int i = 0; i < count; ++i) order[i] = i;
   std::stable_sort(order, order + count, [&](int x, int y) { return calls[x].k > calls[y].k; });
@@ -710,8 +710,16 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
     if (!dec_sk_segments(grp.prob, count, total, grid, b, sg)) return VMLM_OK;
   }
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
-  int stages = kbr < 16 ? kbr : 16;
-  while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  // planes mode: the range's planes resident (mode 1) where they fit beside a
+  // ring of at least two stages, else each k-block's planes in its ring stage
+  // (mode 2)
+  int mode = planes_mode ? 1 : 0, stages = 0;
+  for (;; ++mode) {
+    stages = kbr < 16 ? kbr : 16;
+    while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr, mode).total > static_cast<uint32_t>(kMaxSmem))
+      --stages;
+    if (stages >= 2 || mode != 1) break;
+  }
   if (stages < 2) return VMLM_OK;
   PlanesGroup pg;
   std::memset(&pg, 0, sizeof(pg));
@@ -759,7 +767,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   VMLM_TRY(ensure(ctx->counters, static_cast<size_t>(tiles) * 4, true));
   DecSkParams p = {};
   p.m = M;
-  p.planes_mode = planes_mode ? 1 : 0;
+  p.planes_mode = mode;
   p.rows_b = rows_b;
   p.stages = stages;
   p.tmem_cols = pow2_at_least(kDecSkMaxSeg * rows_b);
@@ -770,7 +778,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   p.counters = static_cast<int*>(ctx->counters.p);
   p.err = ctx->err;
   p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
-  const uint32_t smem = dec_sk_smem_layout(stages, rows_b, kbr).total;
+  const uint32_t smem = dec_sk_smem_layout(stages, rows_b, kbr, mode).total;
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   VMLM_TRY(launch(q8_decode_sk_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st, true, p, grp));

@@ -519,15 +519,22 @@ def test_q8_batch_mixed_and_edge_calls(kernels, oracle):
 
 
 @pytest.mark.parametrize("m,shapes", [(2, [(2000, 1040)] * 12), (16, [(2560, 256)] * 8), (1, C3_SHAPES),
-                                     (8, [(2000, 1040)] * 12), (16, [(1200, 2304)] * 16)])
+                                     (8, [(2000, 1040)] * 12), (16, [(1200, 2304)] * 16),
+                                     (32, [(2000, 1040)] * 12), (32, C3_SHAPES)])
 def test_q8_batch_equal_share(kernels, oracle, m, shapes):
     """Batches with more 128-row tiles than the GPU has SMs run with an equal
     share of k-blocks per CTA: tiles split between CTAs are summed through f64
     slots by the CTA that completes them. The kernel makes the digit planes
-    itself (m = 1) or loads those of the planes kernel (m = 2, 8, 16). Ragged N, a K that ends inside a
-    k-block, tokens holding NaN and Inf, and the same batch twice in a row (the
-    slots and counters must be left at zero): against the oracle, and the two
-    calls bit-identical."""
+    itself (m = 1) or loads those of the planes kernel (m = 2 to 32): once per
+    range where they fit shared memory, else per k-block with its weight box
+    (the C3 set at m = 32)."""
+    _equal_share_case(kernels, oracle, m, shapes)
+
+
+def _equal_share_case(kernels, oracle, m, shapes):
+    """Ragged N, a K that ends inside a k-block, tokens holding NaN and Inf,
+    and the same batch twice in a row (the slots and counters must be left at
+    zero): against the oracle, and the two calls bit-identical."""
     import torch
     calls, host = _batch(oracle, m, shapes, seed=300 + m)
     a, b = 1, len(shapes) - 2
