@@ -58,12 +58,11 @@ constexpr int kDecSkMaxSeg = 4;
 
 struct DecSkParams {
   int m;
-  // 0: the kernel makes the digit planes. 1, 2 (planes mode): the planes,
+  // 0: the kernel makes the digit planes. 1 (planes mode): the planes,
   // exponents and non-finite flags come from q8_planes_group_kernel (each
   // problem's map_p, exps, nonfinite: one exponent per token over the
-  // problem's whole K); 1 loads the range's planes once into a resident
-  // region, 2 loads each k-block's planes into the ring stage of its W box
-  // (for ranges whose planes do not fit shared memory beside a ring)
+  // problem's whole K), and each k-block's planes are loaded into the ring
+  // stage of its W box
   int planes_mode;
   int rows_b;          // UMMA N: plane rows, 16 * ceil(3m / 16)
   int stages;          // W stage ring depth
@@ -83,10 +82,11 @@ struct DecSkSmem {
 
 __host__ __device__ inline DecSkSmem dec_sk_smem_layout(int stages, int rows_b, int kbr, int planes_mode) {
   DecSkSmem s;
-  // a ring stage: the W box, then in planes mode 2 the k-block's planes
-  s.stage = kDecStageBytes + (planes_mode == 2 ? static_cast<uint32_t>(rows_b) * kBlockBytes : 0u);
+  // a ring stage: the W box, then in planes mode the k-block's planes; the
+  // planes the kernel makes itself follow the ring
+  s.stage = kDecStageBytes + (planes_mode ? static_cast<uint32_t>(rows_b) * kBlockBytes : 0u);
   s.b_off = static_cast<uint32_t>(stages) * s.stage;  // the ring first, from offset 0
-  s.bar_off = s.b_off + (planes_mode == 2 ? 0u : static_cast<uint32_t>(kbr) * rows_b * kBlockBytes);
+  s.bar_off = s.b_off + (planes_mode ? 0u : static_cast<uint32_t>(kbr) * rows_b * kBlockBytes);
   // full[stages], empty[stages], planes, tfull[kDecSkMaxSeg], done, drain; then the TMEM address and an abort word
   s.meta_off = s.bar_off + (2 * stages + 3 + kDecSkMaxSeg) * 8 + 16;
   // per segment and token: max |x| bits, non-finite flag, exponent; per segment: the finishing flag
@@ -283,14 +283,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const uint64_t pol = policy_evict_first();
   int pstage = 0, pj = 0;
   uint32_t pphase = 0, issued_mask = 0, last_phase = 0;
-  bool planes_ok = false;  // planes mode 2: the planes kernel has finished (loads may read its planes)
+  bool planes_ok = false;  // planes mode: the planes kernel has finished (loads may read its planes)
   auto issue = [&](int j) {
     const int s = dec_sk_seg_of(sg, j);
     const int kb = dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s);
     mbar_arrive_expect_tx(full_bar + pstage, L.stage);
     tma_load_2d(smem + pstage * L.stage, &grp.prob[dec_sk_pick(sg.g, s)].map, full_bar + pstage, kb * kBlockBytes,
                 dec_sk_pick(sg.tile, s) * kTileRows, pol);
-    if (p.planes_mode == 2 && planes_ok)
+    if (p.planes_mode && planes_ok)
       tma_load_2d(smem + pstage * L.stage + kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, full_bar + pstage,
                   kb * kBlockBytes, 0, policy_evict_last());
     if (trace && issued_mask == 0) trace[8] = globaltimer();
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------ W producer
     if (lane == 0) {
-      if (p.planes_mode == 2) {
+      if (p.planes_mode) {
         // the planes of the first ring, whose W boxes went out before the
         // wait for the planes kernel (same stages, same full barriers)
         pdl_wait_prior();
@@ -381,8 +381,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             tc_fence_after();
             if (trace && !issued) trace[3] = globaltimer();
             const uint32_t a_addr = smem_u32(smem + stage * L.stage);
-            const uint32_t b_addr = p.planes_mode == 2 ? a_addr + kDecStageBytes
-                                                       : smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
+            const uint32_t b_addr =
+                p.planes_mode ? a_addr + kDecStageBytes : smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
             #pragma unroll
             for (uint32_t u = 0; u < 4; ++u)
               umma_i8(acc, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
@@ -407,19 +407,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   } else {
     // ----------------------------------- digit planes, then the epilogues
     if (p.planes_mode) {
-      // mode 1: one TMA load per k-block of the range from its problem's
-      // planes (rows past 3m read as zero); mode 2: the producer loads them
-      // with the W boxes. Then the problems' exponents and flags.
-      if (et == 0 && p.planes_mode == 2) mbar_arrive(planes_bar);
-      if (et == 0 && p.planes_mode == 1) {
-        mbar_arrive_expect_tx(planes_bar, static_cast<uint32_t>(nkb * p.rows_b * kBlockBytes));
-        for (int j = 0; j < nkb; ++j) {
-          const int s = dec_sk_seg_of(sg, j);
-          tma_load_2d(smem + L.b_off + j * p.rows_b * kBlockBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, planes_bar,
-                      (dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s)) * kBlockBytes, 0, policy_evict_last());
-        }
-        if (trace) trace[1] = globaltimer();
-      }
+      // the producer loads the planes with the W boxes; here the problems'
+      // exponents and flags
+      if (et == 0) mbar_arrive(planes_bar);
       if (et < kDecSkMaxSeg * kDecMaxTok) {
         const int s = et / kDecMaxTok, t = et - s * kDecMaxTok;
         if (s < sg.n && t < p.m) {
@@ -429,6 +419,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
       }
       named_bar_sync(1, kDecEpiThreads);
+      if (trace && et == 0) trace[1] = globaltimer();
     } else {
       // pass 1: per segment and token, max |x| and the non-finite flag (32
       // consecutive chunks are one k-block of one token: one segment)
@@ -614,9 +605,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (et == 0) p.counters[gt] = 0;
       }
     }
-    // planes mode after an abort: the planes copy must land before this
-    // CTA's shared memory is released
-    if (p.planes_mode && et == 0 && *abort_flag) mbar_wait(planes_bar, 0, nullptr, abort_flag, kDevTimeoutDrain, false);
     __syncwarp();
     if (lane == 0) mbar_arrive(done_bar);  // TMEM reads of this warp are complete
     if (trace && et == 0) trace[6] = globaltimer();

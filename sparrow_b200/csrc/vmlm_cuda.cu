@@ -710,16 +710,13 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
     if (!dec_sk_segments(grp.prob, count, total, grid, b, sg)) return VMLM_OK;
   }
   const int rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
-  // planes mode: the range's planes resident (mode 1) where they fit beside a
-  // ring of at least two stages, else each k-block's planes in its ring stage
-  // (mode 2)
-  int mode = planes_mode ? 1 : 0, stages = 0;
-  for (;; ++mode) {
-    stages = kbr < 16 ? kbr : 16;
-    while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr, mode).total > static_cast<uint32_t>(kMaxSmem))
-      --stages;
-    if (stages >= 2 || mode != 1) break;
-  }
+  // In planes mode each k-block's planes ride in the ring stage of its W box,
+  // so the MMA starts on the first stage (loading the range's planes once, up
+  // front, measured 1-2 us slower at m = 2..16 and does not fit at m = 32).
+  const int mode = planes_mode ? 1 : 0;
+  int stages = kbr < 16 ? kbr : 16;
+  while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr, mode).total > static_cast<uint32_t>(kMaxSmem))
+    --stages;
   if (stages < 2) return VMLM_OK;
   PlanesGroup pg;
   std::memset(&pg, 0, sizeof(pg));

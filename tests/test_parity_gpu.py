@@ -525,9 +525,8 @@ def test_q8_batch_equal_share(kernels, oracle, m, shapes):
     """Batches with more 128-row tiles than the GPU has SMs run with an equal
     share of k-blocks per CTA: tiles split between CTAs are summed through f64
     slots by the CTA that completes them. The kernel makes the digit planes
-    itself (m = 1) or loads those of the planes kernel (m = 2 to 32): once per
-    range where they fit shared memory, else per k-block with its weight box
-    (the C3 set at m = 32)."""
+    itself (m = 1) or loads those of the planes kernel with each weight box
+    (m = 2 to 32)."""
     _equal_share_case(kernels, oracle, m, shapes)
 
 
