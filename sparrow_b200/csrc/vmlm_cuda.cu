@@ -701,7 +701,8 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   // fits one register batch of the plane warps. Otherwise one
   // q8_planes_group_kernel launch makes every problem's planes first: from
   // two tokens on, the in-kernel digit pass delays the first MMA more than
-  // the extra launch costs (C3 set at m = 2: 25.6 vs 26.8 us).
+  // the extra launch costs (a 2304-hidden decoder layer's seven linears at
+  // m = 2: 25.6 vs 26.8 us).
   const bool planes_mode =
       M > 1 ||
       static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads;
