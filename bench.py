@@ -104,6 +104,7 @@ CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf1
          "c5": ("i8", 4096, 28672, 8192), "c5small": ("i8", 1024, 4096, 8192),
          "c4m64small": ("q8", 64, 16384, 2304), "c3q_m32": ("q8", 32, 2304, 2304), "c3d_m32": ("q8", 32, 2304, 5760),
          "c3g_m32": ("q8", 32, 5760, 2304), "c3b_m1": ("q8batch", 1, 0, 0), "c3b_m2": ("q8batch", 2, 0, 0),
+         "c3b_m8": ("q8batch", 8, 0, 0), "c3b_m32": ("q8batch", 32, 0, 0),
          "f32nt": ("f32nt", M2, N2, K2), "f32nn": ("f32nn", M2, N2, K2)}
 
 
