@@ -32,6 +32,11 @@ thread_local std::string g_err;
 std::recursive_mutex g_mu;
 std::atomic<uint64_t> g_launches{0};
 
+// Allocation-free Q8 entry point (end of this file): whether its scratch is set
+// up on a device, and its device error word, read and cleared by vmlm_sync.
+bool na_ready(int dev);
+int na_take_error(int dev, int* code);
+
 int fail(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
@@ -69,7 +74,7 @@ struct DevBuf {
 // Grow-only device buffer. Growing frees the old buffer (cudaFree waits for
 // the device), so a call that needs more workspace than any earlier call
 // cannot be captured into a CUDA graph.
-int ensure(DevBuf& b, size_t bytes, bool zero = false) {
+int ensure(DevBuf& b, size_t bytes) {
   if (bytes == 0) bytes = 16;
   if (b.bytes >= bytes) return VMLM_OK;
   size_t nb = b.bytes * 2 > bytes ? b.bytes * 2 : bytes;
@@ -78,8 +83,18 @@ int ensure(DevBuf& b, size_t bytes, bool zero = false) {
   b.p = nullptr;
   b.bytes = 0;
   VMLM_CUDA(cudaMalloc(&b.p, nb));
-  if (zero) VMLM_CUDA(cudaMemset(b.p, 0, nb));
   b.bytes = nb;
+  return VMLM_OK;
+}
+
+// ensure() for buffers whose kernels expect zeros (split-tile slots and
+// counters, flag words): a newly allocated buffer is cleared on `st`, the
+// stream of the call that is about to use it, so the clear is ordered before
+// that call's kernels whichever stream (library, caller's, non-blocking) it is.
+int ensure_zeroed(DevBuf& b, size_t bytes, cudaStream_t st) {
+  const size_t had = b.bytes;
+  VMLM_TRY(ensure(b, bytes));
+  if (b.bytes != had) VMLM_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, st));
   return VMLM_OK;
 }
 
@@ -447,8 +462,8 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   if (grid < 1) grid = 1;
   p.streamk = streamk ? 1 : 0;
   if (streamk && kSwapMode) {
-    VMLM_TRY(ensure(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, true));
-    VMLM_TRY(ensure(c->counters, static_cast<size_t>(tiles) * 4, true));
+    VMLM_TRY(ensure_zeroed(c->slots, static_cast<size_t>(grid) * kTileRows * p.bn * 4, st));
+    VMLM_TRY(ensure_zeroed(c->counters, static_cast<size_t>(tiles) * 4, st));
   }
   const int cluster = p.csplit > 1 ? p.csplit : 1;
   p.slots = static_cast<uint32_t*>(c->slots.p);
@@ -761,8 +776,8 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
     VMLM_TRY(launch(q8_planes_group_kernel, dim3(static_cast<unsigned>(M), static_cast<unsigned>(count)),
                     dim3(kPrepThreads), 0, st, false, pg));
   // slots and counters start at zero and are left at zero by every call
-  VMLM_TRY(ensure(ctx->slots, static_cast<size_t>(tiles) * M * kTileRows * 8, true));
-  VMLM_TRY(ensure(ctx->counters, static_cast<size_t>(tiles) * 4, true));
+  VMLM_TRY(ensure_zeroed(ctx->slots, static_cast<size_t>(tiles) * M * kTileRows * 8, st));
+  VMLM_TRY(ensure_zeroed(ctx->counters, static_cast<size_t>(tiles) * 4, st));
   DecSkParams p = {};
   p.m = M;
   p.planes_mode = mode;
@@ -943,12 +958,12 @@ int shard_check(float* const* c_peers, unsigned* const* inbox_peers, int rank, i
 }
 
 int shard_setup(Ctx* ctx, float* const* c_peers, unsigned* const* inbox_peers, int rank, int world, size_t m,
-                size_t n, Shard* sh, size_t* nloc) {
+                size_t n, cudaStream_t st, Shard* sh, size_t* nloc) {
   VMLM_TRY(shard_check(c_peers, inbox_peers, rank, world, m, n));
   const size_t rows = (n + world - 1) / world;
   const size_t r0 = rows * rank;
   *nloc = (r0 + rows < n ? r0 + rows : n) - r0;
-  VMLM_TRY(ensure(ctx->shard_done, 256, true));
+  VMLM_TRY(ensure_zeroed(ctx->shard_done, 256, st));
   sh->world = world;
   sh->rank = rank;
   sh->col_off = static_cast<long long>(r0);
@@ -1076,7 +1091,7 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
     c->norm_m = M;
     c->norm_kp = kp;
   }
-  VMLM_TRY(ensure(c->norm_flags, 256, true));
+  VMLM_TRY(ensure_zeroed(c->norm_flags, 256, st));
   unsigned* fw = static_cast<unsigned*>(c->norm_flags.p);
   unsigned* orword = fw + 32 * c->norm_parity;  // the two words sit on separate 128-byte lines
   unsigned* orword_next = fw + 32 * (c->norm_parity ^ 1u);
@@ -1158,7 +1173,7 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
     c->f32_kp = kp;
     c->f32_b_from_t = false;
   }
-  VMLM_TRY(ensure(c->f32_flags, 512, true));
+  VMLM_TRY(ensure_zeroed(c->f32_flags, 512, st));
   unsigned* fw = static_cast<unsigned*>(c->f32_flags.p);  // four words on separate 128-byte lines
   const unsigned par = c->f32_parity;
   c->f32_parity ^= 1u;
@@ -1241,7 +1256,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   uint16_t* terms = static_cast<uint16_t*>(c->act.p);
   int* flags = static_cast<int*>(c->small.p) + 2 * M;
   int* nonf = static_cast<int*>(c->small.p) + M;
-  VMLM_TRY(ensure(c->sync, 64, true));
+  VMLM_TRY(ensure_zeroed(c->sync, 64, st));
   unsigned* done = static_cast<unsigned*>(c->sync.p);
   VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
                   kp, 0, terms, flags, nonf, done));
@@ -2448,8 +2463,8 @@ int vmlm_sharded_gemm_nt_int8_dev(const float* a, const int8_t* q_shard, const f
   VMLM_TRY(current_ctx(&ctx));
   Shard sh;
   size_t nloc = 0;
-  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, &sh, &nloc));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, st, &sh, &nloc));
   return run_q8(ctx, a, q_shard, scale_shard, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                 static_cast<int>(k), st, &sh);
 }
@@ -2467,8 +2482,8 @@ int vmlm_sharded_gemm_i8i8_dev(const int8_t* x, const int8_t* w_shard, const flo
   VMLM_TRY(current_ctx(&ctx));
   Shard sh;
   size_t nloc = 0;
-  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, &sh, &nloc));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, st, &sh, &nloc));
   return run_i8i8(ctx, x, w_shard, scale_shard, nullptr, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                   static_cast<int>(k), st, &sh);
 }
@@ -2482,18 +2497,34 @@ int vmlm_set_host_pipeline(int max_chunks) {
 
 int vmlm_sync(void* stream) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
+  int dev = -1;
+  VMLM_CUDA(cudaGetDevice(&dev));
+  // The allocation-free entry point keeps its own error word; read it first.
+  // A device that has only seen allocation-free calls gets no context here,
+  // so this call allocates nothing for such a caller either.
+  int na_code = 0;
+  VMLM_TRY(na_take_error(dev, &na_code));
+  if (na_code != 0 && g_ctx.find(dev) == g_ctx.end()) return device_error(na_code);
+  if (na_ready(dev) && g_ctx.find(dev) == g_ctx.end()) {
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
+    VMLM_CUDA(cudaStreamSynchronize(st));
+    return VMLM_OK;
+  }
   Ctx* ctx = nullptr;
   VMLM_TRY(current_ctx(&ctx));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   VMLM_CUDA(cudaStreamSynchronize(st));
+  if (na_code != 0) return device_error(na_code);
   int code = 0;
   VMLM_CUDA(cudaMemcpy(&code, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
-    cudaMemset(ctx->err, 0, sizeof(int));
-    if (ctx->counters.p) cudaMemset(ctx->counters.p, 0, ctx->counters.bytes);
-    if (ctx->sync.p) cudaMemset(ctx->sync.p, 0, ctx->sync.bytes);
-    if (ctx->slots.p) cudaMemset(ctx->slots.p, 0, ctx->slots.bytes);
-    if (ctx->shard_done.p) cudaMemset(ctx->shard_done.p, 0, ctx->shard_done.bytes);
+    // clear on the same stream and wait, so the next call on any stream sees zeros
+    cudaMemsetAsync(ctx->err, 0, sizeof(int), st);
+    if (ctx->counters.p) cudaMemsetAsync(ctx->counters.p, 0, ctx->counters.bytes, st);
+    if (ctx->sync.p) cudaMemsetAsync(ctx->sync.p, 0, ctx->sync.bytes, st);
+    if (ctx->slots.p) cudaMemsetAsync(ctx->slots.p, 0, ctx->slots.bytes, st);
+    if (ctx->shard_done.p) cudaMemsetAsync(ctx->shard_done.p, 0, ctx->shard_done.bytes, st);
+    VMLM_CUDA(cudaStreamSynchronize(st));
     return device_error(code);
   }
   return VMLM_OK;
@@ -2574,6 +2605,28 @@ int na_setup(int dev, NaDevice** out) {
     d.ready = true;
   }
   *out = &d;
+  return VMLM_OK;
+}
+
+bool na_ready(int dev) { return dev >= 0 && dev < 64 && g_na[dev].ready; }
+
+// The allocation-free calls record a kernel's bounded-wait timeout in the
+// array's own error word. Read it after the whole device is idle (those calls
+// may run on any stream); on an error, clear the word together with the
+// split-tile counters and slots, which an aborted launch can leave non-zero
+// and which every later call would otherwise sum into. Allocates nothing.
+int na_take_error(int dev, int* code) {
+  *code = 0;
+  if (!na_ready(dev)) return VMLM_OK;
+  NaDevice& d = g_na[dev];
+  VMLM_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  VMLM_CUDA(cudaMemcpy(&v, d.base + kNaErrOff, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    VMLM_CUDA(cudaMemset(d.base, 0, kNaPlanesOff));
+    VMLM_CUDA(cudaDeviceSynchronize());
+    *code = v;
+  }
   return VMLM_OK;
 }
 

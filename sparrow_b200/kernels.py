@@ -175,11 +175,15 @@ def gemm_nt_int8_dev_noalloc(a, q, scale, c, m, n, k, stream=None) -> None:
     """gemm_nt_int8_dev without any device allocation: its scratch is a fixed
     array inside the library (m <= 16, n <= 131072, k <= 16384). For callers
     that reserve all device memory up front and must not allocate per call.
-    Calls that overlap on the GPU share that scratch and race."""
+    Calls that overlap on the GPU share that scratch and race.
+
+    stream=None runs on the CUDA legacy default stream (the C entry point's
+    NULL), not on the library stream that None selects for the other *_dev
+    calls; pass a stream to order it with other work."""
+    st = ctypes.c_void_p(CUDA_STREAM_LEGACY) if stream is None else _stream_ptr(stream)
     check(lib().vmlm_gemm_nt_int8_dev_noalloc(
         _dev_ptr(a, "float32", m * k, "a"), _dev_ptr(q, "int8", n * k, "q"),
-        _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"), m, n, k,
-        _stream_ptr(stream)))
+        _dev_ptr(scale, "float32", n, "scale"), _dev_ptr(c, "float32", m * n, "c"), m, n, k, st))
 
 
 def gemm_nt_bf16_dev(a, b, c, m, n, k, stream=None) -> None:

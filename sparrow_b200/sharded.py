@@ -104,6 +104,56 @@ class PeerOutputs:
         self.reset()
 
 
+class RankLost(RuntimeError):
+    """A rank of a sharded group left, or stopped answering, between steps."""
+
+    def __init__(self, rank: int, how: str):
+        self.rank = rank
+        super().__init__(f"rank {rank} {how}")
+
+
+class StepGate:
+    """Host-side liveness check before each step of row-sharded calls.
+
+    A sharded call ends only when every rank's outputs have landed, so a rank
+    that is gone makes the others' kernels wait until their bounded wait runs
+    out. The gate finds that out on the host first: `enter(step)` posts this
+    rank's step number to the process group's key-value store and waits, for at
+    most `timeout_s`, until every rank has posted that step; a rank that has
+    called `leave()` (between steps, with nothing of its own in flight) raises
+    RankLost at once, and one that posts nothing in time raises RankLost when
+    the limit runs out. Only then is the step's kernel launched. The store is
+    torch.distributed's (any object with set / get / check works)."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "vmlm_gate"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, what: str, q: int) -> str:
+        return f"{self.prefix}/{what}/{q}"
+
+    def enter(self, step: int) -> None:
+        import time
+        self.store.set(self._key("step", self.rank), str(step))
+        waiting = [q for q in range(self.world) if q != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        while waiting:
+            for q in list(waiting):
+                if self.store.check([self._key("left", q)]):
+                    raise RankLost(q, f"left the group before step {step}")
+                key = self._key("step", q)
+                if self.store.check([key]) and int(self.store.get(key)) >= step:
+                    waiting.remove(q)
+            if waiting and time.monotonic() > deadline:
+                raise RankLost(waiting[0], f"did not reach step {step} within {self.timeout_s} s")
+            if waiting:
+                time.sleep(0.001)
+
+    def leave(self) -> None:
+        """Announce that this rank takes no further steps (call between steps)."""
+        self.store.set(self._key("left", self.rank), "1")
+
+
 def _dev(x, dtype, count, name):
     from .kernels import _dev_ptr
     return _dev_ptr(x, dtype, count, name)

@@ -156,3 +156,55 @@ def test_two_gpu_sharded_calls_give_every_rank_the_whole_result():
         msgs.append(errors.get())
     assert all(p.exitcode == 0 for p in procs), msgs
     assert not msgs, msgs
+
+
+@pytest.mark.timeout(120)
+def test_missing_rank_makes_the_bounded_wait_run_out_and_the_next_call_is_correct(kernels, oracle):
+    """Failure detection without a GPU fault. A two-rank call is made on one GPU
+    for rank 0 only: rank 1's C and inbox are local buffers that no process
+    serves, so rank 1's count never arrives (a flag that nothing sets). The
+    kernel's bounded wait for it (5 s) runs out, it records the timeout and
+    returns; vmlm_sync reports VMLM_ERR_DEVICE_TIMEOUT. After
+    vmlm_sharded_reset the context is usable and the next call (a single-rank
+    call on the same buffers) matches the oracle."""
+    import ctypes
+    import torch
+    from sparrow_b200 import VmlmError
+    from sparrow_b200._lib import lib
+    from sparrow_b200.sharded import shard_rows
+    m, n, k = 1, 4096, 2304
+    x = oracle.fill_normal(m * k, 80, 1.0).reshape(m, k)
+    q, s = oracle.quant_int8(oracle.fill_normal(n * k, 81, 0.02).reshape(n, k))
+    ref = oracle.gemm_nt_int8(x, q, s, nt=os.cpu_count() or 1)
+    dx, dq, ds = torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    c = [torch.zeros((m, n), dtype=torch.float32, device="cuda") for _ in range(2)]
+    inbox = [torch.zeros(4, dtype=torch.int32, device="cuda") for _ in range(2)]
+    for b in inbox:
+        assert lib().vmlm_sharded_reset(ctypes.c_void_p(b.data_ptr())) == 0
+    c_ptrs = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in c])
+    in_ptrs = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in inbox])
+    st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream or 1)
+    r0, r1 = shard_rows(n, 2, 0)
+    qs, ss = dq[r0:r1].contiguous(), ds[r0:r1].contiguous()
+    rc = lib().vmlm_sharded_gemm_nt_int8_dev(
+        ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(qs.data_ptr()), ctypes.c_void_p(ss.data_ptr()),
+        c_ptrs, in_ptrs, 0, 2, m, n, k, sp)
+    assert rc == 0
+    with pytest.raises(VmlmError) as info:
+        kernels.sync(st)
+    assert info.value.status == 7, str(info.value)  # VMLM_ERR_DEVICE_TIMEOUT
+    # rank 0's own columns reached both Cs before the wait; rank 1's never came
+    got = c[0].cpu().numpy()
+    assert oracle.max_rel_err(got[:, r0:r1], ref[:, r0:r1]) <= TIGHT_Q8
+    assert np.all(got[:, r1:] == 0)
+    for b in inbox:
+        assert lib().vmlm_sharded_reset(ctypes.c_void_p(b.data_ptr())) == 0
+    for _ in range(2):
+        c[0].fill_(float("nan"))
+        rc = lib().vmlm_sharded_gemm_nt_int8_dev(
+            ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(dq.data_ptr()), ctypes.c_void_p(ds.data_ptr()),
+            c_ptrs, in_ptrs, 0, 1, m, n, k, sp)
+        assert rc == 0
+        kernels.sync(st)
+        assert oracle.max_rel_err(c[0].cpu().numpy(), ref) <= TIGHT_Q8

@@ -53,3 +53,33 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(kernels):
     with pytest.raises(VmlmError) as info:
         kernels.gemm_nt_int8_dev_noalloc(a, q, s, c, m, n, k)
     assert info.value.status == 2 and "m <= 16" in str(info.value)
+
+
+def test_noalloc_calls_leave_device_memory_unchanged(kernels, oracle):
+    """The point of the entry point: after one warm-up call per kernel it uses
+    (the first launch of a kernel may load its code), further calls of any size
+    within the limits leave the device's free memory exactly as it was, and
+    vmlm_sync (which reads the array's own error word) reports no error."""
+    import torch
+    shapes = [(1, 5760, 2304), (16, 2304, 2304), (3, 300, 7), (8, 40000, 4096)]
+    bufs = []
+    for i, (m, n, k) in enumerate(shapes):
+        x = torch.from_numpy(oracle.fill_normal(m * k, 200 + i, 1.0).reshape(m, k)).cuda()
+        q, s = oracle.quant_int8(oracle.fill_normal(n * k, 210 + i, 0.02).reshape(n, k))
+        bufs.append((x, torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(),
+                     torch.empty((m, n), dtype=torch.float32, device="cuda"), m, n, k))
+    st = torch.cuda.current_stream()
+    for x, q, s, c, m, n, k in bufs[:1] + bufs[2:3]:
+        kernels.gemm_nt_int8_dev_noalloc(x, q, s, c, m, n, k, stream=st)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        for x, q, s, c, m, n, k in bufs:
+            kernels.gemm_nt_int8_dev_noalloc(x, q, s, c, m, n, k, stream=st)
+    torch.cuda.synchronize()
+    kernels.sync(st)
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    for x, q, s, c, m, n, k in bufs:
+        ref = oracle.gemm_nt_int8(x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy())
+        assert oracle.max_rel_err(c.cpu().numpy(), ref) <= TIGHT_Q8
