@@ -87,6 +87,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration section")
+    ap.add_argument("--no-variants", action="store_true", help="skip the f32 and quantisation-variant entries")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="run only this workload, --steps times (for profilers); prints device ms/step")
@@ -418,13 +419,69 @@ def cpu_baseline_c2(x_dev, w_dev, budget_s):
                       f"(ops/src/par.rs split); the Rust reference cannot be built here (no cargo)"}
 
 
-def bench_configs(K, dist, rank, world, flush, pk):
-    """Per-configuration device times: C1, C3, C4, C5, and C2 with general f32 X."""
+NT = os.cpu_count() or 1
+
+
+def cpu_time(fn, budget_s, max_runs=25):
+    """Best and median wall time of fn on the host (one untimed run first)."""
+    fn()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_runs and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return min(times), statistics.median(times), len(times)
+
+
+def cpu_legs(run, amount, unit, sample, budget_s, kind="port"):
+    """The CPU restatement of the reference kernel timed on one core (the
+    reference as shipped is single-threaded) and on every host thread (the
+    column split of ops/src/par.rs:44-62). run(nt) computes the sample; amount
+    is its algorithmic bytes (GB/s) or operations (T(FL)OP/s)."""
+    div = 1e9 if unit == "GB/s" else 1e12
+    out = {"unit": unit, "kind": kind, "threads_all": NT, "sample": sample}
+    for name, nt in (("1core", 1), ("all", NT)):
+        best, med, runs = cpu_time(lambda: run(nt), budget_s)
+        out[name] = round(amount / med / div, 4)
+        out[name + "_best"] = round(amount / best / div, 4)
+        out[name + "_runs"] = runs
+    return out
+
+
+def int8_peak_probe(K):
+    """This device's dense tensor-core rates from the library's probe
+    (back-to-back tcgen05.mma on shared-memory operands): best of 5 launches
+    of about 25 ms after one warm-up, for kind::i8 and for kind::f16 (bf16)."""
+    res = {}
+    for kind, iters in (("int8", 90000), ("bf16", 90000)):
+        K.probe_mma_peak(kind, 2000)
+        rates = [K.probe_mma_peak(kind, iters)[0] for _ in range(5)]
+        res[kind] = {"best": max(rates), "median": statistics.median(rates)}
+    return res
+
+
+def nccl_layout(gathered, m, n):
+    """[world][m][rows] from all_gather_into_tensor -> [m][n] (the padding of the last rank dropped)."""
+    world, _, rows = gathered.shape
+    return gathered.permute(1, 0, 2).reshape(m, world * rows)[:, :n]
+
+
+def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
+    """Per-configuration device times: C1, C3, C4, C5, and C2 with general f32 X.
+    Rank 0 of a 1-GPU run also times the CPU restatement of each (1 core and
+    all threads) and checks the GPU outputs against it; under torchrun the
+    sharded C4 / C5 results (fused all-gather and NCCL all-gather) are compared
+    with each other and, on sampled columns of every rank's shard, with the
+    oracle (`sharded_check`)."""
     import torch
-    from sparrow_b200.sharded import PeerOutputs, sharded_gemm_i8i8, sharded_gemm_nt_int8
+    from oracle import oracle as O
+    from sparrow_b200.sharded import PeerOutputs, shard_rows, sharded_gemm_i8i8, sharded_gemm_nt_int8
     st = torch.cuda.current_stream()
     res = {}
     hbm = pk["hbm_gbs"]
+    do_cpu = rank == 0 and world == 1
+    check = {}
 
     def q8_layer(m, n, k, seed, calls=None):
         x = gen((m, k), seed, 1.0)
@@ -441,27 +498,36 @@ def bench_configs(K, dist, rank, world, flush, pk):
                 "frac_hbm_gemm": nbytes / tg / 1e6 / hbm}
 
     # C1: single Q8 decode GEMV (13.3 MB; L2 flushed between steps)
-    step, nbytes = q8_layer(1, 5760, 2304, 0)
-    res["C1_q8_gemv_1x5760x2304"] = hbm_entry(nbytes, time_steps(step, 50, 5, flush, dist),
-                                              gemm_only(K, step, 20, flush, dist))
+    calls1 = []
+    step, nbytes = q8_layer(1, 5760, 2304, 0, calls1)
+    e = hbm_entry(nbytes, time_steps(step, 50, 5, flush, dist), gemm_only(K, step, 20, flush, dist))
+    if do_cpu:
+        x, q, s, c, m, n, k = calls1[0]
+        step()
+        torch.cuda.synchronize()
+        xn, qn, sn = x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy()
+        e["max_rel_err_vs_oracle"] = O.max_rel_err(c.cpu().numpy(), O.gemm_nt_int8(xn, qn, sn, nt=NT))
+        e["cpu"] = cpu_legs(lambda nt: O.gemm_nt_int8(xn, qn, sn, nt=nt), nbytes, "GB/s",
+                            "full C1 (1x5760x2304)", cpu_budget)
+    res["C1_q8_gemv_1x5760x2304"] = e
+    del calls1
     # C3: the per-layer Q8 set (q, k, v, o, gate, up, down). A step is the
     # seven calls back to back on one stream, as a decoder layer issues them
     # (L2 flushed once per step); the sum of the calls timed one by one, each
     # after its own flush, is reported beside it; and the seven as one batch of
     # independent calls (vmlm_gemm_nt_int8_batch_dev: one grouped launch).
-    shapes = C3_SHAPES
     for m in (1, 8, 32):
         calls = []
-        steps = [q8_layer(m, n, k, 10 * i + m, calls) for i, (n, k) in enumerate(shapes)]
+        steps = [q8_layer(m, n, k, 10 * i + m, calls) for i, (n, k) in enumerate(C3_SHAPES)]
         nbytes = sum(b for _, b in steps)
 
         def layer():
-            for s, _ in steps:
-                s()
+            for s_, _ in steps:
+                s_()
         t = time_steps(layer, 20, 3, flush, dist)
         tg = gemm_only(K, layer, 10, flush, dist) * len(steps)
         entry = hbm_entry(nbytes, t, tg)
-        entry["single_calls_us"] = sum(time_steps(s, 10, 3, flush, dist) for s, _ in steps) * 1e3
+        entry["single_calls_us"] = sum(time_steps(s_, 10, 3, flush, dist) for s_, _ in steps) * 1e3
         entry["step"] = "7 calls back to back, L2 flushed once per step"
         tb = time_steps(lambda: K.gemm_nt_int8_batch_dev(calls, stream=st), 20, 3, flush, dist)
         n0 = K.launch_count()
@@ -469,12 +535,23 @@ def bench_configs(K, dist, rank, world, flush, pk):
         entry["batch"] = {"step_us": tb * 1e3, "GBps": nbytes / tb / 1e6, "frac_hbm": nbytes / tb / 1e6 / hbm,
                           "launches": K.launch_count() - n0,
                           "step": "the 7 calls as one vmlm_gemm_nt_int8_batch_dev call, L2 flushed once per step"}
+        if do_cpu:
+            torch.cuda.synchronize()
+            host = [(x.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy(), c) for x, q, s, c, *_ in calls]
+            entry["max_rel_err_vs_oracle"] = max(O.max_rel_err(c.cpu().numpy(), O.gemm_nt_int8(xn, qn, sn, nt=NT))
+                                                 for xn, qn, sn, c in host)
+
+            def cpu_layer(nt):
+                for xn, qn, sn, _ in host:
+                    O.gemm_nt_int8(xn, qn, sn, nt=nt)
+            entry["cpu"] = cpu_legs(cpu_layer, nbytes, "GB/s", f"full C3 layer set at M={m} (7 calls)", cpu_budget)
+            del host
         res[f"C3_q8_layer_set_M{m}"] = entry
         del steps, calls
     # C4: Q8 LM head, vocab rows sharded over the ranks, all-gather of logits
     n4, k4 = 122753, 2304
-    rows = (n4 + world - 1) // world
-    r0, r1 = rank * rows, min(n4, (rank + 1) * rows)
+    r0, r1 = shard_rows(n4, world, rank) if world > 1 else (0, n4)
+    rows = r1 - r0 if world == 1 else -(-n4 // world)
     q4, s4 = quantise_rows(gen((n4, k4), 41, 0.02)[r0:r1].contiguous())
     nloc = r1 - r0
     for m in (1, 64):
@@ -486,6 +563,18 @@ def bench_configs(K, dist, rank, world, flush, pk):
         tg = gemm_only(K, step, 10, flush, dist)
         entry = hbm_entry(nbytes, t, tg)
         entry.update({"ranks": world, "frac_hbm_gemm_per_gpu": nbytes / world / tg / 1e6 / hbm})
+        if do_cpu:
+            step()
+            torch.cuda.synchronize()
+            frac = 1 if m == 1 else 16
+            ns = n4 // frac
+            xn, qn, sn = x.cpu().numpy(), q4[:ns].cpu().numpy(), s4[:ns].cpu().numpy()
+            entry["max_rel_err_vs_oracle"] = O.max_rel_err(c[:, :ns].cpu().numpy(),
+                                                           O.gemm_nt_int8(xn, qn, sn, nt=NT))
+            sb = ns * k4 + 4 * ns + 4 * m * k4 + 4 * m * ns
+            entry["cpu"] = cpu_legs(lambda nt: O.gemm_nt_int8(xn, qn, sn, nt=nt), sb, "GB/s",
+                                    f"C4 at M={m} on the first {ns} of {n4} vocab rows", cpu_budget)
+            del xn, qn, sn
         if dist:
             gathered = torch.empty((world, m, rows), dtype=torch.float32, device="cuda")
 
@@ -501,6 +590,17 @@ def bench_configs(K, dist, rank, world, flush, pk):
                 sharded_gemm_nt_int8(x, q4, s4, peers, m, n4, k4, stream=st)
             tf = time_steps(step_fused, 20, 3, flush, dist)
             entry.update({"step_fused_allgather_us": tf * 1e3, "GBps_fused_allgather": nbytes / tf / 1e6})
+            def nccl_full():
+                # the GEMM writes [m][nloc] contiguously; pad the last rank's slice to `rows` columns
+                step()
+                pad = torch.zeros((m, rows), dtype=torch.float32, device="cuda")
+                pad[:, :nloc] = c.view(-1)[:m * nloc].view(m, nloc)
+                dist.all_gather_into_tensor(gathered, pad)
+                return nccl_layout(gathered, m, n4)
+            check[f"C4_M{m}"] = sharded_parity(K, O, dist, rank, nccl_full, peers, step_fused, m,
+                                               lambda cs: O.gemm_nt_int8(x.cpu().numpy(), q4[cs].cpu().numpy(),
+                                                                         s4[cs].cpu().numpy()),
+                                               r0, nloc, exact=False)
             torch.cuda.synchronize()
             dist.barrier()
             peers.close()
@@ -509,7 +609,8 @@ def bench_configs(K, dist, rank, world, flush, pk):
     del q4, s4
     # C5: int8 x int8 FFN, W rows sharded, all-gather of the output slices
     m5, n5, k5 = 4096, 28672, 8192
-    cols = (n5 + world - 1) // world
+    r0, r1 = shard_rows(n5, world, rank) if world > 1 else (0, n5)
+    cols = r1 - r0
     g = torch.Generator(device="cuda")
     g.manual_seed(55)
     x5 = torch.randint(-127, 128, (m5, k5), generator=g, device="cuda", dtype=torch.int8)
@@ -521,12 +622,25 @@ def bench_configs(K, dist, rank, world, flush, pk):
     ops = 2.0 * m5 * n5 * k5
     t = time_steps(step, 5, 2, flush, dist)
     tg = gemm_only(K, step, 3, flush, dist)
-    int8_peak = 2.0 * pk["bf16_tflops"]
+    int8_peak = pk.get("int8_tops") or 2.0 * pk["bf16_tflops"]
     entry = {"ops": ops, "ranks": world, "step_us": t * 1e3, "gemm_us": tg * 1e3, "TOPS": ops / t / 1e9,
              "frac_int8_peak_per_gpu": ops / world / tg / 1e9 / int8_peak,
-             "int8_peak_note": f"2 x measured bf16 = {int8_peak:.0f} TOPS (spec dense int8 4500)"}
+             "int8_peak": {"TOPS": int8_peak, "source": pk.get("int8_source", "2 x measured bf16"),
+                           "spec_dense": 4500}}
+    if do_cpu:
+        step()
+        torch.cuda.synchronize()
+        rs = 16
+        xn, wn, sn = x5[:rs].cpu().numpy(), w5.cpu().numpy(), s5.cpu().numpy()
+        rc, _ = O.gemm_i8i8(xn, wn, sn, nt=NT)
+        entry["bit_exact_vs_oracle_rows"] = bool(np.array_equal(c5[:rs].cpu().numpy().view(np.uint32),
+                                                                rc.view(np.uint32)))
+        entry["cpu"] = cpu_legs(lambda nt: O.gemm_i8i8(xn, wn, sn, nt=nt, want_acc=False), 2.0 * rs * n5 * k5,
+                                "TOP/s", f"C5 on the first {rs} of {m5} X rows (exact-int oracle: the "
+                                "reference has no int8 x int8 kernel)", cpu_budget, kind="exact-int oracle")
+        del xn, wn, sn, rc
     if dist:
-        gathered = torch.empty((world, m5, cols), dtype=torch.float32, device="cuda")
+        gathered = torch.empty((world, m5, cols), dtype=torch.float32, device="cuda")  # 28672 % world == 0
 
         def step_ag():
             step()
@@ -538,7 +652,16 @@ def bench_configs(K, dist, rank, world, flush, pk):
         def step_fused():
             sharded_gemm_i8i8(x5, w5, s5, peers, m5, n5, k5, stream=st)
         tf = time_steps(step_fused, 5, 2, flush, dist)
-        entry.update({"step_fused_allgather_us": tf * 1e3, "TOPS_fused_allgather": ops / tf / 1e9})
+        entry.update({"step_fused_allgather_us": tf * 1e3, "TOPS_fused_allgather": ops / tf / 1e9,
+                      "gather_ingress_GBps_per_gpu": 4.0 * m5 * (n5 - cols) / max(tf - tg, 1e-6) / 1e6})
+        rows_s = torch.arange(0, m5, 64, device="cuda")
+        def nccl_full():
+            step_ag()
+            return nccl_layout(gathered, m5, n5)
+        check["C5"] = sharded_parity(K, O, dist, rank, nccl_full, peers, step_fused, m5,
+                                     lambda cs: O.gemm_i8i8(x5[rows_s].cpu().numpy(), w5[cs].cpu().numpy(),
+                                                            s5[cs].cpu().numpy())[0],
+                                     r0, cols, exact=True, rows=rows_s)
         torch.cuda.synchronize()
         dist.barrier()
         peers.close()
@@ -555,6 +678,60 @@ def bench_configs(K, dist, rank, world, flush, pk):
     res["C2_general_f32_activations"] = {"step_us": t * 1e3, "gemm_us": tg * 1e3, "TFLOPS": FLOP_C2 / t / 1e9,
                                          "note": "3 bf16 split terms of X active: 3x tensor work"}
     del x, w
+    if variants:
+        res.update(bench_variants(K, dist, rank, world, flush, pk))
+    return res, check
+
+
+def sharded_parity(K, O, dist, rank, nccl_full, peers, step_fused, m, oracle_cols, c0, nloc, exact, rows=None):
+    """One more call of each sharded form: every rank's fused-gather C must equal
+    the NCCL-gathered [m, n] (bit for bit, or within the Q8 bound), and 256
+    sampled columns of this rank's shard must match the oracle. Max / min over
+    ranks, so rank 0 reports for all."""
+    import torch
+    ref = nccl_full()
+    torch.cuda.synchronize()
+    peers.c.fill_(float("nan"))
+    torch.cuda.synchronize()
+    dist.barrier()
+    step_fused()
+    torch.cuda.synchronize()
+    K.sync()
+    same = torch.equal(peers.c.view(torch.int32), ref.contiguous().view(torch.int32))
+    denom = ref.abs().max().clamp_min(1e-30)
+    diff = ((peers.c - ref).abs().max() / denom).nan_to_num(nan=float("inf")).item()
+    g = torch.Generator()
+    g.manual_seed(1000 + rank)
+    cols = torch.randperm(nloc, generator=g)[:256].sort().values
+    want = oracle_cols(cols.cuda())
+    got = peers.c[:, c0 + cols.cuda()]
+    if rows is not None:
+        got = got[rows]
+    got = got.cpu().numpy()
+    oerr = O.max_rel_err(got, want) if not exact else (0.0 if np.array_equal(got.view(np.uint32),
+                                                                            want.view(np.uint32)) else 1.0)
+    t = torch.tensor([diff, oerr, 0.0 if same else 1.0], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    diff, oerr, notsame = t.tolist()
+    tol = 0.0 if exact else 2e-5
+    out = {"fused_vs_nccl_bit_exact": notsame == 0.0, "fused_vs_nccl_max_rel": diff}
+    if exact:
+        out["oracle_sampled_bit_exact"] = oerr == 0.0
+    else:
+        out["oracle_sampled_max_rel"] = oerr
+    out["ok"] = bool(diff <= tol and oerr <= tol)
+    return out
+
+
+def bench_variants(K, dist, rank, world, flush, pk):
+    """The f32 GEMMs (the rest of OP_GEMM) and the quantisation variants of
+    tests/src/quant.rs, one GPU; rank 0 of a 1-GPU run also times their CPU
+    restatements."""
+    import torch
+    st = torch.cuda.current_stream()
+    res = {}
+    hbm = pk["hbm_gbs"]
+    c = torch.empty((M2, N2), dtype=torch.float32, device="cuda")
     # f32 GEMMs (gemm_nt, NN gemm) at the C2 shape, general f32 operands: six
     # bf16 term-pair passes on the tensor cores
     for name, fn, bshape in (("F32_gemm_nt_512x2304x2304", K.gemm_nt_f32_dev, (N2, K2)),
@@ -630,6 +807,73 @@ def timed_call(fn):
     return time.perf_counter() - t0
 
 
+def copy_floor(a_h, a_d, c_h, c_d, steps):
+    """Wall time of the e2e step's copies alone, on the same pinned buffers: the
+    H2D of A and the D2H of C as two cudaMemcpyAsync on one stream, then a
+    synchronize (ms, median of `steps`)."""
+    import torch
+    for _ in range(3):
+        a_d.copy_(a_h, non_blocking=True)
+        c_h.copy_(c_d, non_blocking=True)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        a_d.copy_(a_h, non_blocking=True)
+        c_h.copy_(c_d, non_blocking=True)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts) * 1e3
+
+
+def r4(v):
+    return None if v is None else round(float(v), 4)
+
+
+def make_summary(value, ms_per_step, roofline, e2e, configs, check, probe, cpu, world):
+    """Compact per-configuration record, printed as the last key of the bench
+    line: device time, the roofline fraction of each configuration's dominant
+    bound, the CPU restatement on 1 core and on all threads, and the parity
+    checks made in this run."""
+    s = {"C2_headline": {"us": r4(ms_per_step * 1e3), "TFLOPS": r4(value / world), "gemm_frac": r4(roofline["frac"]),
+                         "e2e_us": r4(e2e["ms_per_step"] * 1e3), "copy_floor_us": r4(e2e.get("copy_floor_ms", 0) * 1e3),
+                         "cpu_all_TFLOPS": r4(cpu["value"]) if cpu else None}}
+    if probe:
+        s["peaks_probe"] = {"int8_TOPS": r4(probe["int8"]["best"]), "bf16_TFLOPS": r4(probe["bf16"]["best"])}
+    if not configs:
+        return s
+    for key, short in (("C1_q8_gemv_1x5760x2304", "C1"),):
+        e = configs[key]
+        s[short] = {"us": r4(e["step_us"]), "gemm_us": r4(e["gemm_us"]), "frac_hbm": r4(e["frac_hbm_gemm"]),
+                    "err": r4(e.get("max_rel_err_vs_oracle")),
+                    "cpu1_GBps": r4(e.get("cpu", {}).get("1core")), "cpuN_GBps": r4(e.get("cpu", {}).get("all"))}
+    for m in (1, 8, 32):
+        e = configs[f"C3_q8_layer_set_M{m}"]
+        s[f"C3_M{m}"] = {"calls_us": r4(e["step_us"]), "batch_us": r4(e["batch"]["step_us"]),
+                         "frac_hbm_batch": r4(e["batch"]["frac_hbm"]), "err": r4(e.get("max_rel_err_vs_oracle")),
+                         "cpu1_GBps": r4(e.get("cpu", {}).get("1core")),
+                         "cpuN_GBps": r4(e.get("cpu", {}).get("all"))}
+    for m in (1, 64):
+        e = configs[f"C4_q8_lm_head_M{m}"]
+        d = {"us": r4(e["step_us"]), "gemm_us": r4(e["gemm_us"]), "frac_hbm_per_gpu": r4(e["frac_hbm_gemm_per_gpu"]),
+             "err": r4(e.get("max_rel_err_vs_oracle")), "cpu1_GBps": r4(e.get("cpu", {}).get("1core")),
+             "cpuN_GBps": r4(e.get("cpu", {}).get("all"))}
+        if "step_fused_allgather_us" in e:
+            d.update({"fused_gather_us": r4(e["step_fused_allgather_us"]), "nccl_gather_us": r4(e["step_allgather_us"])})
+        s[f"C4_M{m}"] = d
+    e = configs["C5_i8i8_ffn_4096x28672x8192"]
+    d = {"us": r4(e["step_us"]), "gemm_us": r4(e["gemm_us"]), "frac_int8": r4(e["frac_int8_peak_per_gpu"]),
+         "int8_peak_TOPS": r4(e["int8_peak"]["TOPS"]), "bit_exact_rows": e.get("bit_exact_vs_oracle_rows"),
+         "cpu1_TOPS": r4(e.get("cpu", {}).get("1core")), "cpuN_TOPS": r4(e.get("cpu", {}).get("all"))}
+    if "step_fused_allgather_us" in e:
+        d.update({"fused_gather_us": r4(e["step_fused_allgather_us"]), "nccl_gather_us": r4(e["step_allgather_us"]),
+                  "ingress_GBps": r4(e["gather_ingress_GBps_per_gpu"])})
+    s["C5"] = d
+    if check:
+        s["sharded_check"] = dict(check, all_ok=all(v["ok"] for v in check.values()))
+    return s
+
+
 def run_ours(args):
     import torch
     import sparrow_b200.kernels as K
@@ -701,15 +945,24 @@ def run_ours(args):
         K.gemm_nt_bf16(a_np, w_h, c_np, M2, N2, K2)
         e2e_t.append(time.perf_counter() - t0)
     K.unregister_all()
-    e2e_s = max_over_ranks(dist, sum(e2e_t) / len(e2e_t))
+    e2e_s = max_over_ranks(dist, statistics.median(e2e_t))
+    floor_ms = max_over_ranks(dist, copy_floor(a_h, torch.empty_like(x), c_h, c, max(args.steps, 20)))
     e2e = {"value": world * FLOP_C2 / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M2 * K2 * 4,
            "d2h_bytes_per_step": M2 * N2 * 4, "ms_per_step": e2e_s * 1e3,
-           "api": "vmlm_gemm_nt_bf16 (host pointers, synchronous; weights registered once)"}
+           "copy_floor_ms": floor_ms, "device_step_ms": ms_per_step,
+           "ratio_to_copy_floor_plus_device": e2e_s * 1e3 / (floor_ms + ms_per_step),
+           "api": "vmlm_gemm_nt_bf16 (host pointers, synchronous; weights registered once); median step; "
+                  "copy_floor_ms = pinned H2D of A + D2H of C alone (cudaMemcpyAsync on one stream)"}
     ok = bool(np.array_equal(c_np.view(np.uint32), c.cpu().numpy().view(np.uint32)))
 
-    configs = None
+    probe = int8_peak_probe(K)
+    pk["int8_tops"] = probe["int8"]["best"]
+    pk["int8_source"] = "this run's tcgen05 kind::i8 probe (vmlm_probe_mma_peak), best of 5"
+
+    configs, check = None, None
     if not args.no_configs:
-        configs = bench_configs(K, dist, rank, world, flush, pk)
+        configs, check = bench_configs(K, dist, rank, world, flush, pk, args.cpu_seconds / 4,
+                                       variants=world == 1 and not args.no_variants)
     clocks.on = False
     clocks.stop()
 
@@ -717,6 +970,7 @@ def run_ours(args):
     if rank == 0 and world == 1:
         cpu = cpu_baseline_c2(x, w, args.cpu_seconds)
 
+    summary = make_summary(value, ms_per_step, roofline, e2e, configs, check, probe, cpu, world)
     out = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16",
@@ -725,7 +979,7 @@ def run_ours(args):
                       "k": K2, "parallelism": f"replicas x{world}",
                       "l2": "flushed before every timed step (256 MiB write, outside the events)"},
            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "e2e_matches_device_path": ok,
-           "gpu_launches": launches, "clocks": clocks.summary(), "configs": configs}
+           "gpu_launches": launches, "clocks": clocks.summary(), "configs": configs, "summary": summary}
     if rank == 0:
         print(json.dumps(out), flush=True)
     if dist:

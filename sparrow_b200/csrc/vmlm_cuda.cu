@@ -16,6 +16,7 @@
 
 #include "../../include/vmlm_cuda.h"
 #include "prep.cuh"
+#include "probe.cuh"
 #include "decode.cuh"
 #include "decode_sk.cuh"
 #include "tc2_gemm.cuh"
@@ -2486,6 +2487,36 @@ int vmlm_sharded_gemm_i8i8_dev(const int8_t* x, const int8_t* w_shard, const flo
   VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, st, &sh, &nloc));
   return run_i8i8(ctx, x, w_shard, scale_shard, nullptr, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                   static_cast<int>(k), st, &sh);
+}
+
+int vmlm_probe_mma_peak(int kind, int iters, double* tops, double* ms) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (kind != 0 && kind != 1) return fail(VMLM_ERR_ARG, "probe_mma_peak: kind must be 0 (bf16) or 1 (int8)");
+  if (iters < 1 || iters > kProbeMaxIters)
+    return fail(VMLM_ERR_ARG, "probe_mma_peak: iters must be in [1, %d]", kProbeMaxIters);
+  Ctx* ctx = nullptr;
+  VMLM_TRY(current_ctx(&ctx));
+  auto kern = kind == 0 ? mma_peak_kernel<0> : mma_peak_kernel<1>;
+  VMLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem));
+  cudaEvent_t e0, e1;
+  VMLM_CUDA(cudaEventCreate(&e0));
+  VMLM_CUDA(cudaEventCreate(&e1));
+  cudaEventRecord(e0, ctx->stream);
+  const int rc = launch(kern, dim3(static_cast<unsigned>(ctx->sms)), dim3(kProbeThreads), kProbeSmem, ctx->stream,
+                        false, iters, ctx->err);
+  cudaEventRecord(e1, ctx->stream);
+  const cudaError_t se = cudaEventSynchronize(e1);
+  float t = 0.f;
+  cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  VMLM_TRY(rc);
+  if (se != cudaSuccess) return fail(VMLM_ERR_CUDA, "probe_mma_peak: %s", cudaGetErrorString(se));
+  VMLM_TRY(vmlm_sync(nullptr));
+  const double ops = static_cast<double>(ctx->sms) * iters * 4.0 * 2.0 * 128.0 * 256.0 * (kind == 0 ? 16.0 : 32.0);
+  if (ms) *ms = t;
+  if (tops) *tops = t > 0.f ? ops / (t * 1e-3) / 1e12 : 0.0;
+  return VMLM_OK;
 }
 
 int vmlm_set_host_pipeline(int max_chunks) {

@@ -97,6 +97,16 @@ def launch_count() -> int:
     return int(lib().vmlm_launch_count())
 
 
+def probe_mma_peak(kind: str, iters: int):
+    """Dense tensor-core rate of the current device from back-to-back tcgen05.mma
+    on shared-memory operands: kind "bf16" (kind::f16) or "int8" (kind::i8).
+    Returns (TFLOP/s or TOP/s, kernel ms)."""
+    code = {"bf16": 0, "int8": 1}[kind]
+    tops, ms = ctypes.c_double(), ctypes.c_double()
+    check(lib().vmlm_probe_mma_peak(code, int(iters), ctypes.byref(tops), ctypes.byref(ms)))
+    return tops.value, ms.value
+
+
 def profile_enable(on: bool) -> None:
     """Bracket each tensor-core GEMM launch with CUDA events (diagnostics)."""
     check(lib().vmlm_profile_enable(1 if on else 0))
