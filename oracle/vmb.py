@@ -11,6 +11,9 @@ constant pool (vmlm_pool_*). Nothing in the product library imports it.
   layerb         the OP_LAYERB base update (core/src/interp.rs:1019-1045)
   const_offset   const_ptr / const_ptr_based (:438-479): the layer base on a
                  CONSTANT slot and its bound
+  audit          audit_const_dtypes (:241-345): the load-time check that a
+                 non-f32 constant is read only as a GEMM B operand (or as a
+                 bf16 EMB table with an f32 destination)
 """
 import struct
 
@@ -87,3 +90,44 @@ def const_offset(parsed, slot: int, base: int) -> int:
     if off + base + rows * cols * DTYPE_SIZE[dt] > parsed["header"]["const_len"]:
         raise VmExit(9, "layer base walks past the constant pool")
     return off + base
+
+
+# opcodes (trans/src/opcode.rs:6-94) and dtypes (core/src/format.rs:73-79) the audit names
+OP_SLICE, OP_GEMM, OP_EMB, OP_SHAPE, OP_WRITECOL, OP_PUSH, OP_POP, OP_LOOP_CNT = 6, 10, 14, 52, 71, 86, 87, 89
+DT_F32, DT_I8, DT_BF16 = 0, 2, 4
+
+
+def audit(image: bytes, parsed) -> None:
+    """audit_const_dtypes (core/src/interp.rs:241-345) over the TEXT section:
+    raises VmExit(9, message) where the VM prints and exits 9. Slot numbers
+    past the table count as f32 (the VM's probe skips them)."""
+    hdr, slots = parsed["header"], parsed["slots"]
+
+    def dtype(s):
+        return slots[s][5] if s < len(slots) else DT_F32
+
+    for i in range(hdr["text_len"] // 16):
+        op, _fl, _dt, dst, a, b = struct.unpack_from("<BBHIII", image, hdr["text_off"] + 16 * i)
+        if op == OP_GEMM:
+            if dtype(b) in (DT_BF16, DT_I8, DT_F32):
+                continue
+            raise VmExit(9, "gemm B has no kernel for this dtype")
+        if op == OP_EMB:
+            if dtype(a) != DT_BF16:
+                continue
+            if dtype(dst) == DT_F32:
+                continue
+        if op == OP_SHAPE:
+            checks = (False, False, False)
+        elif op == OP_LOOP_CNT:
+            checks = (False, True, False)
+        else:
+            checks = (True, True, op not in (OP_SLICE, OP_WRITECOL, OP_PUSH, OP_POP))
+        for field, check in zip((dst, a, b), checks):
+            if not check or field >= len(slots):
+                continue
+            dt = slots[field][5]
+            if dt == DT_F32:
+                continue
+            what = {DT_BF16: "bf16", DT_I8: "i8"}.get(dt, "non-f32")
+            raise VmExit(9, f"op {op} uses {what} const at slot {field} (only a GEMM may read a non-f32 operand)")

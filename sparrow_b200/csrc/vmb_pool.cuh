@@ -5,6 +5,7 @@
 #pragma once
 #include <cstdint>
 #include <cstring>
+#include <string>
 #include <vector>
 
 namespace vmlm {
@@ -17,6 +18,10 @@ constexpr size_t kVmbSlotEnt = 16;           // SLOT_ENT: kind, idx_or_off, rows
 constexpr size_t kVmbInsSize = 16;           // INS_SIZE: op u8, fl u8, dt u16, dst, a, b
 constexpr uint32_t kVmbSlotConst = 0, kVmbSlotAct = 1, kVmbSlotState = 2, kVmbSlotGrad = 3, kVmbSlotParam = 4;
 constexpr uint8_t kVmbOpGemm = 10;           // trans/src/opcode.rs OP_GEMM
+// Opcodes whose fields the load-time dtype audit treats specially (trans/src/opcode.rs:11, 17, 50, 65, 81, 82, 94)
+constexpr uint8_t kVmbOpSlice = 6, kVmbOpEmb = 14, kVmbOpShape = 52, kVmbOpWritecol = 71, kVmbOpPush = 86,
+                  kVmbOpPop = 87, kVmbOpLoopCnt = 89;
+constexpr uint8_t kVmbDtF32 = 0, kVmbDtI8 = 2, kVmbDtBf16 = 4;
 constexpr size_t kVmbRegionPad = 64;         // Vm::load allocates every scratch region with 64 bytes of slack
 
 // format.rs dtype_size: bytes per element, 0 for an unknown dtype.
@@ -147,6 +152,55 @@ inline uint64_t vmb_layerb(uint64_t base, float d) {
   }
   const uint64_t back = to_u(-d);
   return base > back ? base - back : 0;
+}
+
+// The load-time dtype audit of Vm::load (audit_const_dtypes, core/src/interp.rs:241-345): a non-f32
+// constant may be read only as the B operand of OP_GEMM (bf16 or i8; any other non-f32 B has no kernel) or
+// as the bf16 table of OP_EMB with an f32 destination; every other instruction field that names a slot must
+// name an f32 one. Fields that hold numbers rather than slots are not checked: SHAPE (all), LOOP_CNT's dst
+// and b, the b of SLICE / WRITECOL / PUSH / POP. Slot numbers past the table are skipped, as the VM's probe
+// skips them (the VM's GEMM / EMB arms would read past the table there). Returns 0, or 8 with the VM's
+// message (it prints it and exits 9).
+inline int vmb_audit(const uint8_t* b, const VmbLayout& L, std::string* msg) {
+  const size_t n_ins = L.text_len / kVmbInsSize;
+  const size_t n_slots = L.slots.size();
+  auto dtype = [&](uint32_t s) { return s < n_slots ? L.slots[s].dtype : kVmbDtF32; };
+  for (size_t i = 0; i < n_ins; ++i) {
+    const uint8_t* ins = b + L.text_off + i * kVmbInsSize;
+    const uint8_t op = ins[0];
+    const uint32_t dst = vmb_u32(ins + 4), a = vmb_u32(ins + 8), bb = vmb_u32(ins + 12);
+    if (op == kVmbOpGemm) {
+      const uint8_t bdt = dtype(bb);
+      if (bdt == kVmbDtBf16 || bdt == kVmbDtI8 || bdt == kVmbDtF32) continue;
+      *msg = "gemm B has no kernel for this dtype";
+      return 8;
+    }
+    if (op == kVmbOpEmb) {
+      if (dtype(a) != kVmbDtBf16) continue;
+      if (dtype(dst) == kVmbDtF32) continue;
+    }
+    bool cd = true, ca = true, cb = true;
+    if (op == kVmbOpShape) {
+      cd = ca = cb = false;
+    } else if (op == kVmbOpLoopCnt) {
+      cd = cb = false;
+    } else if (op == kVmbOpSlice || op == kVmbOpWritecol || op == kVmbOpPush || op == kVmbOpPop) {
+      cb = false;
+    }
+    const uint32_t fields[3] = {dst, a, bb};
+    const bool check[3] = {cd, ca, cb};
+    for (int f = 0; f < 3; ++f) {
+      if (!check[f] || fields[f] >= n_slots) continue;
+      const uint8_t dt = L.slots[fields[f]].dtype;
+      if (dt == kVmbDtF32) continue;
+      const char* what = dt == kVmbDtBf16 ? " uses bf16 const at slot " : dt == kVmbDtI8 ? " uses i8 const at slot "
+                                                                                         : " uses non-f32 const at slot ";
+      *msg = "op " + std::to_string(op) + what + std::to_string(fields[f]) +
+             " (only a GEMM may read a non-f32 operand)";
+      return 8;
+    }
+  }
+  return 0;
 }
 
 }  // namespace vmlm

@@ -1676,6 +1676,8 @@ int vmlm_pool_load(const void* vmb, size_t len, const void* weights, size_t weig
   const char* msg = "";
   const int rc = vmlm::vmb_parse(static_cast<const uint8_t*>(vmb), len, weights != nullptr, weights_len, &L, &msg);
   if (rc) return fail(rc, "%s", msg);
+  std::string audit;
+  if (vmlm::vmb_audit(static_cast<const uint8_t*>(vmb), L, &audit)) return fail(VMLM_ERR_OPERATOR, "%s", audit.c_str());
   Ctx* ctx = nullptr;
   VMLM_TRY(current_ctx(&ctx));
   vmlm_pool* p = new vmlm_pool();

@@ -91,6 +91,54 @@ def test_pool_load_slot_past_the_pool():
     assert e.value.status == SHAPE
 
 
+def test_audit_passes_the_reference_program():
+    img = _tiny()
+    vmb.audit(img, vmb.parse(img))  # the reference's own program loads in the VM
+
+
+OP_COPY, OP_EWADD = 3, 4  # any instruction other than the special cases reads its slots as f32
+
+
+def _audit_image(text, dt_w=4):
+    """Slots: 0 activation [2,4], 1 constant W [4,4] of dtype dt_w, 2 activation [2,4], 3 f32 constant."""
+    w = np.zeros((4, 4), np.uint16 if dt_w in (1, 4) else np.int8 if dt_w == 2 else np.float32)
+    return build([("W", w, dt_w), ("F", np.zeros((4, 4), np.float32), 0)],
+                 [("x", vmb.SLOT_ACT, 0, 2, 4), ("W", vmb.SLOT_CONST, 0, 4, 4), ("y", vmb.SLOT_ACT, 64, 2, 4),
+                  ("F", vmb.SLOT_CONST, 1, 4, 4)], text=text, act_bytes=128)
+
+
+@pytest.mark.parametrize("text,dt_w,msg", [
+    (ins(OP_COPY, dst=2, a=1), 4, "op 3 uses bf16 const at slot 1 (only a GEMM may read a non-f32 operand)"),
+    (ins(OP_EWADD, dst=2, a=0, b=1), 2, "op 4 uses i8 const at slot 1 (only a GEMM may read a non-f32 operand)"),
+    (ins(OP_COPY, dst=1, a=0), 1, "op 3 uses non-f32 const at slot 1 (only a GEMM may read a non-f32 operand)"),
+    (ins(OP_GEMM, dst=2, a=0, b=1), 1, "gemm B has no kernel for this dtype"),
+    (ins(vmb.OP_EMB, dst=1, a=1, b=0), 4, "op 14 uses bf16 const at slot 1"),
+])
+def test_audit_rejects_non_f32_constants_outside_gemm(text, dt_w, msg):
+    img = _audit_image(text, dt_w)
+    with pytest.raises(vmb.VmExit) as ve:
+        vmb.audit(img, vmb.parse(img))
+    assert ve.value.code == 9 and msg in ve.value.msg
+    with pytest.raises(VmlmError) as e:
+        K.Pool(img)  # rejected before any device work
+    assert e.value.status == OPERATOR and msg in str(e.value)
+
+
+@pytest.mark.parametrize("text,dt_w", [
+    (ins(OP_GEMM, dst=2, a=0, b=1), 4),                     # bf16 B operand
+    (ins(OP_GEMM, dst=2, a=0, b=1, dt=3), 2),               # i8 B operand, scale slot in dt
+    (ins(vmb.OP_EMB, dst=2, a=1, b=0), 4),                  # bf16 table, f32 destination
+    (ins(vmb.OP_SHAPE, dst=1, a=1, b=1), 4),                # SHAPE fields are numbers
+    (ins(vmb.OP_SLICE, dst=2, a=0, b=1), 4),                # SLICE b is a column offset
+    (ins(vmb.OP_LOOP_CNT, dst=1, a=0, b=1), 2),             # LOOP_CNT: only a is a slot
+    (ins(OP_COPY, dst=2, a=3), 4),                          # f32 constants are fine anywhere
+    (ins(OP_COPY, dst=2, a=99), 4),                         # slot numbers past the table are skipped
+])
+def test_audit_accepts_what_the_vm_accepts(text, dt_w):
+    img = _audit_image(text, dt_w)
+    vmb.audit(img, vmb.parse(img))
+
+
 # --------------------------------------------------------------------- GPU
 
 def _d2h(addr, nbytes):
