@@ -1065,4 +1065,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Row-sharded calls gathered by copy engines: a peer's count, added once this
+// rank's copies into the peer's C are done (the kernel follows them on the
+// copy stream), and the bounded wait for every rank's count of a call.
+__global__ void peer_signal_kernel(unsigned* inbox) {
+  if (threadIdx.x == 0) {
+    fence_sc_sys();
+    red_add_release_sys(inbox, 1u);
+  }
+}
+
+__global__ void peer_wait_kernel(const unsigned* inbox, unsigned target, int* err) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long t0 = globaltimer();
+  while (static_cast<int>(ld_acquire_sys(inbox) - target) < 0) {
+    if (globaltimer() - t0 > kPeerWaitLimitNs) {
+      atomicCAS(err, 0, kDevTimeoutPeers);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 }  // namespace vmlm

@@ -99,6 +99,9 @@ int ensure_zeroed(DevBuf& b, size_t bytes, cudaStream_t st) {
   return VMLM_OK;
 }
 
+constexpr int kCeMaxChunks = 8;           // GEMM row chunks of a copy-engine-gathered sharded call
+constexpr double kCeMinPeerBytes = 16e6;  // peer bytes per call from which the copy engines carry the gather
+
 struct Ctx {
   int dev = -1;
   int sms = 0;
@@ -130,6 +133,11 @@ struct Ctx {
   // host-pointer calls pipelined by row chunks: copies in and out on streams of
   // their own, ordered against the compute stream by events
   cudaStream_t s_in = nullptr, s_out = nullptr;
+  // row-sharded calls gathered by copy engines: one stream per peer, events
+  // for the chunks of the GEMM and for each peer stream's last copy
+  cudaStream_t peer_st[kMaxPeers] = {};
+  cudaEvent_t chunk_ev[kCeMaxChunks] = {};
+  cudaEvent_t peer_done[kMaxPeers] = {};
   std::vector<cudaEvent_t> pipe_ev;
   bool attrs_set = false;
   std::map<std::pair<int, uint32_t>, int> dec_clusters;  // (cluster size, smem) -> co-resident clusters
@@ -1294,10 +1302,12 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
 
 // ---------------------------------------------------------- int8 x int8
 
+// ldo > 0: C rows are ldo elements apart (a column slice of a wider C); else N.
 int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float* out, int32_t* acc, int M, int N,
-             int K, cudaStream_t st, const Shard* sh = nullptr) {
+             int K, cudaStream_t st, const Shard* sh = nullptr, long long ldo = 0) {
   const bool tc_ok = K > 0 && K % 16 == 0 && aligned16(x) && aligned16(w);
   if (!tc_ok) {
+    if (ldo > 0 && ldo != N) return fail(VMLM_ERR_SHAPE, "gemm_i8i8: strided output needs the tensor-core path");
     const long long warps = static_cast<long long>(M) * N;
     return launch(i8i8_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, false,
                   x, w, scale, out, acc, M, N, K);
@@ -1316,8 +1326,8 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   p.a_box_elems = 128;
   p.out = out;
   p.acc_out = acc;
-  p.ldo = N;
-  p.vec_out = (N % 4 == 0) && (!out || aligned16(out)) && (!acc || aligned16(acc));
+  p.ldo = ldo > 0 ? ldo : N;
+  p.vec_out = (N % 4 == 0) && (p.ldo % 4 == 0) && (!out || aligned16(out)) && (!acc || aligned16(acc));
   p.scale = scale;
   p.n_tokens = M;
   CUtensorMap ma, mb;
@@ -1333,6 +1343,56 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, p.bn));
   if (sh) apply_shard(p, *sh);
   return run_tc<TcMode::kI8Norm>(c, st, ma, mb, p, false, false, plan.split);
+}
+
+// Row-sharded int8 x int8 call whose all-gather is carried by the copy
+// engines: the GEMM runs in row chunks on `st`, each chunk written into this
+// rank's own C (its column slice); after each chunk, one copy stream per peer
+// copies that slice block into the peer's C (2-D copies over NVLink), so the
+// transfer of chunk i overlaps the GEMM of chunk i + 1. When a peer stream's
+// copies are done it adds 1 to that peer's inbox; this rank's stream then
+// waits (bounded) until its own inbox holds every rank's count for the call,
+// and for its own outgoing copies. Used when the gather dominates (large
+// outputs), where SM stores to peers run below the copy engines' rate.
+int run_sharded_ce_i8i8(Ctx* ctx, const int8_t* x, const int8_t* w, const float* scale, const Shard& sh, int M,
+                        int nloc, int K, cudaStream_t st) {
+  const int world = sh.world, rank = sh.rank;
+  float* own = sh.out[rank] + sh.col_off;
+  const long long n = sh.n_total;
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    if (!ctx->peer_st[q]) VMLM_CUDA(cudaStreamCreateWithFlags(&ctx->peer_st[q], cudaStreamNonBlocking));
+    if (!ctx->peer_done[q]) VMLM_CUDA(cudaEventCreateWithFlags(&ctx->peer_done[q], cudaEventDisableTiming));
+  }
+  for (cudaEvent_t& e : ctx->chunk_ev)
+    if (!e) VMLM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  // chunks of whole 256-row pair tiles: more of them the more the transfer
+  // outweighs the GEMM (it grows with world - 1 against the GEMM's 1 / world)
+  const int unit = 2 * kTileRows;
+  const int want = std::min(kCeMaxChunks, 2 * world);
+  const int chunks = static_cast<int>(std::max(1ll, std::min<long long>(want, M / unit)));
+  const int per = static_cast<int>(cdiv(cdiv(M, chunks), unit) * unit);
+  for (int r0 = 0, ch = 0; r0 < M; r0 += per, ++ch) {
+    const int rows = std::min(per, M - r0);
+    VMLM_TRY(run_i8i8(ctx, x + static_cast<long long>(r0) * K, w, scale, own + r0 * n, nullptr, rows, nloc, K, st,
+                      nullptr, n));
+    VMLM_CUDA(cudaEventRecord(ctx->chunk_ev[ch], st));
+    for (int q = 0; q < world; ++q) {
+      if (q == rank) continue;
+      VMLM_CUDA(cudaStreamWaitEvent(ctx->peer_st[q], ctx->chunk_ev[ch], 0));
+      VMLM_CUDA(cudaMemcpy2DAsync(sh.out[q] + sh.col_off + r0 * n, n * 4, own + r0 * n, n * 4,
+                                  static_cast<size_t>(nloc) * 4, rows, cudaMemcpyDeviceToDevice, ctx->peer_st[q]));
+    }
+  }
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, ctx->peer_st[q], false, sh.inbox[q]));
+    VMLM_CUDA(cudaEventRecord(ctx->peer_done[q], ctx->peer_st[q]));
+    VMLM_CUDA(cudaStreamWaitEvent(st, ctx->peer_done[q], 0));
+  }
+  VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, st, false, sh.inbox[rank]));
+  return launch(peer_wait_kernel, dim3(1), dim3(32), 0, st, false, static_cast<const unsigned*>(sh.inbox[rank]),
+                sh.target, ctx->err);
 }
 
 // ------------------------------------------------------------ host API
@@ -1843,6 +1903,12 @@ int vmlm_shutdown(void) {
     for (cudaEvent_t e : c->pipe_ev) cudaEventDestroy(e);
     if (c->s_in) cudaStreamDestroy(c->s_in);
     if (c->s_out) cudaStreamDestroy(c->s_out);
+    for (int q = 0; q < kMaxPeers; ++q) {
+      if (c->peer_st[q]) cudaStreamDestroy(c->peer_st[q]);
+      if (c->peer_done[q]) cudaEventDestroy(c->peer_done[q]);
+    }
+    for (cudaEvent_t e : c->chunk_ev)
+      if (e) cudaEventDestroy(e);
     cudaStreamDestroy(c->stream);
     delete c;
   }
@@ -2487,6 +2553,11 @@ int vmlm_sharded_gemm_i8i8_dev(const int8_t* x, const int8_t* w_shard, const flo
   size_t nloc = 0;
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, st, &sh, &nloc));
+  // large outputs: the copy engines carry the gather, the GEMM in row chunks overlapping it
+  const double peer_bytes = 4.0 * m * nloc * (world - 1);
+  if (world > 1 && peer_bytes >= kCeMinPeerBytes && m >= 512)
+    return run_sharded_ce_i8i8(ctx, x, w_shard, scale_shard, sh, static_cast<int>(m), static_cast<int>(nloc),
+                               static_cast<int>(k), st);
   return run_i8i8(ctx, x, w_shard, scale_shard, nullptr, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                   static_cast<int>(k), st, &sh);
 }

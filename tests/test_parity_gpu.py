@@ -555,3 +555,24 @@ def _equal_share_case(kernels, oracle, m, shapes):
         assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref))
         fin = np.isfinite(ref).all(axis=1)
         assert oracle.max_rel_err(np.ascontiguousarray(got[fin]), np.ascontiguousarray(ref[fin])) <= TIGHT_Q8
+
+
+def test_q8_batch_equal_share_uneven_magnitudes_across_k(kernels, oracle):
+    """One token, a decoder layer's seven linears as one batch (equal shares per
+    CTA, each segment of a row with its own exponent): rows whose magnitudes
+    differ by 2^40 along K. A segment over the small part gets an exponent 40
+    larger; the f64 partials are then no longer on one grid and their sum may
+    round in the last bits depending on the order of the atomic adds, but the
+    result stays within the Q8 bound of the reference."""
+    import torch
+    m = 1
+    calls, host = _batch(oracle, m, C3_SHAPES, seed=77)
+    for (dx, _, _, _, _, _, k), (x, _, _) in zip(calls, host):
+        x[:, : k // 2] *= np.float32(2.0 ** -40)
+        dx.copy_(torch.from_numpy(x))
+    st = torch.cuda.current_stream()
+    kernels.gemm_nt_int8_batch_dev(calls, stream=st)
+    kernels.sync(st)
+    for (dx, dq, ds, dc, m_, n, k), (x, q, s) in zip(calls, host):
+        ref = oracle.gemm_nt_int8(x, q, s, nt=NT)
+        assert oracle.max_rel_err(dc.cpu().numpy(), ref) <= TIGHT_Q8, (n, k)
