@@ -635,7 +635,7 @@ int plan_decode(Ctx* ctx, int M, int N, int K, bool planes_mode, DecPlan* plan) 
 // planes != nullptr: planes mode (q8_planes_kernel's planes [3M][kp], exps, nonfinite).
 int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
                cudaStream_t st, const DecPlan& plan, const int8_t* planes = nullptr, int kp = 0,
-               const int* exps = nullptr, const int* nonf = nullptr) {
+               const int* exps = nullptr, const int* nonf = nullptr, long long ldo = 0) {
   DecParams p = {};
   p.n = N;
   p.k = K;
@@ -652,7 +652,7 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   p.w = q;
   p.scale = scale;
   p.out = out;
-  p.ldo = N;
+  p.ldo = ldo > 0 ? ldo : N;
   p.err = ctx->err;
   const long long grid = cdiv(N, kTileRows) * plan.c;
   p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
@@ -992,13 +992,16 @@ int shard_setup(Ctx* ctx, float* const* c_peers, unsigned* const* inbox_peers, i
 // norm_g != nullptr: C = Q8 GEMM of rmsnorm(a) (gain norm_g, norm_eps): the
 // norm is fused into the activation encoding, and everything after it reads
 // the normalised rows.
+// ldo > 0: C rows are ldo elements apart (a column slice of a wider C); else N.
 int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* out, int M, int N, int K,
-           cudaStream_t st, const Shard* sh = nullptr, const float* norm_g = nullptr, float norm_eps = 0.f) {
+           cudaStream_t st, const Shard* sh = nullptr, const float* norm_g = nullptr, float norm_eps = 0.f,
+           long long ldo = 0) {
+  const long long ldc = ldo > 0 ? ldo : N;
   const bool dec_ok = !sh && K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
   if (dec_ok && !norm_g) {
     DecPlan dp;
     VMLM_TRY(plan_decode(c, M, N, K, false, &dp));
-    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp);
+    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp, nullptr, 0, nullptr, nullptr, ldc);
   }
   const int kp = static_cast<int>(cdiv(K, 16) * 16);
   VMLM_TRY(ensure(c->act, static_cast<size_t>(3) * M * (kp ? kp : 16)));
@@ -1021,14 +1024,14 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
     // kernel on the planes just made (one wave of clusters)
     DecPlan dp;
     VMLM_TRY(plan_decode(c, M, N, K, true, &dp));
-    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp, planes, kp, exps, nonf);
+    if (dp.c > 0) return run_decode(c, a, q, scale, out, M, N, K, st, dp, planes, kp, exps, nonf, ldc);
   }
   const bool tc_ok = K > 0 && K % 16 == 0 && K <= 131072 && aligned16(q);
   if (!tc_ok) {
     const long long warps = static_cast<long long>(M) * N;
     return launch(q8_generic_kernel, dim3(static_cast<unsigned>(cdiv(warps * 32, 256))), dim3(256), 0, st, true, q,
                   scale, static_cast<const int8_t*>(planes), kp, static_cast<const int*>(exps),
-                  static_cast<const int*>(nonf), a, static_cast<long long>(K), out, static_cast<long long>(N), M, N,
+                  static_cast<const int*>(nonf), a, static_cast<long long>(K), out, ldc, M, N,
                   K);
   }
   const int tok = static_cast<int>(cdiv(M < 80 ? M : 80, 16) * 16);
@@ -1043,7 +1046,7 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   p.tm_fastest = 0;
   p.a_box_elems = 128;
   p.out = out;
-  p.ldo = N;
+  p.ldo = ldc;
   p.vec_out = 0;
   p.scale = scale;
   p.exps = exps;
@@ -1389,6 +1392,37 @@ int run_sharded_ce_i8i8(Ctx* ctx, const int8_t* x, const int8_t* w, const float*
     VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, ctx->peer_st[q], false, sh.inbox[q]));
     VMLM_CUDA(cudaEventRecord(ctx->peer_done[q], ctx->peer_st[q]));
     VMLM_CUDA(cudaStreamWaitEvent(st, ctx->peer_done[q], 0));
+  }
+  VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, st, false, sh.inbox[rank]));
+  return launch(peer_wait_kernel, dim3(1), dim3(32), 0, st, false, static_cast<const unsigned*>(sh.inbox[rank]),
+                sh.target, ctx->err);
+}
+
+// The Q8 form of the copy-engine gather (LM head at many tokens): the whole
+// shard's GEMM into this rank's column slice of its own C, then one 2-D copy
+// per peer on that peer's copy stream, the peer's count after it, and the
+// bounded wait for every rank's count (as run_sharded_ce_i8i8).
+int run_sharded_ce_q8(Ctx* ctx, const float* a, const int8_t* q, const float* scale, const Shard& sh, int M, int nloc,
+                      int K, cudaStream_t st) {
+  const int world = sh.world, rank = sh.rank;
+  float* own = sh.out[rank] + sh.col_off;
+  const long long n = sh.n_total;
+  for (int p = 0; p < world; ++p) {
+    if (p == rank) continue;
+    if (!ctx->peer_st[p]) VMLM_CUDA(cudaStreamCreateWithFlags(&ctx->peer_st[p], cudaStreamNonBlocking));
+    if (!ctx->peer_done[p]) VMLM_CUDA(cudaEventCreateWithFlags(&ctx->peer_done[p], cudaEventDisableTiming));
+  }
+  if (!ctx->chunk_ev[0]) VMLM_CUDA(cudaEventCreateWithFlags(&ctx->chunk_ev[0], cudaEventDisableTiming));
+  VMLM_TRY(run_q8(ctx, a, q, scale, own, M, nloc, K, st, nullptr, nullptr, 0.f, n));
+  VMLM_CUDA(cudaEventRecord(ctx->chunk_ev[0], st));
+  for (int p = 0; p < world; ++p) {
+    if (p == rank) continue;
+    VMLM_CUDA(cudaStreamWaitEvent(ctx->peer_st[p], ctx->chunk_ev[0], 0));
+    VMLM_CUDA(cudaMemcpy2DAsync(sh.out[p] + sh.col_off, n * 4, own, n * 4, static_cast<size_t>(nloc) * 4, M,
+                                cudaMemcpyDeviceToDevice, ctx->peer_st[p]));
+    VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, ctx->peer_st[p], false, sh.inbox[p]));
+    VMLM_CUDA(cudaEventRecord(ctx->peer_done[p], ctx->peer_st[p]));
+    VMLM_CUDA(cudaStreamWaitEvent(st, ctx->peer_done[p], 0));
   }
   VMLM_TRY(launch(peer_signal_kernel, dim3(1), dim3(32), 0, st, false, sh.inbox[rank]));
   return launch(peer_wait_kernel, dim3(1), dim3(32), 0, st, false, static_cast<const unsigned*>(sh.inbox[rank]),
@@ -2534,6 +2568,10 @@ int vmlm_sharded_gemm_nt_int8_dev(const float* a, const int8_t* q_shard, const f
   size_t nloc = 0;
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   VMLM_TRY(shard_setup(ctx, c_peers, inbox_peers, rank, world, m, n, st, &sh, &nloc));
+  const double peer_bytes = 4.0 * m * nloc * (world - 1);
+  if (world > 1 && peer_bytes >= kCeMinPeerBytes)
+    return run_sharded_ce_q8(ctx, a, q_shard, scale_shard, sh, static_cast<int>(m), static_cast<int>(nloc),
+                             static_cast<int>(k), st);
   return run_q8(ctx, a, q_shard, scale_shard, nullptr, static_cast<int>(m), static_cast<int>(nloc),
                 static_cast<int>(k), st, &sh);
 }

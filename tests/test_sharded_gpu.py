@@ -77,8 +77,9 @@ def _two_gpu_rank(rank, world, port, errors):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         g = torch.Generator(device="cuda")
-        # Q8 LM-head shape, M = 1 and 64: full weight on every rank for the comparison
-        for m, n, k in ((1, 30011, 2304), (64, 16384, 2304)):
+        # Q8 LM-head shape, M = 1 and 64 (the all-gather in the GEMM epilogue), and one whose
+        # output per rank is large enough for the copy-engine gather: full weight on every rank
+        for m, n, k in ((1, 30011, 2304), (64, 16384, 2304), (128, 65536, 2304)):
             g.manual_seed(7 + m)
             x = torch.randn((m, k), generator=g, device="cuda")
             q = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
@@ -104,8 +105,8 @@ def _two_gpu_rank(rank, world, port, errors):
             dist.barrier()
             peers.close()
             dist.barrier()
-        # int8 x int8 FFN shapes (smaller), bit-exact: a K-split plan, and one
-        # on CTA pairs (256-row tiles over two SMs) with the peer stores
+        # int8 x int8 FFN shapes (smaller), bit-exact: a K-split plan with the peer
+        # stores, and one large enough for the copy-engine gather of a chunked GEMM
         for m, n, k in ((512, 8192, 1024), (2048, 8192, 1024)):
             g.manual_seed(99 + m)
             x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
