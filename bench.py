@@ -92,6 +92,8 @@ def parse():
     ap.add_argument("--case", choices=sorted(CASES), default=None,
                     help="run only this workload, --steps times (for profilers); prints device ms/step")
     ap.add_argument("--trace", action="store_true", help="with --case: per-CTA phase timestamps of one launch")
+    ap.add_argument("--rotate", action="store_true",
+                    help="with --case: steps back to back over input copies larger than twice L2 (no flush)")
     ap.add_argument("--warm", action="store_true",
                     help="with --trace: trace a launch that follows another without an L2 flush in between")
     return ap.parse_args()
@@ -112,45 +114,57 @@ CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf1
 
 
 def run_case(args):
-    """One workload through the device entry point, L2 flushed between steps."""
+    """One workload through the device entry point: L2 flushed between steps,
+    or (--rotate) steps back to back over input copies larger than twice L2."""
     import torch
     import sparrow_b200.kernels as K
     torch.cuda.set_device(0)
     K.init(0)
     kind, m, n, k = CASES[args.case]
     st = torch.cuda.current_stream()
-    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
-    if kind == "q8":
-        x = gen((m, k), 0, 1.0)
-        q, s = quantise_rows(gen((n, k), 1, 0.02))
-        step = lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)  # noqa: E731
-    elif kind == "q8batch":
-        # the C3 layer set (q, k, v, o, gate, up, down) as one batch of independent calls
-        calls = []
-        for i, (n_i, k_i) in enumerate(C3_SHAPES):
-            x = gen((m, k_i), 10 * i + m, 1.0)
-            q, s = quantise_rows(gen((n_i, k_i), 10 * i + 1 + m, 0.02))
-            calls.append((x, q, s, torch.empty((m, n_i), dtype=torch.float32, device="cuda"), m, n_i, k_i))
-        n, k = sum(n_i for n_i, _ in C3_SHAPES), 0
-        step = lambda: K.gemm_nt_int8_batch_dev(calls, stream=st)  # noqa: E731
-    elif kind in ("bf16", "bf16f"):
-        x = gen((m, k), 0, 1.0)
-        if kind == "bf16":
-            x = x.to(torch.bfloat16).float().contiguous()
-        w = gen((n, k), 1, 0.02).to(torch.bfloat16)
-        step = lambda: K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)  # noqa: E731
-    elif kind in ("f32nt", "f32nn"):
-        x = gen((m, k), 0, 1.0)
-        w = gen((k, n) if kind == "f32nn" else (n, k), 1, 0.02)
-        fn = K.gemm_f32_dev if kind == "f32nn" else K.gemm_nt_f32_dev
-        step = lambda: fn(x, w, c, m, n, k, stream=st)  # noqa: E731
-    else:
+
+    def make(r):
+        """The step on input copy r (r = 0: the seeds the flushed timing has always used)."""
+        c = torch.empty((m if kind != "q8batch" else 1, n if n else 1), dtype=torch.float32, device="cuda")
+        if kind == "q8":
+            x = gen((m, k), 0, 1.0)
+            q, s = quantise_rows(gen((n, k), 1 + 1000 * r, 0.02))
+            return (lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)), n * k
+        if kind == "q8batch":
+            # the C3 layer set (q, k, v, o, gate, up, down) as one batch of independent calls
+            calls = []
+            for i, (n_i, k_i) in enumerate(C3_SHAPES):
+                x = gen((m, k_i), 10 * i + m, 1.0)
+                q, s = quantise_rows(gen((n_i, k_i), 10 * i + 1 + m + 1000 * r, 0.02))
+                calls.append((x, q, s, torch.empty((m, n_i), dtype=torch.float32, device="cuda"), m, n_i, k_i))
+            return (lambda: K.gemm_nt_int8_batch_dev(calls, stream=st)), sum(a * b for a, b in C3_SHAPES)
+        if kind in ("bf16", "bf16f"):
+            x = gen((m, k), 0 + 1000 * r, 1.0)
+            if kind == "bf16":
+                x = x.to(torch.bfloat16).float().contiguous()
+            w = gen((n, k), 1 + 1000 * r, 0.02).to(torch.bfloat16)
+            return (lambda: K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)), 4 * m * k + 2 * n * k
+        if kind in ("f32nt", "f32nn"):
+            x = gen((m, k), 0 + 1000 * r, 1.0)
+            w = gen((k, n) if kind == "f32nn" else (n, k), 1 + 1000 * r, 0.02)
+            fn = K.gemm_f32_dev if kind == "f32nn" else K.gemm_nt_f32_dev
+            return (lambda: fn(x, w, c, m, n, k, stream=st)), 4 * m * k + 4 * n * k
         g = torch.Generator(device="cuda")
-        g.manual_seed(5)
+        g.manual_seed(5 + r)
         x = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
         w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
         s = gen((n,), 2, 0.02).abs() + 1e-3
-        step = lambda: K.gemm_i8i8_dev(x, w, s, c, None, m, n, k, stream=st)  # noqa: E731
+        return (lambda: K.gemm_i8i8_dev(x, w, s, c, None, m, n, k, stream=st)), m * k + n * k
+
+    step, nbytes = make(0)
+    if kind == "q8batch":
+        n, k = sum(n_i for n_i, _ in C3_SHAPES), 0
+    if args.rotate:
+        steps = [step] + [make(r)[0] for r in range(1, copies_for(nbytes))]
+        t = time_rotating(steps, args.steps, args.warmup)
+        print(json.dumps({"case": args.case, "shape": [m, n, k], "ms_per_step": t, "copies": len(steps),
+                          "timing": "steps back to back over rotating input copies"}), flush=True)
+        return
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     t = time_steps(step, args.steps, args.warmup, flush)
     out = {"case": args.case, "shape": [m, n, k], "ms_per_step": t}
@@ -469,9 +483,18 @@ def cpu_baseline_c2(x_dev, w_dev, budget_s):
         O.gemm_nt_bf16(x, w, nt=nt)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
+    # the reference as shipped is single-threaded: one core too (a few runs)
+    one = []
+    t_end = time.perf_counter() + budget_s / 4
+    while not one or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        O.gemm_nt_bf16(x, w, nt=1)
+        one.append(time.perf_counter() - t0)
     return {"value": FLOP_C2 / med / 1e12, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+            "one_core": FLOP_C2 / statistics.median(one) / 1e12,
             "sample": f"full C2 workload, {len(times)} runs (median), output columns split over {nt} threads "
-                      f"(ops/src/par.rs split); the Rust reference cannot be built here (no cargo)"}
+                      f"(ops/src/par.rs split); one_core: {len(one)} runs on one thread; the Rust reference "
+                      "cannot be built here (no cargo)"}
 
 
 NT = os.cpu_count() or 1
@@ -740,7 +763,7 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
             sharded_gemm_i8i8(x5, w5, s5, peers, m5, n5, k5, stream=st)
         tf = time_steps(step_fused, 5, 2, flush, dist)
         entry.update({"step_fused_allgather_us": tf * 1e3, "TOPS_fused_allgather": ops / tf / 1e9,
-                      "gather_ingress_GBps_per_gpu": 4.0 * m5 * (n5 - cols) / max(tf - tg, 1e-6) / 1e6})
+                      "gather_ingress_GBps_over_call": 4.0 * m5 * (n5 - cols) / tf / 1e6})
         entry["rot"].update({"allgather_us": time_rotating([step_ag], 10, 2, dist) * 1e3,
                              "fused_allgather_us": time_rotating([step_fused], 10, 2, dist) * 1e3})
         rows_s = torch.arange(0, m5, 64, device="cuda")
@@ -897,22 +920,36 @@ def timed_call(fn):
 
 
 def copy_floor(a_h, a_d, c_h, c_d, steps):
-    """Wall time of the e2e step's copies alone, on the same pinned buffers: the
-    H2D of A and the D2H of C as two cudaMemcpyAsync on one stream, then a
-    synchronize (ms, median of `steps`)."""
+    """Wall time of the e2e step's copies alone, on the same pinned buffers
+    (ms, median of `steps`): the H2D of A and the D2H of C one after the other
+    on one stream, and the two at once on two streams (the floor of a call
+    whose copies in and out overlap)."""
     import torch
-    for _ in range(3):
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def serial():
         a_d.copy_(a_h, non_blocking=True)
         c_h.copy_(c_d, non_blocking=True)
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        a_d.copy_(a_h, non_blocking=True)
-        c_h.copy_(c_d, non_blocking=True)
+
+    def duplex():
+        with torch.cuda.stream(s_in):
+            a_d.copy_(a_h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            c_h.copy_(c_d, non_blocking=True)
+
+    out = []
+    for fn in (serial, duplex):
+        for _ in range(3):
+            fn()
         torch.cuda.synchronize()
-        ts.append(time.perf_counter() - t0)
-    return statistics.median(ts) * 1e3
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        out.append(statistics.median(ts) * 1e3)
+    return out
 
 
 def r4(v):
@@ -928,7 +965,9 @@ def make_summary(value, ms_per_step, flushed_ms, roofline, e2e, configs, check, 
     s = {"C2_headline": {"us": r4(ms_per_step * 1e3), "flushed_us": r4(flushed_ms * 1e3), "TFLOPS": r4(value / world),
                          "gemm_us": r4(roofline["kernel_us"]), "gemm_frac": r4(roofline["frac"]),
                          "e2e_us": r4(e2e["ms_per_step"] * 1e3), "copy_floor_us": r4(e2e.get("copy_floor_ms", 0) * 1e3),
-                         "cpu_all_TFLOPS": r4(cpu["value"]) if cpu else None}}
+                         "copy_duplex_us": r4(e2e.get("copy_floor_duplex_ms", 0) * 1e3),
+                         "cpu_all_TFLOPS": r4(cpu["value"]) if cpu else None,
+                         "cpu1_TFLOPS": r4(cpu["one_core"]) if cpu else None}}
     if probe:
         s["peaks_probe"] = {"int8_TOPS": r4(probe["int8"]["best"]), "bf16_TFLOPS": r4(probe["bf16"]["best"])}
     if not configs:
@@ -958,9 +997,10 @@ def make_summary(value, ms_per_step, flushed_ms, roofline, e2e, configs, check, 
          "frac_int8": r4(e["rot"]["frac_int8_peak_per_gpu"]), "int8_peak_TOPS": r4(e["int8_peak"]["TOPS"]),
          "flushed_us": r4(e["step_us"]), "bit_exact_rows": e.get("bit_exact_vs_oracle_rows"), **cpu_of(e, "TOPS")}
     if "fused_allgather_us" in e["rot"]:
+        # bytes each GPU receives from its peers, over the whole sharded call
         d.update({"fused_gather_us": r4(e["rot"]["fused_allgather_us"]), "nccl_gather_us": r4(e["rot"]["allgather_us"]),
-                  "ingress_GBps": r4(4.0 * 4096 * 28672 * (1 - 1 / world) / (e["rot"]["fused_allgather_us"] -
-                                                                           e["rot"]["gemm_us"]) / 1e3)})
+                  "ingress_GBps_over_call": r4(4.0 * 4096 * 28672 * (1 - 1 / world) / e["rot"]["fused_allgather_us"]
+                                               / 1e3)})
     s["C5"] = d
     if check:
         s["sharded_check"] = dict(check, all_ok=all(v["ok"] for v in check.values()))
@@ -1050,13 +1090,16 @@ def run_ours(args):
         e2e_t.append(time.perf_counter() - t0)
     K.unregister_all()
     e2e_s = max_over_ranks(dist, statistics.median(e2e_t))
-    floor_ms = max_over_ranks(dist, copy_floor(a_h, torch.empty_like(x), c_h, c, max(args.steps, 20)))
+    floor_ser, floor_dup = copy_floor(a_h, torch.empty_like(x), c_h, c, max(args.steps, 20))
+    floor_ms = max_over_ranks(dist, floor_ser)
+    floor_dup = max_over_ranks(dist, floor_dup)
     e2e = {"value": world * FLOP_C2 / e2e_s / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M2 * K2 * 4,
            "d2h_bytes_per_step": M2 * N2 * 4, "ms_per_step": e2e_s * 1e3,
-           "copy_floor_ms": floor_ms, "device_step_ms": ms_per_step,
+           "copy_floor_ms": floor_ms, "copy_floor_duplex_ms": floor_dup, "device_step_ms": ms_per_step,
            "ratio_to_copy_floor_plus_device": e2e_s * 1e3 / (floor_ms + ms_per_step),
            "api": "vmlm_gemm_nt_bf16 (host pointers, synchronous; weights registered once); median step; "
-                  "copy_floor_ms = pinned H2D of A + D2H of C alone (cudaMemcpyAsync on one stream)"}
+                  "copy_floor_ms = pinned H2D of A + D2H of C alone (cudaMemcpyAsync on one stream); "
+                  "copy_floor_duplex_ms = the two at once on two streams"}
     ok = bool(np.array_equal(c_np.view(np.uint32), c.cpu().numpy().view(np.uint32)))
 
     probe = int8_peak_probe(K)
