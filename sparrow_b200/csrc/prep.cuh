@@ -410,14 +410,31 @@ __device__ __forceinline__ void norm_terms_row(const float* __restrict__ xr, int
   }
 }
 
+// zc != nullptr: also zero row t of C (zn columns, row stride ldc; zvec: rows
+// 16-byte aligned), for a GEMM that adds partial sums into C.
 __global__ void __launch_bounds__(kNormPrepThreads) bf16_terms_norm_kernel(
     const float* __restrict__ x, long long ldx, int M, int K, int kp, int vec, uint16_t* __restrict__ out,
-    uint8_t* __restrict__ dirty, unsigned* __restrict__ orword, unsigned* __restrict__ orword_next) {
+    uint8_t* __restrict__ dirty, unsigned* __restrict__ orword, unsigned* __restrict__ orword_next,
+    float* __restrict__ zc, long long ldc, int zn, int zvec) {
   pdl_launch_dependents();
+  // Launched as a programmatic dependent of the previous kernel in the stream
+  // (the GEMM of the previous call lets it start early): its term buffer,
+  // flag words and C may still be in use until that kernel completes.
+  pdl_wait_prior();
   __shared__ int redi[32];
   const int t = blockIdx.x;
   if (t >= M) return;
   if (t == 0 && threadIdx.x == 0) *orword_next = 0u;
+  if (zc) {
+    float* zr = zc + static_cast<long long>(t) * ldc;
+    if (zvec) {
+      for (int j = threadIdx.x; j < zn / 4; j += kNormPrepThreads)
+        reinterpret_cast<float4*>(zr)[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = (zn / 4) * 4 + threadIdx.x; j < zn; j += kNormPrepThreads) zr[j] = 0.f;
+    } else {
+      for (int j = threadIdx.x; j < zn; j += kNormPrepThreads) zr[j] = 0.f;
+    }
+  }
   norm_terms_row<false>(x + static_cast<long long>(t) * ldx, K, kp, vec, out + static_cast<long long>(t) * 3 * kp,
                         dirty + t, nullptr, orword, redi);
 }

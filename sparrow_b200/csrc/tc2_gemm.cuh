@@ -10,6 +10,10 @@
 // each SM loads fewer operand bytes than a 128 x bn tile on one SM (B is
 // split between the two), which is what bounds these GEMMs (per-SM L2 -> SM
 // bandwidth; in swap mode the planes are re-read for every weight tile).
+// kBf16Norm calls with few tiles split K in two (p.ksplit = 2): twice the
+// pairs, half the operand bytes each, and each pair adds its partial into C
+// (zeroed by the prep kernel) with red.global.add. f32 addition commutes, so
+// the two partials give the same bits in either order.
 //
 // Warp roles as in tc_gemm_kernel (320 threads). Barriers:
 //   full[s]   even CTA only: its producer expects both CTAs' bytes; both CTAs'
@@ -111,18 +115,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Both CTAs' barriers are initialised before any remote arrival or copy.
   cluster_arrive_release();
   cluster_wait_acquire();
+  // The next kernel in the stream may be scheduled now: kernels this library
+  // launches as programmatic dependents wait for this one to complete before
+  // they touch memory it reads or writes (they only prefetch weights first).
+  pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t full_even = mapa_shared(smem_u32(full_bar), 0);
   const uint32_t tempty_even = mapa_shared(smem_u32(tempty_bar), 0);
   const int kbt = p.kb_per_term;
 
-  // Tile i of this pair (round-robin over pairs): this CTA's 128 rows of A
-  // start at a_row; tn is the column tile. Both CTAs see the same sequence.
-  auto tile_of = [&](int i, int& a_row, int& tn) -> bool {
-    const int tile = pair + i * npairs;
-    if (tile >= tiles) return false;
+  // Work item i of this pair (round-robin over pairs): this CTA's 128 rows of
+  // A start at a_row; tn is the column tile; k-blocks [kb0, kb1) of each term
+  // (the whole K, or one of p.ksplit ranges: items [r*tiles, (r+1)*tiles) take
+  // range r). Both CTAs see the same sequence.
+  const int ks = p.ksplit > 1 ? p.ksplit : 1;
+  auto tile_of = [&](int i, int& a_row, int& tn, int& kb0, int& kb1) -> bool {
+    const int item = pair + i * npairs;
+    if (item >= tiles * ks) return false;
+    const int tile = item % tiles;
+    const int r = item / tiles;
     tn = tile / p.tiles_m;
     a_row = (tile % p.tiles_m) * kPairRows + static_cast<int>(crank) * kTileRows;
+    kb0 = r * kbt / ks;
+    kb1 = (r + 1) * kbt / ks;
     return true;
   };
 
@@ -141,12 +156,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int a_row, tn;
-      for (int i = 0; ok && tile_of(i, a_row, tn); ++i) {
+      int a_row, tn, kb0, kb1;
+      for (int i = 0; ok && tile_of(i, a_row, tn, kb0, kb1); ++i) {
         const int b_row = tn * p.bn + static_cast<int>(crank) * (p.bn / 2);
-        for (int j = 0; j < T * kbt; ++j) {
-          const int term = j / kbt;
-          const int kin = j - term * kbt;
+        const int nkb = kb1 - kb0;
+        for (int j = 0; j < T * nkb; ++j) {
+          const int term = j / nkb;
+          const int kin = kb0 + (j - term * nkb);
           const unsigned long long tw = trace ? globaltimer() : 0;
           if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
             ok = false;
@@ -188,15 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true, issued = false;
       unsigned long long wait_accum = 0, wait_full = 0;  // trace: time waiting for TMEM / for stages
-      int a_row, tn;
-      for (int i = 0; ok && tile_of(i, a_row, tn); ++i) {
+      int a_row, tn, kb0, kb1;
+      for (int i = 0; ok && tile_of(i, a_row, tn, kb0, kb1); ++i) {
         const int buf = i & 1;
         const unsigned long long tw0 = trace ? globaltimer() : 0;
         if (!mbar_wait(tempty_bar + buf, ((i >> 1) & 1) ^ 1, p.err, abort_flag, kDevTimeoutAccumFree)) break;
         if (trace) wait_accum += globaltimer() - tw0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
-        for (int j = 0; j < T * kbt; ++j) {
+        for (int j = 0; j < T * (kb1 - kb0); ++j) {
           const unsigned long long tw1 = trace ? globaltimer() : 0;
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
@@ -246,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait_prior();
     unsigned long long epi_wait = 0;  // trace: time waiting for accumulators
     unsigned long long epi_ld = 0, epi_fin = 0;  // trace: time in TMEM loads / finishing and storing
-    int a_row, tn;
-    for (int i = 0; tile_of(i, a_row, tn); ++i) {
+    int a_row, tn, kb0, kb1;
+    for (int i = 0; tile_of(i, a_row, tn, kb0, kb1); ++i) {
       const int buf = i & 1;
       const int grow = a_row + row;
       float scale_n = 0.f;

@@ -94,6 +94,8 @@ struct TcParams {
   uint32_t* slots;   // swap modes: [grid] slots of [tok][128] combined values, all zero between calls
   int* counters;     // [tiles] k-blocks finished so far (self-resetting)
   int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
+  int ksplit;        // tc2_gemm_kernel, normal modes: K ranges per pair tile (1 or 2); with 2 each
+                     // range's partial is added into C (zeroed beforehand) with red.global.add
   // kF32Norm (C = A . B^T, both operands f32 split into three bf16 terms):
   // B's terms at j * term_stride along its K, B's OR word, per-row NaN/Inf
   // flags of A and B, both term buffers ([rows][3 * term_stride]) for the
@@ -259,7 +261,10 @@ __device__ __forceinline__ uint32_t term_pairs(const TcParams& p, int* np) {
 // through a per-warp shared buffer, so that each store instruction writes 8
 // rows x 64 contiguous bytes instead of 32 rows x 16 bytes.
 // kAdd: f32 values added to the destination's old values (C += ...).
-template <bool kAdd = false>
+// kRed: f32 values added to the destination in L2 (red.global.add), for
+// partial sums of one output from two CTAs; f32 addition is commutative, so
+// two partials added into a zeroed C give the same bits in either order.
+template <bool kAdd = false, bool kRed = false>
 __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, int row0, int nrows, int col0,
                                                   int ncols, bool vec, uint32_t* buf, const uint32_t (&v)[16]) {
   const int lane = threadIdx.x & 31;
@@ -276,6 +281,10 @@ __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, i
       const uint32_t* s = buf + r * 17 + c;
       if (vec && col0 + c + 4 <= ncols) {
         uint4 o = make_uint4(s[0], s[1], s[2], s[3]);
+        if constexpr (kRed) {
+          red_add_v4_f32(reinterpret_cast<float*>(d), o);
+          continue;
+        }
         if constexpr (kAdd) {
           const float4 q = *reinterpret_cast<const float4*>(d);
           o = make_uint4(__float_as_uint(__fadd_rn(__uint_as_float(o.x), q.x)),
@@ -287,7 +296,9 @@ __device__ __forceinline__ void store_block_32x16(uint32_t* dst, long long ld, i
       } else {
         for (int j = 0; j < 4; ++j)
           if (col0 + c + j < ncols) {
-            if constexpr (kAdd)
+            if constexpr (kRed)
+              red_add_f32(reinterpret_cast<float*>(d + j), __uint_as_float(s[j]));
+            else if constexpr (kAdd)
               d[j] = __float_as_uint(__fadd_rn(__uint_as_float(s[j]), __uint_as_float(d[j])));
             else
               d[j] = s[j];
@@ -397,7 +408,11 @@ __device__ __forceinline__ void epi_norm16(const TcParams& p, int row0, int col0
     else
       store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, f);
   } else if (p.npeers == 0) {
-    store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, v);
+    if (MODE == TcMode::kBf16Norm && p.ksplit > 1)
+      store_block_32x16<false, true>(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out,
+                                     buf, v);
+    else
+      store_block_32x16(reinterpret_cast<uint32_t*>(p.out), p.ldo, row0, p.rows, col0, p.cols, p.vec_out, buf, v);
   } else {
     for (int q = 0; q < p.npeers; ++q)
       store_block_32x16(reinterpret_cast<uint32_t*>(p.peer_out[q] + p.col_off), p.ldo, row0, p.rows, col0, p.cols,
@@ -569,6 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The next kernel in the stream may be scheduled now: kernels this library
+  // launches as programmatic dependents wait for this one to complete before
+  // they touch memory it reads or writes (they only prefetch weights first).
+  pdl_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
 
   const int cta = blockIdx.x;

@@ -391,7 +391,7 @@ struct NormPlan {
 };
 
 template <TcMode MODE>
-int plan_norm(Ctx* ctx, int rows, int N, int K, int esz, bool int_acc, NormPlan* out) {
+int plan_norm(Ctx* ctx, int rows, int N, int K, int esz, bool int_acc, NormPlan* out, double* t_out = nullptr) {
   const int cand[3] = {256, 128, 64};
   const double eff[3] = {1.0, 0.85, 0.5};
   const double l2_bps = 120e9;                             // per SM
@@ -424,6 +424,7 @@ int plan_norm(Ctx* ctx, int rows, int N, int K, int esz, bool int_acc, NormPlan*
     }
   }
   *out = best;
+  if (t_out) *t_out = best_t;
   return VMLM_OK;
 }
 
@@ -533,9 +534,12 @@ bool use_pairs(const NormPlan& plan, long long rows, long long cols, int sms) {
 }
 
 // p: a parameter set whose tiles_m / bn / maps the caller fills for pair
-// tiles (A box 128 rows, B box bn / 2 rows).
+// tiles (A box 128 rows, B box bn / 2 rows), and ksplit (0 or 1: whole K;
+// 2: kBf16Norm only, C zeroed before the launch).
 template <TcMode MODE>
 int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool pdl) {
+  if (p.ksplit > 1 && (MODE != TcMode::kBf16Norm || p.ksplit > 2 || p.ksplit > p.kb_per_term))
+    return fail(VMLM_ERR_SHAPE, "a K split of pair tiles takes bf16 calls, two ranges, a k-block each");
   p.stages = tc2_stages(p.bn);
   p.tmem_cols = pow2_at_least(2 * p.bn);
   p.csplit = 0;
@@ -544,7 +548,7 @@ int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& m
   int max_pairs = 0;
   VMLM_TRY(tc2_max_pairs<MODE>(c, L.total, &max_pairs));
   if (max_pairs < 1) return fail(VMLM_ERR_CUDA, "no CTA pair fits on this device");
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * (p.ksplit > 1 ? p.ksplit : 1);
   const long long pairs = tiles < max_pairs ? tiles : max_pairs;
   p.err = c->err;
   p.trace = (g_trace && g_trace_dev == c->dev && static_cast<size_t>(2 * pairs) <= g_trace_ctas) ? g_trace : nullptr;
@@ -1083,11 +1087,47 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
 struct Bf16Plan {
   NormPlan plan;
   bool pairs = false;
+  int pair_bn = kPairBn;  // pairs: tile width
+  int ksplit = 1;         // pairs: K ranges per tile (2: partials added into a zeroed C)
 };
 
+// One-CTA tiles (with a cluster K split where that fills the SMs), or 256-row
+// CTA-pair tiles, whole K or K split in two. A pair tile loads fewer operand
+// bytes per SM than one-CTA tiles of the same width (B is split between the
+// two SMs); split in two, each range adds its partial into C in L2
+// (red.global.add; the prep kernel zeroes C first). The cluster K split of
+// one-CTA tiles exchanges partials through distributed shared memory, which
+// costs several microseconds (remote stores run at about 36 GB/s per SM).
 int bf16_norm_plan(Ctx* c, int M, int N, int K, Bf16Plan* out) {
-  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &out->plan));
+  double t_norm = 0.0;
+  VMLM_TRY(plan_norm<TcMode::kBf16Norm>(c, M, N, K, 2, false, &out->plan, &t_norm));
   out->pairs = use_pairs(out->plan, M, N, c->sms);
+  out->pair_bn = kPairBn;
+  out->ksplit = 1;
+  if (out->pairs || M < 2 * kTileRows) return VMLM_OK;
+  const double l2_bps = 120e9;   // per SM, as plan_norm
+  const double red_bps = 60e9;   // per SM, partial sums added in L2
+  const double t_exchange = out->plan.split > 1 ? 3.0e-6 : 0.0;
+  double best = t_norm + t_exchange;
+  const long long kb = cdiv(K, 64);
+  const int pair_slots = c->sms / 2;
+  for (int bn : {128, 256}) {
+    for (int ks = 1; ks <= 2 && ks <= kb; ++ks) {
+      const long long items = cdiv(M, 2 * kTileRows) * cdiv(N, bn) * ks;
+      const double waves = static_cast<double>(cdiv(items, pair_slots));
+      const double kk = static_cast<double>(kb) / ks;
+      const double t_load = kk * (kTileRows + bn / 2) * kBlockBytes / l2_bps;
+      const double t_mma = static_cast<double>(kTileRows) * bn * 64 * kk / (11e12 / 2.0);
+      const double t_red = ks > 1 ? static_cast<double>(kTileRows) * bn * 4 / red_bps : 0.0;
+      const double t = waves * ((t_load > t_mma ? t_load : t_mma) + t_red);
+      if (t < best * 0.999) {
+        best = t;
+        out->pairs = true;
+        out->pair_bn = bn;
+        out->ksplit = ks;
+      }
+    }
+  }
   return VMLM_OK;
 }
 
@@ -1109,17 +1149,20 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   unsigned* orword_next = fw + 32 * (c->norm_parity ^ 1u);
   c->norm_parity ^= 1u;
   uint16_t* terms = static_cast<uint16_t*>(c->norm_terms.p);
-  VMLM_TRY(launch(bf16_terms_norm_kernel, dim3(M), dim3(kNormPrepThreads), 0, st, false, a,
-                  static_cast<long long>(K), M, K, kp, static_cast<int>((K % 4 == 0) && aligned16(a)), terms,
-                  static_cast<uint8_t*>(c->norm_dirty.p), orword, orword_next));
-  TcParams p = {};
-  p.rows = M;
-  p.cols = N;
   Bf16Plan bp;
   if (force)
     bp = *force;
   else
     VMLM_TRY(bf16_norm_plan(c, M, N, K, &bp));
+  // a K split of pair tiles adds two partials into C: the prep zeroes it first
+  const bool zero_c = bp.pairs && bp.ksplit > 1;
+  VMLM_TRY(launch(bf16_terms_norm_kernel, dim3(M), dim3(kNormPrepThreads), 0, st, true, a,
+                  static_cast<long long>(K), M, K, kp, static_cast<int>((K % 4 == 0) && aligned16(a)), terms,
+                  static_cast<uint8_t*>(c->norm_dirty.p), orword, orword_next, zero_c ? out : nullptr,
+                  static_cast<long long>(N), N, static_cast<int>((N % 4 == 0) && aligned16(out))));
+  TcParams p = {};
+  p.rows = M;
+  p.cols = N;
   const NormPlan plan = bp.plan;
   p.bn = plan.bn;
   p.max_terms = 3;
@@ -1141,10 +1184,11 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
   CUtensorMap ma, mb;
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, terms, 3ull * kp, M, 6ull * kp, 64, kTileRows));
   if (bp.pairs) {
-    p.bn = kPairBn;
+    p.bn = bp.pair_bn;
+    p.ksplit = bp.ksplit;
     p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
     p.tiles_n = static_cast<int>(cdiv(N, p.bn));
-    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, kPairBn / 2));
+    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn / 2));
     return run_tc2<TcMode::kBf16Norm>(c, st, ma, mb, p, true);
   }
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
