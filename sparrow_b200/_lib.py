@@ -58,6 +58,7 @@ SIGNATURES = {
     "vmlm_launch_count": (ctypes.c_uint64, []),
     "vmlm_profile_enable": (I, [I]),
     "vmlm_profile_take": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)]),
+    "vmlm_profile_kernel": (I, [ctypes.c_char_p, ctypes.c_size_t]),
     "vmlm_probe_mma_peak": (I, [I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "vmlm_trace_enable": (I, [I]),
     "vmlm_trace_take": (I, [P, S]),

@@ -42,10 +42,11 @@ struct Tc2Smem {
   uint32_t a_bytes, b_bytes, total;
 };
 
-__host__ __device__ inline Tc2Smem tc2_smem_layout(int stages, int bn) {
+// a_bytes / b_bytes: one stage of each operand (kps k-blocks of 128 bytes per row)
+__host__ __device__ inline Tc2Smem tc2_smem_layout(int stages, int bn, int kps = 1) {
   Tc2Smem s;
-  s.a_bytes = kTileRows * kBlockBytes;
-  s.b_bytes = static_cast<uint32_t>(bn / 2) * kBlockBytes;
+  s.a_bytes = static_cast<uint32_t>(kps) * kTileRows * kBlockBytes;
+  s.b_bytes = static_cast<uint32_t>(kps) * static_cast<uint32_t>(bn / 2) * kBlockBytes;
   s.a_off = 0;
   s.b_off = s.a_off + stages * s.a_bytes;
   s.bar_off = s.b_off + stages * s.b_bytes;
@@ -69,7 +70,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  const Tc2Smem L = tc2_smem_layout(p.stages, p.bn);
+  const Tc2Smem L = tc2_smem_layout(p.stages, p.bn, p.kps);
+  const uint32_t a_kb_bytes = kTileRows * kBlockBytes;                         // one k-block of A
+  const uint32_t b_kb_bytes = static_cast<uint32_t>(p.bn / 2) * kBlockBytes;  // one k-block of B
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty_bar = full_bar + p.stages;
   uint64_t* tfull_bar = empty_bar + p.stages;
@@ -159,10 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int a_row, tn, kb0, kb1;
       for (int i = 0; ok && tile_of(i, a_row, tn, kb0, kb1); ++i) {
         const int b_row = tn * p.bn + static_cast<int>(crank) * (p.bn / 2);
-        const int nkb = kb1 - kb0;
-        for (int j = 0; j < T * nkb; ++j) {
-          const int term = j / nkb;
-          const int kin = kb0 + (j - term * nkb);
+        const int nops = (kb1 - kb0 + p.kps - 1) / p.kps;  // stages per term
+        for (int j = 0; j < T * nops; ++j) {
+          const int term = j / nops;
+          const int kin = kb0 + (j - term * nops) * p.kps;
           const unsigned long long tw = trace ? globaltimer() : 0;
           if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) {
             ok = false;
@@ -170,10 +173,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (trace) wait_empty += globaltimer() - tw;
           if (crank == 0) mbar_arrive_expect_tx(full_bar + stage, 2 * (L.a_bytes + L.b_bytes));
-          const int kbx = kin * p.a_box_elems;
           const uint32_t fb = full_even + stage * 8;
-          tma_load_2d_pair(smem + L.a_off + stage * L.a_bytes, &tmA, fb, term * p.term_stride + kbx, a_row, pol_a);
-          tma_load_2d_pair(smem + L.b_off + stage * L.b_bytes, &tmB, fb, kbx, b_row, pol_b);
+          if (p.kps == 1) {
+            const int kbx = kin * p.a_box_elems;
+            tma_load_2d_pair(smem + L.a_off + stage * L.a_bytes, &tmA, fb, term * p.term_stride + kbx, a_row, pol_a);
+            tma_load_2d_pair(smem + L.b_off + stage * L.b_bytes, &tmB, fb, kbx, b_row, pol_b);
+          } else {
+            // k-blocks past this range's end are loaded (zeros past K) but not multiplied
+            tma_load_3d_pair(smem + L.a_off + stage * L.a_bytes, &tmA, fb, a_row, term * p.term_kb + kin, pol_a);
+            tma_load_3d_pair(smem + L.b_off + stage * L.b_bytes, &tmB, fb, b_row, kin, pol_b);
+          }
           issued_mask |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
@@ -212,7 +221,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (trace) wait_accum += globaltimer() - tw0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * p.bn);
-        for (int j = 0; j < T * (kb1 - kb0); ++j) {
+        const int nkb = kb1 - kb0;
+        const int nops = (nkb + p.kps - 1) / p.kps;
+        for (int j = 0; j < T * nops; ++j) {
           const unsigned long long tw1 = trace ? globaltimer() : 0;
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
@@ -221,17 +232,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (trace) wait_full += globaltimer() - tw1;
           tc_fence_after();
           if (trace && !issued) trace[3] = globaltimer();
+          const int o = j % nops;
+          const int nv = min(p.kps, nkb - o * p.kps);  // k-blocks of this stage inside the range
           const uint32_t a_addr = smem_u32(smem + L.a_off + stage * L.a_bytes);
           const uint32_t b_addr = smem_u32(smem + L.b_off + stage * L.b_bytes);
-          #pragma unroll
-          for (uint32_t u = 0; u < 4; ++u) {
-            const uint64_t ad = umma_desc_sw128(a_addr + 32 * u);
-            const uint64_t bd = umma_desc_sw128(b_addr + 32 * u);
-            const uint32_t acc = (j > 0 || u > 0) ? 1u : 0u;
-            if constexpr (kInt)
-              umma_i8_pair(d_tmem, ad, bd, idesc, acc);
-            else
-              umma_f16_pair(d_tmem, ad, bd, idesc, acc);
+          for (int v = 0; v < nv; ++v) {
+            #pragma unroll
+            for (uint32_t u = 0; u < 4; ++u) {
+              const uint64_t ad = umma_desc_sw128(a_addr + v * a_kb_bytes + 32 * u);
+              const uint64_t bd = umma_desc_sw128(b_addr + v * b_kb_bytes + 32 * u);
+              const uint32_t acc = (j > 0 || v > 0 || u > 0) ? 1u : 0u;
+              if constexpr (kInt)
+                umma_i8_pair(d_tmem, ad, bd, idesc, acc);
+              else
+                umma_f16_pair(d_tmem, ad, bd, idesc, acc);
+            }
           }
           issued = true;
           umma_commit_pair(empty_bar + stage);

@@ -96,6 +96,9 @@ struct TcParams {
   int csplit;        // normal modes: > 1 = each tile's K split over a cluster of csplit CTAs
   int ksplit;        // tc2_gemm_kernel, normal modes: K ranges per pair tile (1 or 2); with 2 each
                      // range's partial is added into C (zeroed beforehand) with red.global.add
+  int kps;           // tc2_gemm_kernel: k-blocks per stage (1: 2-D tensor maps; 2..3: 3-D maps, one
+                     // load per operand per stage; A's k-block coordinate of term t is t * term_kb + kb)
+  int term_kb;       // k-blocks per term in A's 3-D map (kBf16Norm)
   // kF32Norm (C = A . B^T, both operands f32 split into three bf16 terms):
   // B's terms at j * term_stride along its K, B's OR word, per-row NaN/Inf
   // flags of A and B, both term buffers ([rows][3 * term_stride]) for the

@@ -328,6 +328,27 @@ int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t 
   return VMLM_OK;
 }
 
+// 3-D view (128-byte k-block, row, k-block index) of a row-major matrix whose
+// row pitch is a whole number of 128-byte k-blocks; a box of box_rows rows x
+// box_kb k-blocks lands as box_kb consecutive 128-byte-swizzled tiles
+// (tma_load_3d). Rows and k-blocks past the matrix read as zeros.
+int make_map3(CUtensorMap* m, CUtensorMapDataType dt, int esz, const void* base, uint64_t rows, uint64_t row_bytes,
+              uint32_t box_rows, uint32_t box_kb) {
+  if (row_bytes % 128 != 0) return fail(VMLM_ERR_SHAPE, "3-D tensor map needs whole 128-byte k-blocks per row");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(128 / esz), rows, row_bytes / 128};
+  cuuint64_t strides[2] = {row_bytes, 128};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / esz), box_rows, box_kb};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(VMLM_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d): rows %llu, pitch %llu, box %u x %u",
+                static_cast<int>(r), static_cast<unsigned long long>(rows), static_cast<unsigned long long>(row_bytes),
+                box_rows, box_kb);
+  return VMLM_OK;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 inline int pow2_at_least(int v) {
@@ -442,9 +463,24 @@ int prof_begin(Ctx* c, cudaStream_t st, ProfPair* pp) {
   return VMLM_OK;
 }
 
-int prof_end(cudaStream_t st, const ProfPair& pp) {
+// The last profiled launch: kernel and plan, for vmlm_profile_kernel.
+std::string g_prof_last;
+
+const char* tc_mode_name(TcMode m) {
+  switch (m) {
+    case TcMode::kQ8Swap: return "kQ8Swap";
+    case TcMode::kBf16Swap: return "kBf16Swap";
+    case TcMode::kBf16Norm: return "kBf16Norm";
+    case TcMode::kI8Norm: return "kI8Norm";
+    case TcMode::kF32Norm: return "kF32Norm";
+  }
+  return "?";
+}
+
+int prof_end(cudaStream_t st, const ProfPair& pp, const std::string& what) {
   VMLM_CUDA(cudaEventRecord(pp.b, st));
   g_prof_live.push_back(pp);
+  g_prof_last = what;
   return VMLM_OK;
 }
 
@@ -488,7 +524,11 @@ int run_tc(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb
   VMLM_TRY(prof_begin(c, st, &pp));
   VMLM_TRY(launch_ex(tc_gemm_kernel<MODE>, dim3(static_cast<unsigned>(grid)), dim3(kThreads), L.total, st, false,
                      cluster, ma, mb, p));
-  return prof_end(st, pp);
+  char what[160];
+  snprintf(what, sizeof what, "tc_gemm_kernel<%s>: %d CTAs, tiles %d x %d (128 x %d), %s %d", tc_mode_name(MODE),
+           static_cast<int>(grid), p.tiles_m, p.tiles_n, p.bn, p.csplit > 1 ? "cluster K split" : "stream-K",
+           p.csplit > 1 ? p.csplit : p.streamk);
+  return prof_end(st, pp, what);
 }
 
 // Large prefill GEMMs on CTA pairs (tc2_gemm_kernel): 256 x 256 tiles, one
@@ -522,10 +562,22 @@ int tc2_max_pairs(Ctx* ctx, uint32_t smem, int* out) {
   return VMLM_OK;
 }
 
-int tc2_stages(int bn) {
+int tc2_stages(int bn, int kps = 1) {
   int stages = 16;
-  while (stages >= 2 && tc2_smem_layout(stages, bn).total > static_cast<uint32_t>(kMaxSmem)) --stages;
+  while (stages >= 2 && tc2_smem_layout(stages, bn, kps).total > static_cast<uint32_t>(kMaxSmem)) --stages;
   return stages;
+}
+
+// k-blocks per stage of a CTA-pair launch. Several k-blocks per load (3-D
+// maps) stream far faster than one (a 128-row x 128-byte 2-D box streams at
+// about 5 TB/s from HBM and 32 GB/s per SM from L2; three k-blocks per load
+// reach 6.5 TB/s and 84 GB/s per SM), so take 3, or 2, while two stages fit;
+// 3-D maps need both operands' row pitches to be whole k-blocks.
+int tc2_pick_kps(int bn, uint64_t a_row_bytes, uint64_t b_row_bytes) {
+  if (a_row_bytes % 128 != 0 || b_row_bytes % 128 != 0) return 1;
+  for (int kps = 3; kps >= 2; --kps)
+    if (tc2_stages(bn, kps) >= 2) return kps;
+  return 1;
 }
 
 bool use_pairs(const NormPlan& plan, long long rows, long long cols, int sms) {
@@ -540,11 +592,13 @@ template <TcMode MODE>
 int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, TcParams p, bool pdl) {
   if (p.ksplit > 1 && (MODE != TcMode::kBf16Norm || p.ksplit > 2 || p.ksplit > p.kb_per_term))
     return fail(VMLM_ERR_SHAPE, "a K split of pair tiles takes bf16 calls, two ranges, a k-block each");
-  p.stages = tc2_stages(p.bn);
+  if (p.kps < 1) p.kps = 1;
+  p.stages = tc2_stages(p.bn, p.kps);
+  if (p.stages < 2) return fail(VMLM_ERR_SHAPE, "pair tile too large for shared memory");
   p.tmem_cols = pow2_at_least(2 * p.bn);
   p.csplit = 0;
   p.streamk = 0;
-  const Tc2Smem L = tc2_smem_layout(p.stages, p.bn);
+  const Tc2Smem L = tc2_smem_layout(p.stages, p.bn, p.kps);
   int max_pairs = 0;
   VMLM_TRY(tc2_max_pairs<MODE>(c, L.total, &max_pairs));
   if (max_pairs < 1) return fail(VMLM_ERR_CUDA, "no CTA pair fits on this device");
@@ -559,7 +613,10 @@ int run_tc2(Ctx* c, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& m
   VMLM_TRY(prof_begin(c, st, &pp));
   VMLM_TRY(launch_ex(tc2_gemm_kernel<MODE>, dim3(static_cast<unsigned>(2 * pairs)), dim3(kThreads), L.total, st,
                      false, 2, ma, mb, p));
-  return prof_end(st, pp);
+  char what[160];
+  snprintf(what, sizeof what, "tc2_gemm_kernel<%s>: %d CTA pairs, tiles %d x %d (256 x %d), K ranges %d",
+           tc_mode_name(MODE), static_cast<int>(pairs), p.tiles_m, p.tiles_n, p.bn, p.ksplit > 1 ? p.ksplit : 1);
+  return prof_end(st, pp, what);
 }
 
 int check_dims(size_t m, size_t n, size_t k) {
@@ -674,7 +731,8 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   VMLM_TRY(launch_ex(q8_decode_kernel<DecNoGroup>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), plan.smem,
                      st, true, plan.c, mw, mp, p, DecNoGroup{0}));
-  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  if (g_profile) VMLM_TRY(prof_end(st, pp, "q8_decode_kernel: " + std::to_string(grid) + " CTAs, clusters of " +
+                                                std::to_string(plan.c)));
   return VMLM_OK;
 }
 
@@ -808,7 +866,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   VMLM_TRY(launch(q8_decode_sk_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st, true, p, grp));
-  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  if (g_profile) VMLM_TRY(prof_end(st, pp, "q8_decode_sk_kernel: " + std::to_string(grid) + " CTAs, equal shares"));
   *done = true;
   return VMLM_OK;
 }
@@ -920,7 +978,9 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   // the tensor-map arguments of the ungrouped form are unused here
   VMLM_TRY(launch_ex(q8_decode_kernel<DecGroup>, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st,
                      true, c, grp.prob[0].map, grp.prob[0].map, p, grp));
-  if (g_profile) VMLM_TRY(prof_end(st, pp));
+  if (g_profile)
+    VMLM_TRY(prof_end(st, pp, "q8_decode_kernel (grouped): " + std::to_string(grid) + " CTAs, clusters of " +
+                                  std::to_string(c)));
   *done = true;
   return VMLM_OK;
 }
@@ -1067,8 +1127,14 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   if (!use_streamk(p, c->sms) && N >= kPairRows) {
     // whole tiles: CTA pairs over 256 weight rows, each SM loading half the planes
     p.tiles_m = static_cast<int>(cdiv(N, kPairRows));
-    VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
-    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn / 2));
+    p.kps = tc2_pick_kps(p.bn, K, kp);
+    if (p.kps > 1) {
+      VMLM_TRY(make_map3(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, N, K, kTileRows, p.kps));
+      VMLM_TRY(make_map3(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, planes, 3ull * M, kp, p.bn / 2, p.kps));
+    } else {
+      VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+      VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128, p.bn / 2));
+    }
     return run_tc2<TcMode::kQ8Swap>(c, st, ma, mb, p, true);
   }
   VMLM_TRY(make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
@@ -1188,7 +1254,15 @@ int run_bf16_norm(Ctx* c, const float* a, const uint16_t* b, float* out, int M, 
     p.ksplit = bp.ksplit;
     p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
     p.tiles_n = static_cast<int>(cdiv(N, p.bn));
-    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn / 2));
+    // the terms' rows hold three terms of kp elements: whole k-blocks when kp % 64 == 0
+    p.kps = kp % 64 == 0 ? tc2_pick_kps(p.bn, 6ull * kp, 2ull * K) : 1;
+    if (p.kps > 1) {
+      p.term_kb = kp / 64;
+      VMLM_TRY(make_map3(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, terms, M, 6ull * kp, kTileRows, p.kps));
+      VMLM_TRY(make_map3(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, N, 2ull * K, p.bn / 2, p.kps));
+    } else {
+      VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn / 2));
+    }
     return run_tc2<TcMode::kBf16Norm>(c, st, ma, mb, p, true);
   }
   VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, 2ull * K, 64, p.bn));
@@ -1383,7 +1457,13 @@ int run_i8i8(Ctx* c, const int8_t* x, const int8_t* w, const float* scale, float
     p.bn = kPairBn;
     p.tiles_m = static_cast<int>(cdiv(M, 2 * kTileRows));
     p.tiles_n = static_cast<int>(cdiv(N, p.bn));
-    VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, kPairBn / 2));
+    p.kps = tc2_pick_kps(p.bn, K, K);
+    if (p.kps > 1) {
+      VMLM_TRY(make_map3(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, M, K, kTileRows, p.kps));
+      VMLM_TRY(make_map3(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, N, K, kPairBn / 2, p.kps));
+    } else {
+      VMLM_TRY(make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, 128, kPairBn / 2));
+    }
     if (sh) apply_shard(p, *sh);
     return run_tc2<TcMode::kI8Norm>(c, st, ma, mb, p, false);
   }
@@ -2508,6 +2588,13 @@ int vmlm_trace_take(uint64_t* host, size_t n_values) {
 int vmlm_profile_enable(int on) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   g_profile = on != 0;
+  return VMLM_OK;
+}
+
+int vmlm_profile_kernel(char* buf, size_t n) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!buf || n == 0) return fail(VMLM_ERR_ARG, "vmlm_profile_kernel: null buffer");
+  snprintf(buf, n, "%s", g_prof_last.c_str());
   return VMLM_OK;
 }
 

@@ -133,6 +133,13 @@ def profile_take():
     return ms.value, n.value
 
 
+def profile_kernel() -> str:
+    """Kernel and tile plan of the last profiled GEMM launch."""
+    buf = ctypes.create_string_buffer(256)
+    check(lib().vmlm_profile_kernel(buf, len(buf)))
+    return buf.value.decode()
+
+
 # ------------------------------------------------------- reference operators
 
 def gemm_nt_int8(a, q, scale, c, m, n, k) -> None:
