@@ -121,7 +121,8 @@ def run_case(args):
     torch.cuda.set_device(0)
     K.init(0)
     kind, m, n, k = CASES[args.case]
-    st = torch.cuda.current_stream()
+    st = torch.cuda.Stream()  # CUDA graphs cannot be captured on the legacy default stream
+    torch.cuda.set_stream(st)
 
     def make(r):
         """The step on input copy r (r = 0: the seeds the flushed timing has always used)."""
@@ -380,24 +381,48 @@ def copies_for(nbytes):
     return max(1, -(-2 * L2_BYTES // int(nbytes)))
 
 
-def time_rotating(steps, k, warmup, dist=None):
+def time_rotating(steps, k, warmup, dist=None, graph=True):
     """Device time per step of k steps run back to back, cycling through
     `steps` (one per input copy, together larger than twice L2), between one
     event pair on the current stream; max over ranks; ms/step. No L2 flush:
     the inputs are cold because they are larger than L2, the code and launch
-    path are warm, as in a loop over layers."""
+    path are warm, as in a loop over layers.
+
+    graph=True: the k steps are captured in one CUDA graph (after the warm-up
+    steps have sized the library's workspace) and the graph is replayed once
+    untimed and once timed, as an engine runs its step loop; the host's
+    per-call work (argument checks, tensor-map encoding, launches) then stays
+    out of the device time. graph=False: the steps are issued one by one from
+    the host (sharded calls, whose cross-rank handshake counts calls, and NCCL
+    collectives are timed this way)."""
     import torch
     n = len(steps)
     for i in range(warmup):
         steps[i % n]()
+    torch.cuda.synchronize()
     barrier(dist)
     st = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(st)
-    for i in range(k):
-        steps[i % n]()
-    b.record(st)
-    torch.cuda.synchronize()
+    if graph:
+        k += k % 2  # an even count: bf16 calls alternate between two flag words
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(k):
+                steps[i % n]()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier(dist)
+        a.record(st)
+        g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        del g
+    else:
+        a.record(st)
+        for i in range(k):
+            steps[i % n]()
+        b.record(st)
+        torch.cuda.synchronize()
     barrier(dist)
     return max_over_ranks(dist, a.elapsed_time(b)) / k
 
@@ -570,10 +595,14 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
         step = lambda: K.gemm_nt_int8_dev(x, q, s, c, m, n, k, stream=st)  # noqa: E731
         return step, n * k + 4 * n + 4 * m * k + 4 * m * n
 
-    def rot_entry(nbytes, copies, t, tg):
-        return {"step_us": t * 1e3, "gemm_us": tg * 1e3, "frac_hbm_step": nbytes / t / 1e6 / hbm,
-                "frac_hbm_gemm": nbytes / tg / 1e6 / hbm, "copies": copies,
-                "how": "steps back to back over rotating input copies (more than twice L2), no flush"}
+    def rot_entry(nbytes, copies, t, tg, t_eager=None):
+        e = {"step_us": t * 1e3, "gemm_us": tg * 1e3, "frac_hbm_step": nbytes / t / 1e6 / hbm,
+             "frac_hbm_gemm": nbytes / tg / 1e6 / hbm, "copies": copies,
+             "how": "steps back to back over rotating input copies (more than twice L2), no flush, captured in "
+                    "one CUDA graph; gemm_us: the GEMM launch alone, issued from the host between an event pair"}
+        if t_eager is not None:
+            e["eager_step_us"] = t_eager * 1e3  # the same steps issued one by one from Python
+        return e
 
     def hbm_entry(nbytes, t, tg):
         return {"bytes": nbytes, "step_us": t * 1e3, "gemm_us": tg * 1e3, "GBps_step": nbytes / t / 1e6,
@@ -585,7 +614,8 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
     step, nbytes = q8_layer(1, 5760, 2304, 0, calls1)
     e = hbm_entry(nbytes, time_steps(step, 50, 5, flush, dist), gemm_only(K, step, 20, flush, dist))
     rot = [q8_layer(1, 5760, 2304, 1000 + 2 * i)[0] for i in range(copies_for(nbytes))]
-    e["rot"] = rot_entry(nbytes, len(rot), time_rotating(rot, 200, 10, dist), gemm_only_rotating(K, rot, 100, dist))
+    e["rot"] = rot_entry(nbytes, len(rot), time_rotating(rot, 200, 10, dist), gemm_only_rotating(K, rot, 100, dist),
+                         time_rotating(rot, 200, 10, dist, graph=False))
     del rot
     if do_cpu:
         x, q, s, c, m, n, k = calls1[0]
@@ -630,9 +660,12 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
             bat_steps.append(lambda cr=cr: K.gemm_nt_int8_batch_dev(cr, stream=st))
         tl = time_rotating(lay_steps, 60, 5, dist)
         tbr = time_rotating(bat_steps, 60, 5, dist)
+        tbr_eager = time_rotating(bat_steps, 60, 5, dist, graph=False)
         entry["rot"] = {"layer_us": tl * 1e3, "frac_hbm_layer": nbytes / tl / 1e6 / hbm, "batch_us": tbr * 1e3,
                         "frac_hbm_batch": nbytes / tbr / 1e6 / hbm, "copies": len(bat_steps),
-                        "how": "steps back to back over rotating copies of the layer's inputs, no flush"}
+                        "batch_eager_us": tbr_eager * 1e3,
+                        "how": "steps back to back over rotating copies of the layer's inputs, no flush, captured "
+                               "in one CUDA graph (batch_eager_us: the batch calls issued one by one from Python)"}
         del lay_steps, bat_steps
         if do_cpu:
             torch.cuda.synchronize()
@@ -664,7 +697,7 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
         entry.update({"ranks": world, "frac_hbm_gemm_per_gpu": nbytes / world / tg / 1e6 / hbm})
         # the weight shard alone is larger than twice L2 at one rank; at more ranks, back to back
         entry["rot"] = rot_entry(nbytes, 1, time_rotating([step], 40, 3, dist),
-                                 gemm_only_rotating(K, [step], 20, dist))
+                                 gemm_only_rotating(K, [step], 20, dist), time_rotating([step], 40, 3, dist, graph=False))
         entry["rot"]["frac_hbm_gemm_per_gpu"] = nbytes / world / entry["rot"]["gemm_us"] / 1e3 / hbm
         if do_cpu:
             step()
@@ -693,8 +726,8 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
                 sharded_gemm_nt_int8(x, q4, s4, peers, m, n4, k4, stream=st)
             tf = time_steps(step_fused, 20, 3, flush, dist)
             entry.update({"step_fused_allgather_us": tf * 1e3, "GBps_fused_allgather": nbytes / tf / 1e6})
-            entry["rot"].update({"allgather_us": time_rotating([step_ag], 40, 3, dist) * 1e3,
-                                 "fused_allgather_us": time_rotating([step_fused], 40, 3, dist) * 1e3})
+            entry["rot"].update({"allgather_us": time_rotating([step_ag], 40, 3, dist, graph=False) * 1e3,
+                                 "fused_allgather_us": time_rotating([step_fused], 40, 3, dist, graph=False) * 1e3})
             def nccl_full():
                 # the GEMM writes [m][nloc] contiguously; pad the last rank's slice to `rows` columns
                 step()
@@ -764,8 +797,8 @@ def bench_configs(K, dist, rank, world, flush, pk, cpu_budget, variants):
         tf = time_steps(step_fused, 5, 2, flush, dist)
         entry.update({"step_fused_allgather_us": tf * 1e3, "TOPS_fused_allgather": ops / tf / 1e9,
                       "gather_ingress_GBps_over_call": 4.0 * m5 * (n5 - cols) / tf / 1e6})
-        entry["rot"].update({"allgather_us": time_rotating([step_ag], 10, 2, dist) * 1e3,
-                             "fused_allgather_us": time_rotating([step_fused], 10, 2, dist) * 1e3})
+        entry["rot"].update({"allgather_us": time_rotating([step_ag], 10, 2, dist, graph=False) * 1e3,
+                             "fused_allgather_us": time_rotating([step_fused], 10, 2, dist, graph=False) * 1e3})
         rows_s = torch.arange(0, m5, 64, device="cuda")
         def nccl_full():
             step_ag()
@@ -956,13 +989,14 @@ def r4(v):
     return None if v is None else round(float(v), 4)
 
 
-def make_summary(value, ms_per_step, flushed_ms, roofline, e2e, configs, check, probe, cpu, world):
+def make_summary(value, ms_per_step, eager_ms, flushed_ms, roofline, e2e, configs, check, probe, cpu, world):
     """Compact per-configuration record, printed as the last key of the bench
     line: device time (steps back to back over inputs larger than L2; and one
     step after an L2 flush, `flushed_us`), the roofline fraction of each
     configuration's dominant bound, the CPU restatement on 1 core and on all
     threads, and the parity checks made in this run."""
-    s = {"C2_headline": {"us": r4(ms_per_step * 1e3), "flushed_us": r4(flushed_ms * 1e3), "TFLOPS": r4(value / world),
+    s = {"C2_headline": {"us": r4(ms_per_step * 1e3), "eager_us": r4(eager_ms * 1e3), "flushed_us": r4(flushed_ms * 1e3),
+                         "TFLOPS": r4(value / world),
                          "gemm_us": r4(roofline["kernel_us"]), "gemm_frac": r4(roofline["frac"]),
                          "e2e_us": r4(e2e["ms_per_step"] * 1e3), "copy_floor_us": r4(e2e.get("copy_floor_ms", 0) * 1e3),
                          "copy_duplex_us": r4(e2e.get("copy_floor_duplex_ms", 0) * 1e3),
@@ -975,26 +1009,28 @@ def make_summary(value, ms_per_step, flushed_ms, roofline, e2e, configs, check, 
     cpu_of = lambda e, unit: {"cpu1_" + unit: r4(e.get("cpu", {}).get("1core")),  # noqa: E731
                               "cpuN_" + unit: r4(e.get("cpu", {}).get("all"))}
     e = configs["C1_q8_gemv_1x5760x2304"]
-    s["C1"] = {"us": r4(e["rot"]["step_us"]), "gemm_us": r4(e["rot"]["gemm_us"]),
-               "frac_hbm": r4(e["rot"]["frac_hbm_gemm"]), "flushed_us": r4(e["step_us"]),
-               "err": r4(e.get("max_rel_err_vs_oracle")), **cpu_of(e, "GBps")}
+    s["C1"] = {"us": r4(e["rot"]["step_us"]), "eager_us": r4(e["rot"].get("eager_step_us")),
+               "frac_hbm": r4(e["rot"]["frac_hbm_step"]), "gemm_us": r4(e["rot"]["gemm_us"]),
+               "flushed_us": r4(e["step_us"]), "err": r4(e.get("max_rel_err_vs_oracle")), **cpu_of(e, "GBps")}
     for m in (1, 8, 32):
         e = configs[f"C3_q8_layer_set_M{m}"]
         s[f"C3_M{m}"] = {"batch_us": r4(e["rot"]["batch_us"]), "frac_hbm_batch": r4(e["rot"]["frac_hbm_batch"]),
+                         "batch_eager_us": r4(e["rot"].get("batch_eager_us")),
                          "calls_us": r4(e["rot"]["layer_us"]), "batch_flushed_us": r4(e["batch"]["step_us"]),
                          "err": r4(e.get("max_rel_err_vs_oracle")), **cpu_of(e, "GBps")}
     for m in (1, 64):
         e = configs[f"C4_q8_lm_head_M{m}"]
-        d = {"us": r4(e["rot"]["step_us"]), "gemm_us": r4(e["rot"]["gemm_us"]),
-             "frac_hbm_per_gpu": r4(e["rot"]["frac_hbm_gemm_per_gpu"]), "flushed_us": r4(e["step_us"]),
-             "err": r4(e.get("max_rel_err_vs_oracle")), **cpu_of(e, "GBps")}
+        d = {"us": r4(e["rot"]["step_us"]), "eager_us": r4(e["rot"].get("eager_step_us")),
+             "frac_hbm_per_gpu": r4(e["rot"]["frac_hbm_step"] / world), "gemm_us": r4(e["rot"]["gemm_us"]),
+             "flushed_us": r4(e["step_us"]), "err": r4(e.get("max_rel_err_vs_oracle")), **cpu_of(e, "GBps")}
         if "fused_allgather_us" in e["rot"]:
             d.update({"fused_gather_us": r4(e["rot"]["fused_allgather_us"]),
                       "nccl_gather_us": r4(e["rot"]["allgather_us"])})
         s[f"C4_M{m}"] = d
     e = configs["C5_i8i8_ffn_4096x28672x8192"]
     d = {"us": r4(e["rot"]["step_us"]), "gemm_us": r4(e["rot"]["gemm_us"]),
-         "frac_int8": r4(e["rot"]["frac_int8_peak_per_gpu"]), "int8_peak_TOPS": r4(e["int8_peak"]["TOPS"]),
+         "frac_int8": r4(e["ops"] / world / e["rot"]["step_us"] / 1e6 / e["int8_peak"]["TOPS"]),
+         "int8_peak_TOPS": r4(e["int8_peak"]["TOPS"]),
          "flushed_us": r4(e["step_us"]), "bit_exact_rows": e.get("bit_exact_vs_oracle_rows"), **cpu_of(e, "TOPS")}
     if "fused_allgather_us" in e["rot"]:
         # bytes each GPU receives from its peers, over the whole sharded call
@@ -1014,7 +1050,9 @@ def run_ours(args):
     dev = torch.cuda.current_device()
     K.init(dev)
     pk = peaks()
-    st = torch.cuda.current_stream()
+    # all device work on one side stream: CUDA graphs cannot be captured on the legacy default stream
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
 
     x = gen((M2, K2), 0, 1.0).to(torch.bfloat16).float().contiguous()
@@ -1043,21 +1081,34 @@ def run_ours(args):
 
     for i in range(args.warmup):
         steps[i % copies]()
+    torch.cuda.synchronize()
+    barrier(dist)
+    # The timed steps: captured in one CUDA graph (an engine runs its layer
+    # loop that way; the host's per-call work then stays out of the device
+    # time), replayed once untimed and once between the event pair.
+    n0 = K.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(args.steps):
+            steps[i % copies]()
+    launches = K.launch_count() - n0  # library kernels in the graph: the timed replay launches these
+    graph.replay()
+    torch.cuda.synchronize()
     barrier(dist)
     time.sleep(0.3)
     clocks.on = True
-    n0 = K.launch_count()
     ev_a, ev_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev_a.record(st)
-    for i in range(args.steps):
-        steps[i % copies]()
+    graph.replay()
     ev_b.record(st)
     torch.cuda.synchronize()
     barrier(dist)
-    launches = K.launch_count() - n0
     dev_ms = max_over_ranks(dist, ev_a.elapsed_time(ev_b))
     ms_per_step = dev_ms / args.steps
     value = world * FLOP_C2 / (ms_per_step / 1e3) / 1e12
+    del graph
+    # the same steps issued one by one from Python (each call's host work included when it exceeds the GPU's)
+    eager_ms = time_rotating(steps, args.steps, 0, dist, graph=False)
     # the single-step latency with L2 flushed before the step, for comparison
     flushed_ms = time_steps(step, max(20, min(args.steps, 100)), 3, flush, dist)
 
@@ -1118,7 +1169,7 @@ def run_ours(args):
     if rank == 0 and world == 1:
         cpu = cpu_baseline_c2(x, w, args.cpu_seconds)
 
-    summary = make_summary(value, ms_per_step, flushed_ms, roofline, e2e, configs, check, probe, cpu, world)
+    summary = make_summary(value, ms_per_step, eager_ms, flushed_ms, roofline, e2e, configs, check, probe, cpu, world)
     out = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16",
@@ -1127,8 +1178,11 @@ def run_ours(args):
                       "k": K2, "parallelism": f"replicas x{world}",
                       "l2": f"inputs larger than L2: steps back to back over {copies} rotating copies of X and W "
                             f"({copies * (M2 * K2 * 4 + N2 * K2 * 2) / 1e6:.0f} MB, more than twice L2); "
-                            "latency_flushed_us is one step with L2 flushed before it"},
-           "latency_flushed_us": flushed_ms * 1e3,
+                            "latency_flushed_us is one step with L2 flushed before it",
+                      "timing": f"the {args.steps} timed steps captured in one CUDA graph, replayed once untimed "
+                                "and once between the event pair; eager_ms_per_step: the same steps issued one "
+                                "by one from Python"},
+           "latency_flushed_us": flushed_ms * 1e3, "eager_ms_per_step": eager_ms,
            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "e2e_matches_device_path": ok,
            "gpu_launches": launches, "clocks": clocks.summary(), "configs": configs, "summary": summary}
     if rank == 0:

@@ -53,6 +53,7 @@ struct DecParams {
   int rows_b;    // UMMA N: plane rows, 16 * ceil(3m / 16)
   int kbr_max;   // largest k-block range of one CTA
   int stages;    // W stage ring depth
+  int kps;       // k-blocks per W stage: 1 (2-D tensor maps) or 2..3 (3-D maps, one load per stage)
   int tmem_cols;
   int vec_x;     // x rows allow float4 loads
   // planes mode: the digit planes, exponents and non-finite flags come from
@@ -75,8 +76,9 @@ struct DecParams {
 // own weight tensor map, pointers and sizes; tile0 is its first tile (problems
 // are listed by descending k, so the longest tiles start first).
 struct DecProblem {
-  CUtensorMap map;    // W [n][k] int8, box 128 x 128
+  CUtensorMap map;    // W [n][k] int8, box 128 x 128 (2-D), or 128 rows x kps k-blocks (3-D, kps > 1)
   CUtensorMap map_p;  // planes mode: the problem's planes [3m][kp], box 128 x rows_b
+  CUtensorMap map3;   // q8_decode_sk_kernel with kps > 1: W as a 3-D map, box 128 rows x kps k-blocks
   const int* exps;
   const int* nonfinite;
   const float* x;
@@ -105,9 +107,9 @@ struct DecSmem {
   uint32_t b_off, recv_off, bar_off, meta_off, total;
 };
 
-__host__ __device__ inline DecSmem dec_smem_layout(int stages, int rows_b, int kbr, int m, int c) {
+__host__ __device__ inline DecSmem dec_smem_layout(int stages, int rows_b, int kbr, int m, int c, int kps = 1) {
   DecSmem s;
-  s.b_off = static_cast<uint32_t>(stages) * kDecStageBytes;  // W stages first, from offset 0
+  s.b_off = static_cast<uint32_t>(stages) * kps * kDecStageBytes;  // W stages first, from offset 0
   s.recv_off = s.b_off + static_cast<uint32_t>(kbr) * rows_b * kBlockBytes;
   const uint32_t recv = c > 1 ? static_cast<uint32_t>(c) * m * dec_rows_per_cta(c) * 8 : 0;
   s.bar_off = s.recv_off + ((recv + 15u) & ~15u);
@@ -160,7 +162,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  const DecSmem L = dec_smem_layout(p.stages, p.rows_b, p.kbr_max, p.m, p.cluster);
+  const DecSmem L = dec_smem_layout(p.stages, p.rows_b, p.kbr_max, p.m, p.cluster, p.kps);
+  const uint32_t stage_bytes = static_cast<uint32_t>(p.kps) * kDecStageBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty_bar = full_bar + p.stages;
   uint64_t* planes_bar = empty_bar + p.stages;
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb / c);
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * p.kb / c);
   const int nkb = kb1 - kb0;
+  const int nops = (nkb + p.kps - 1) / p.kps;  // W stages of this CTA's range
   unsigned long long* trace = p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceSlots : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
 
@@ -257,11 +261,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const uint64_t pol = policy_evict_first();
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0, last_phase = 0;
-      for (int j = 0; j < nkb; ++j) {
+      for (int o = 0; o < nops; ++o) {
         if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(full_bar + stage, kDecStageBytes);
-        tma_load_2d(smem + stage * kDecStageBytes, map_w, full_bar + stage, (kb0 + j) * kBlockBytes,
-                    tile * kTileRows, pol);
+        mbar_arrive_expect_tx(full_bar + stage, stage_bytes);
+        if (p.kps == 1)
+          tma_load_2d(smem + stage * stage_bytes, map_w, full_bar + stage, (kb0 + o) * kBlockBytes, tile * kTileRows,
+                      pol);
+        else  // k-blocks past this CTA's range are loaded (zeros past K) but not multiplied
+          tma_load_3d(smem + stage * stage_bytes, map_w, full_bar + stage, tile * kTileRows, kb0 + o * p.kps, pol);
         issued_mask |= 1u << stage;
         last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
         if (++stage == p.stages) {
@@ -286,19 +293,23 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int j = 0; j < nkb; ++j) {
+        for (int o = 0; o < nops; ++o) {
           if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (trace && !issued) trace[3] = globaltimer();
-          const uint32_t a_addr = smem_u32(smem + stage * kDecStageBytes);
-          const uint32_t b_addr = smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
-          #pragma unroll
-          for (uint32_t u = 0; u < 4; ++u)
-            umma_i8(tmem_base, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
-                    (j > 0 || u > 0) ? 1u : 0u);
+          const int nv = min(p.kps, nkb - o * p.kps);
+          for (int v = 0; v < nv; ++v) {
+            const int j = o * p.kps + v;
+            const uint32_t a_addr = smem_u32(smem + stage * stage_bytes + v * kDecStageBytes);
+            const uint32_t b_addr = smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
+            #pragma unroll
+            for (uint32_t u = 0; u < 4; ++u)
+              umma_i8(tmem_base, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
+                      (j > 0 || u > 0) ? 1u : 0u);
+          }
           issued = true;
           umma_commit(empty_bar + stage);
           if (++stage == p.stages) {

@@ -66,6 +66,8 @@ struct DecSkParams {
   int planes_mode;
   int rows_b;          // UMMA N: plane rows, 16 * ceil(3m / 16)
   int stages;          // W stage ring depth
+  int kps;             // k-blocks per stage (1..3): a stage holds up to kps consecutive k-blocks of one segment;
+                       // full ones arrive by one 3-D load (DecProblem::map3), shorter ones by 2-D loads
   int tmem_cols;       // kDecSkMaxSeg accumulators of rows_b columns, rounded up to a power of two
   int kbr_max;         // longest k-block range of one CTA
   int grid;            // CTAs; CTA b takes k-blocks [b * kb_total / grid, (b + 1) * kb_total / grid)
@@ -80,11 +82,13 @@ struct DecSkSmem {
   uint32_t stage, b_off, bar_off, meta_off, total;
 };
 
-__host__ __device__ inline DecSkSmem dec_sk_smem_layout(int stages, int rows_b, int kbr, int planes_mode) {
+__host__ __device__ inline DecSkSmem dec_sk_smem_layout(int stages, int rows_b, int kbr, int planes_mode,
+                                                        int kps = 1) {
   DecSkSmem s;
-  // a ring stage: the W box, then in planes mode the k-block's planes; the
-  // planes the kernel makes itself follow the ring
-  s.stage = kDecStageBytes + (planes_mode ? static_cast<uint32_t>(rows_b) * kBlockBytes : 0u);
+  // a ring stage: kps W boxes, then in planes mode their k-blocks' planes;
+  // the planes the kernel makes itself follow the ring
+  s.stage = static_cast<uint32_t>(kps) *
+            (kDecStageBytes + (planes_mode ? static_cast<uint32_t>(rows_b) * kBlockBytes : 0u));
   s.b_off = static_cast<uint32_t>(stages) * s.stage;  // the ring first, from offset 0
   s.bar_off = s.b_off + (planes_mode ? 0u : static_cast<uint32_t>(kbr) * rows_b * kBlockBytes);
   // full[stages], empty[stages], planes, tfull[kDecSkMaxSeg], done, drain; then the TMEM address and an abort word
@@ -228,7 +232,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  const DecSkSmem L = dec_sk_smem_layout(p.stages, p.rows_b, p.kbr_max, p.planes_mode);
+  const DecSkSmem L = dec_sk_smem_layout(p.stages, p.rows_b, p.kbr_max, p.planes_mode, p.kps);
+  const uint32_t planes_slot0 = static_cast<uint32_t>(p.kps) * kDecStageBytes;  // a stage's planes, after its W
+  const uint32_t planes_kb = static_cast<uint32_t>(p.rows_b) * kBlockBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty_bar = full_bar + p.stages;
   uint64_t* planes_bar = empty_bar + p.stages;
@@ -279,20 +285,38 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   // W producer state (thread 0). The first ring of W loads is issued right
   // after the barriers are initialised, before the CTA-wide barrier below:
-  // the weight stream does not wait for the other warps' set-up.
+  // the weight stream does not wait for the other warps' set-up. Stage o
+  // holds the k-blocks [j, j + n) of one segment (n <= kps): the range's
+  // segments cut into runs of kps, the last run of each segment shorter.
   const uint64_t pol = policy_evict_first();
-  int pstage = 0, pj = 0;
+  int pstage = 0, pj = 0, nops = 0;
   uint32_t pphase = 0, issued_mask = 0, last_phase = 0;
   bool planes_ok = false;  // planes mode: the planes kernel has finished (loads may read its planes)
-  auto issue = [&](int j) {
-    const int s = dec_sk_seg_of(sg, j);
+  // planes of stage `st` holding local k-blocks [j, j + n) of segment s
+  auto issue_planes = [&](int st, int s, int j, int n) {
     const int kb = dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s);
-    mbar_arrive_expect_tx(full_bar + pstage, L.stage);
-    tma_load_2d(smem + pstage * L.stage, &grp.prob[dec_sk_pick(sg.g, s)].map, full_bar + pstage, kb * kBlockBytes,
-                dec_sk_pick(sg.tile, s) * kTileRows, pol);
-    if (p.planes_mode && planes_ok)
-      tma_load_2d(smem + pstage * L.stage + kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, full_bar + pstage,
-                  kb * kBlockBytes, 0, policy_evict_last());
+    for (int v = 0; v < n; ++v)
+      tma_load_2d(smem + st * L.stage + planes_slot0 + v * planes_kb, &grp.prob[dec_sk_pick(sg.g, s)].map_p,
+                  full_bar + st, (kb + v) * kBlockBytes, 0, policy_evict_last());
+  };
+  auto issue = [&]() {  // the stage that starts at local k-block pj
+    const int s = dec_sk_seg_of(sg, pj);
+    const int j1 = dec_sk_pick(sg.j0, s) + dec_sk_pick(sg.hi, s) - dec_sk_pick(sg.lo, s);
+    const int n = min(p.kps, j1 - pj);
+    const int kb = dec_sk_pick(sg.lo, s) + pj - dec_sk_pick(sg.j0, s);
+    const DecProblem& pr = grp.prob[dec_sk_pick(sg.g, s)];
+    const int row = dec_sk_pick(sg.tile, s) * kTileRows;
+    mbar_arrive_expect_tx(full_bar + pstage, n * (kDecStageBytes + (p.planes_mode ? planes_kb : 0u)));
+    uint8_t* st = smem + pstage * L.stage;
+    if (n > 1 && n == p.kps) {
+      tma_load_3d(st, &pr.map3, full_bar + pstage, row, kb, pol);
+    } else {
+      for (int v = 0; v < n; ++v)
+        tma_load_2d(st + v * kDecStageBytes, &pr.map, full_bar + pstage, (kb + v) * kBlockBytes, row, pol);
+    }
+    if (p.planes_mode && planes_ok) issue_planes(pstage, s, pj, n);
+    pj += n;
+    ++nops;
     if (trace && issued_mask == 0) trace[8] = globaltimer();
     issued_mask |= 1u << pstage;
     last_phase = (last_phase & ~(1u << pstage)) | (pphase << pstage);
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
   };
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&grp.prob[sg.g[0]].map);
+    tma_prefetch_desc(p.kps > 1 ? &grp.prob[sg.g[0]].map3 : &grp.prob[sg.g[0]].map);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(full_bar + s, 1);
       mbar_init(empty_bar + s, 1);
@@ -313,13 +337,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    for (; pj < nkb && pj < p.stages; ++pj) issue(pj);  // every stage is free
+    while (pj < nkb && nops < p.stages) issue();  // every stage is free
     pdl_launch_dependents();
   }
   if (threadIdx.x == 32) {
+    // the segments' maps (a segment's last stage may take the 2-D map)
     #pragma unroll
-    for (int s = 1; s < kDecSkMaxSeg; ++s)
-      if (s < sg.n) tma_prefetch_desc(&grp.prob[sg.g[s]].map);
+    for (int s = 0; s < kDecSkMaxSeg; ++s)
+      if (s < sg.n) {
+        if (s > 0 || p.kps > 1) tma_prefetch_desc(&grp.prob[sg.g[s]].map);
+        if (p.kps > 1 && s > 0) tma_prefetch_desc(&grp.prob[sg.g[s]].map3);
+      }
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + kDecSkMaxSeg * kDecMaxTok) {
     s_max[threadIdx.x - 64] = 0;
@@ -340,15 +368,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // wait for the planes kernel (same stages, same full barriers)
         pdl_wait_prior();
         planes_ok = true;
-        for (int j = 0; j < pj; ++j) {
+        for (int o = 0, j = 0; o < nops; ++o) {  // replay the first ring's stages
           const int s = dec_sk_seg_of(sg, j);
-          tma_load_2d(smem + j * L.stage + kDecStageBytes, &grp.prob[dec_sk_pick(sg.g, s)].map_p, full_bar + j,
-                      (dec_sk_pick(sg.lo, s) + j - dec_sk_pick(sg.j0, s)) * kBlockBytes, 0, policy_evict_last());
+          const int j1 = dec_sk_pick(sg.j0, s) + dec_sk_pick(sg.hi, s) - dec_sk_pick(sg.lo, s);
+          const int n = min(p.kps, j1 - j);
+          issue_planes(o, s, j, n);
+          j += n;
         }
       }
-      for (; pj < nkb; ++pj) {
+      while (pj < nkb) {
         if (!mbar_wait(empty_bar + pstage, pphase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
-        issue(pj);
+        issue();
       }
       if (trace) trace[2] = globaltimer();
       if (*abort_flag) {
@@ -373,20 +403,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           const int j1 = j0 + dec_sk_pick(sg.hi, s) - dec_sk_pick(sg.lo, s);
           const uint32_t acc = tmem_base + static_cast<uint32_t>(s * p.rows_b);
           #pragma unroll 1
-          for (int j = j0; j < j1; ++j) {
+          for (int j = j0; j < j1; j += p.kps) {
             if (!mbar_wait(full_bar + stage, phase, p.err, abort_flag, kDevTimeoutFull)) {
               ok = false;
               break;
             }
             tc_fence_after();
             if (trace && !issued) trace[3] = globaltimer();
-            const uint32_t a_addr = smem_u32(smem + stage * L.stage);
-            const uint32_t b_addr =
-                p.planes_mode ? a_addr + kDecStageBytes : smem_u32(smem + L.b_off + j * p.rows_b * kBlockBytes);
-            #pragma unroll
-            for (uint32_t u = 0; u < 4; ++u)
-              umma_i8(acc, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
-                      (j > j0 || u > 0) ? 1u : 0u);
+            const int n = min(p.kps, j1 - j);
+            const uint32_t st = smem_u32(smem + stage * L.stage);
+            for (int v = 0; v < n; ++v) {
+              const uint32_t a_addr = st + v * kDecStageBytes;
+              const uint32_t b_addr = p.planes_mode ? st + planes_slot0 + v * planes_kb
+                                                    : smem_u32(smem + L.b_off + (j + v) * p.rows_b * kBlockBytes);
+              #pragma unroll
+              for (uint32_t u = 0; u < 4; ++u)
+                umma_i8(acc, umma_desc_sw128(a_addr + 32 * u), umma_desc_sw128(b_addr + 32 * u), idesc,
+                        (j + v > j0 || u > 0) ? 1u : 0u);
+            }
             issued = true;
             umma_commit(empty_bar + stage);
             if (++stage == p.stages) {

@@ -636,7 +636,17 @@ struct DecPlan {
   int stages = 0;
   int kbr = 0;
   uint32_t smem = 0;
+  int kps = 1;  // k-blocks per W stage (3-D maps when > 1)
 };
+
+// k-blocks per W stage of a decode CTA streaming ranges of about kbr k-blocks
+// of rows of row_bytes: 3 (or 2, when that wastes fewer k-blocks at the end of
+// a range) when rows are whole 128-byte k-blocks (3-D tensor maps), else 1.
+int dec_pick_kps(long long row_bytes, int kbr) {
+  if (row_bytes % 128 != 0 || kbr < 2) return 1;
+  const int waste3 = static_cast<int>(cdiv(kbr, 3) * 3 - kbr), waste2 = static_cast<int>(cdiv(kbr, 2) * 2 - kbr);
+  return waste2 < waste3 ? 2 : 3;
+}
 
 int max_active_clusters(Ctx* ctx, int cl, uint32_t smem, int* out) {
   const auto key = std::make_pair(cl, smem);
@@ -678,16 +688,19 @@ int plan_decode(Ctx* ctx, int M, int N, int K, bool planes_mode, DecPlan* plan) 
     if (!planes_mode &&
         static_cast<long long>(M) * kbr * (kBlockBytes / 4) > static_cast<long long>(kDecRegChunks) * kDecEpiThreads)
       continue;
-    int stages = kbr < 16 ? kbr : 16;
-    while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c).total > static_cast<uint32_t>(kMaxSmem)) --stages;
-    if (stages < 1 || (stages < 2 && kbr > 1)) continue;
-    const uint32_t smem = dec_smem_layout(stages, rows_b, kbr, M, c).total;
+    const int kps = dec_pick_kps(K, kbr);
+    const int ops = static_cast<int>(cdiv(kbr, kps));
+    int stages = ops < 16 ? ops : 16;
+    while (stages >= 1 && dec_smem_layout(stages, rows_b, kbr, M, c, kps).total > static_cast<uint32_t>(kMaxSmem))
+      --stages;
+    if (stages < 1 || (stages < 2 && ops > 1)) continue;
+    const uint32_t smem = dec_smem_layout(stages, rows_b, kbr, M, c, kps).total;
     int active = 0;
     VMLM_TRY(max_active_clusters(ctx, c, smem, &active));
     if (tiles > active) continue;  // one wave only
     if (tiles * c > best_ctas) {
       best_ctas = tiles * c;
-      *plan = DecPlan{c, stages, kbr, smem};
+      *plan = DecPlan{c, stages, kbr, smem, kps};
     }
   }
   return VMLM_OK;
@@ -706,6 +719,7 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   p.rows_b = static_cast<int>(16 * cdiv(3 * M, 16));
   p.kbr_max = plan.kbr;
   p.stages = plan.stages;
+  p.kps = plan.kps;
   p.tmem_cols = pow2_at_least(p.rows_b);
   p.vec_x = (K % 4 == 0) && aligned16(a);
   p.x = a;
@@ -721,7 +735,10 @@ int run_decode(Ctx* ctx, const float* a, const int8_t* q, const float* scale, fl
   p.exps = exps;
   p.nonfinite = nonf;
   CUtensorMap mw, mp;
-  VMLM_TRY(make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
+  if (p.kps > 1)
+    VMLM_TRY(make_map3(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, N, K, kTileRows, p.kps));
+  else
+    VMLM_TRY(make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, 128, kTileRows));
   if (planes)
     VMLM_TRY(make_map(&mp, CU_TENSOR_MAP_DATA_TYPE_UINT8, planes, K, 3ull * M, kp, 128,
                       static_cast<uint32_t>(p.rows_b)));
@@ -801,8 +818,12 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   // so the MMA starts on the first stage (loading the range's planes once, up
   // front, measured 1-2 us slower at m = 2..16 and does not fit at m = 32).
   const int mode = planes_mode ? 1 : 0;
-  int stages = kbr < 16 ? kbr : 16;
-  while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr, mode).total > static_cast<uint32_t>(kMaxSmem))
+  // three k-blocks per stage (3-D maps) when every problem's rows are whole k-blocks
+  int kps = 3;
+  for (int i = 0; i < count; ++i)
+    if (calls[i].k % 128 != 0) kps = 1;
+  int stages = 16;
+  while (stages >= 2 && dec_sk_smem_layout(stages, rows_b, kbr, mode, kps).total > static_cast<uint32_t>(kMaxSmem))
     --stages;
   if (stages < 2) return VMLM_OK;
   PlanesGroup pg;
@@ -823,6 +844,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
     const Q8Call& q = calls[order[i]];
     DecProblem& pr = grp.prob[i];
     VMLM_TRY(make_map(&pr.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, q.q, q.k, q.n, q.k, 128, kTileRows));
+    if (kps > 1) VMLM_TRY(make_map3(&pr.map3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.q, q.n, q.k, kTileRows, kps));
     pr.x = q.a;
     pr.w = q.q;
     pr.scale = q.scale;
@@ -854,6 +876,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   p.planes_mode = mode;
   p.rows_b = rows_b;
   p.stages = stages;
+  p.kps = kps;
   p.tmem_cols = pow2_at_least(kDecSkMaxSeg * rows_b);
   p.kbr_max = kbr;
   p.grid = grid;
@@ -862,7 +885,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   p.counters = static_cast<int*>(ctx->counters.p);
   p.err = ctx->err;
   p.trace = (g_trace && g_trace_dev == ctx->dev && static_cast<size_t>(grid) <= g_trace_ctas) ? g_trace : nullptr;
-  const uint32_t smem = dec_sk_smem_layout(stages, rows_b, kbr, mode).total;
+  const uint32_t smem = dec_sk_smem_layout(stages, rows_b, kbr, mode, kps).total;
   ProfPair pp;
   if (g_profile) VMLM_TRY(prof_begin(ctx, st, &pp));
   VMLM_TRY(launch(q8_decode_sk_kernel, dim3(static_cast<unsigned>(grid)), dim3(kDecThreads), smem, st, true, p, grp));
@@ -963,6 +986,7 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
                     dim3(kPrepThreads), 0, st, false, pg));
   DecParams p = {};
   p.m = M;
+  p.kps = 1;
   p.cluster = c;
   p.planes_mode = planes_mode ? 1 : 0;
   p.rows_b = rows_b;
