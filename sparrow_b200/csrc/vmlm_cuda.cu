@@ -571,12 +571,16 @@ int tc2_stages(int bn, int kps = 1) {
 // k-blocks per stage of a CTA-pair launch. Several k-blocks per load (3-D
 // maps) stream far faster than one (a 128-row x 128-byte 2-D box streams at
 // about 5 TB/s from HBM and 32 GB/s per SM from L2; three k-blocks per load
-// reach 6.5 TB/s and 84 GB/s per SM), so take 3, or 2, while two stages fit;
-// 3-D maps need both operands' row pitches to be whole k-blocks.
+// reach 6.5 TB/s and 84 GB/s per SM), so take 3, or 2, while three stages
+// fit, else while two do (with two stages the MMA of a tensor-bound tile
+// waits for each refill: C5 630 us with 2 k-blocks x 3 stages, 696 us with
+// 3 x 2, 705 us with 1 x 6). 3-D maps need both operands' row pitches to be
+// whole k-blocks.
 int tc2_pick_kps(int bn, uint64_t a_row_bytes, uint64_t b_row_bytes) {
   if (a_row_bytes % 128 != 0 || b_row_bytes % 128 != 0) return 1;
-  for (int kps = 3; kps >= 2; --kps)
-    if (tc2_stages(bn, kps) >= 2) return kps;
+  for (int min_stages = 3; min_stages >= 2; --min_stages)
+    for (int kps = 3; kps >= 2; --kps)
+      if (tc2_stages(bn, kps) >= min_stages) return kps;
   return 1;
 }
 
