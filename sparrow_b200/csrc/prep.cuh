@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kPrepThreads) q8_planes_kernel(const float* __
                                                                  int K, int kp, int8_t* __restrict__ planes,
                                                                  int* __restrict__ exps, int* __restrict__ nonfinite) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ float redf[32];
   __shared__ int redi[32];
   const int t = blockIdx.x;
@@ -197,6 +198,7 @@ struct PlanesGroup {
 
 __global__ void __launch_bounds__(kPrepThreads) q8_planes_group_kernel(const __grid_constant__ PlanesGroup g) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ float redf[32];
   __shared__ int redi[32];
   if (static_cast<int>(blockIdx.y) >= g.count || static_cast<int>(blockIdx.x) >= g.m) return;
@@ -228,6 +230,7 @@ __global__ void __launch_bounds__(kPrepThreads) q8_norm_planes_kernel(
     const float* __restrict__ src, long long lds, const float* __restrict__ g, float eps, int M, int K, int kp,
     float* __restrict__ xn, int8_t* __restrict__ planes, int* __restrict__ exps, int* __restrict__ nonfinite) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ float redf[32];
   __shared__ int redi[32];
   const int t = blockIdx.x;
@@ -449,6 +452,7 @@ __global__ void __launch_bounds__(kNormPrepThreads) f32_terms_nt_kernel(
     uint8_t* __restrict__ dirty_b, int* __restrict__ nf_a, int* __restrict__ nf_b, unsigned* __restrict__ or_a,
     unsigned* __restrict__ or_a_next, unsigned* __restrict__ or_b, unsigned* __restrict__ or_b_next) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ int redi[32];
   const int r = blockIdx.x;
   if (r == 0 && threadIdx.x == 0) {
@@ -481,6 +485,7 @@ __global__ void __launch_bounds__(kNormPrepThreads) f32_terms_nn_kernel(
     unsigned* __restrict__ or_a, unsigned* __restrict__ or_a_next, unsigned* __restrict__ or_b,
     unsigned* __restrict__ or_b_next) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ float tile[kTransTile][kTransTile + 1];
   __shared__ int redi[32];
   const int cta = blockIdx.x;
@@ -537,6 +542,7 @@ __global__ void __launch_bounds__(kPrepThreads) bf16_terms_kernel(const float* _
                                                                   int* __restrict__ nonfinite,
                                                                   unsigned* __restrict__ done) {
   pdl_launch_dependents();
+  pdl_wait_prior();  // a programmatic dependent: the previous kernel may still read these outputs or write the inputs
   __shared__ int redi[32];
   __shared__ int is_last;
   const int t = blockIdx.x;

@@ -871,7 +871,7 @@ int run_decode_group_sk(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t s
   }
   if (planes_mode)
     VMLM_TRY(launch(q8_planes_group_kernel, dim3(static_cast<unsigned>(M), static_cast<unsigned>(count)),
-                    dim3(kPrepThreads), 0, st, false, pg));
+                    dim3(kPrepThreads), 0, st, true, pg));
   // slots and counters start at zero and are left at zero by every call
   VMLM_TRY(ensure_zeroed(ctx->slots, static_cast<size_t>(tiles) * M * kTileRows * 8, st));
   VMLM_TRY(ensure_zeroed(ctx->counters, static_cast<size_t>(tiles) * 4, st));
@@ -987,7 +987,7 @@ int run_decode_group(Ctx* ctx, const Q8Call* calls, int count, cudaStream_t st, 
   }
   if (planes_mode)
     VMLM_TRY(launch(q8_planes_group_kernel, dim3(static_cast<unsigned>(M), static_cast<unsigned>(count)),
-                    dim3(kPrepThreads), 0, st, false, pg));
+                    dim3(kPrepThreads), 0, st, true, pg));
   DecParams p = {};
   p.m = M;
   p.kps = 1;
@@ -1104,11 +1104,11 @@ int run_q8(Ctx* c, const float* a, const int8_t* q, const float* scale, float* o
   if (norm_g) {
     VMLM_TRY(ensure(c->xn, static_cast<size_t>(M) * (K ? K : 1) * 4));
     float* xn = static_cast<float*>(c->xn.p);
-    VMLM_TRY(launch(q8_norm_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K),
+    VMLM_TRY(launch(q8_norm_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, true, a, static_cast<long long>(K),
                     norm_g, norm_eps, M, K, kp, xn, planes, exps, nonf));
     a = xn;
   } else {
-    VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+    VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, true, a, static_cast<long long>(K), M, K,
                     kp, planes, exps, nonf));
   }
   if (dec_ok) {
@@ -1355,7 +1355,7 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
     c->f32_nft_par ^= 1u;
     const int ntx = static_cast<int>(cdiv(N, kTransTile)), nty = kp / kTransTile;
     VMLM_TRY(launch(f32_terms_nn_kernel, dim3(static_cast<unsigned>(ntx * nty + M)), dim3(kNormPrepThreads), 0, st,
-                    false, a, static_cast<long long>(K), M, vec_a, b, static_cast<long long>(N), N, K, kp, ntx, nty,
+                    true, a, static_cast<long long>(K), M, vec_a, b, static_cast<long long>(N), N, K, kp, ntx, nty,
                     ta, tb, da, nfa, nfb, nfb_next, or_a, or_a_next, or_b, or_b_next));
     c->f32_b_from_t = true;
   } else {
@@ -1365,7 +1365,7 @@ int run_f32(Ctx* c, const float* a, const float* b, float* out, int M, int N, in
       c->f32_b_from_t = false;
     }
     const int vec_b = (K % 4 == 0) && aligned16(b);
-    VMLM_TRY(launch(f32_terms_nt_kernel, dim3(static_cast<unsigned>(M + N)), dim3(kNormPrepThreads), 0, st, false,
+    VMLM_TRY(launch(f32_terms_nt_kernel, dim3(static_cast<unsigned>(M + N)), dim3(kNormPrepThreads), 0, st, true,
                     a, static_cast<long long>(K), M, vec_a, b, static_cast<long long>(K), N, vec_b, K, kp, ta, tb, da,
                     db, nfa, nfb, or_a, or_a_next, or_b, or_b_next));
   }
@@ -1416,7 +1416,7 @@ int run_bf16(Ctx* c, const float* a, const uint16_t* b, float* out, int M, int N
   int* nonf = static_cast<int*>(c->small.p) + M;
   VMLM_TRY(ensure_zeroed(c->sync, 64, st));
   unsigned* done = static_cast<unsigned*>(c->sync.p);
-  VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+  VMLM_TRY(launch(bf16_terms_kernel, dim3(M), dim3(kPrepThreads), 0, st, true, a, static_cast<long long>(K), M, K,
                   kp, 0, terms, flags, nonf, done));
   TcParams p = {};
   p.max_terms = 1;
@@ -2954,7 +2954,7 @@ extern "C" int vmlm_gemm_nt_int8_dev_noalloc(const float* a, const int8_t* q, co
   int8_t* planes = reinterpret_cast<int8_t*>(d->base + kNaPlanesOff);
   int* exps = reinterpret_cast<int*>(d->base + kNaMetaOff);
   int* nonf = exps + kNaMaxM;
-  VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, false, a, static_cast<long long>(K), M, K,
+  VMLM_TRY(launch(q8_planes_kernel, dim3(M), dim3(kPrepThreads), 0, st, true, a, static_cast<long long>(K), M, K,
                   kp, planes, exps, nonf));
   const bool tc_ok = K > 0 && K % 16 == 0 && aligned16(q);
   if (!tc_ok) {
