@@ -450,6 +450,17 @@ int plan_norm(Ctx* ctx, int rows, int N, int K, int esz, bool int_acc, NormPlan*
 }
 
 // Diagnostics: an event pair around one GEMM launch (vmlm_profile_enable).
+// Record a profiling event on st. Inside a stream capture the record becomes
+// an event-record node of the graph (cudaEventRecordExternal), so the times
+// can be read after the graph is replayed.
+cudaError_t prof_record(cudaEvent_t e, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t r = cudaStreamIsCapturing(st, &cs);
+  if (r != cudaSuccess) return r;
+  return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal)
+                                             : cudaEventRecord(e, st);
+}
+
 int prof_begin(Ctx* c, cudaStream_t st, ProfPair* pp) {
   if (!g_prof_free.empty() && g_prof_free.back().dev == c->dev) {
     *pp = g_prof_free.back();
@@ -459,7 +470,7 @@ int prof_begin(Ctx* c, cudaStream_t st, ProfPair* pp) {
     VMLM_CUDA(cudaEventCreate(&pp->b));
     pp->dev = c->dev;
   }
-  VMLM_CUDA(cudaEventRecord(pp->a, st));
+  VMLM_CUDA(prof_record(pp->a, st));
   return VMLM_OK;
 }
 
@@ -478,7 +489,7 @@ const char* tc_mode_name(TcMode m) {
 }
 
 int prof_end(cudaStream_t st, const ProfPair& pp, const std::string& what) {
-  VMLM_CUDA(cudaEventRecord(pp.b, st));
+  VMLM_CUDA(prof_record(pp.b, st));
   g_prof_live.push_back(pp);
   g_prof_last = what;
   return VMLM_OK;

@@ -99,3 +99,36 @@ def test_graph_int8_prefill(kernels):
     c = torch.empty((m, n), device="cuda")
     _capture_and_compare(torch, [lambda st: K.gemm_i8i8_dev(x, w, s, c, None, m, n, k, stream=st)] * 2, [c])
     assert np.isfinite(c.cpu().numpy()).all()
+
+
+def test_graph_profiled_gemm_launches_report_times(kernels):
+    """Launch profiling inside a capture: the event pairs around each GEMM
+    launch become graph nodes, and after a replay every pair holds a time."""
+    import torch
+    K = kernels
+    torch.cuda.set_device(0)
+    K.init(0)
+    m, n, k = 512, 2304, 2304
+    x = _gen(torch, (m, k), 1, 1.0).to(torch.bfloat16).float().contiguous()
+    w = _gen(torch, (n, k), 2, 0.02).to(torch.bfloat16)
+    c = torch.empty((m, n), device="cuda")
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)
+    torch.cuda.synchronize()
+    ref = c.clone()
+    K.profile_enable(True)
+    K.profile_take()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(4):
+            K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)
+    K.profile_enable(False)
+    c.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    ms, launches = K.profile_take()
+    del g
+    assert launches == 4
+    assert 0.0 < ms / launches < 1.0
+    assert torch.equal(c.view(torch.int32), ref.view(torch.int32))
