@@ -113,8 +113,8 @@ __host__ __device__ inline DecSmem dec_smem_layout(int stages, int rows_b, int k
   s.recv_off = s.b_off + static_cast<uint32_t>(kbr) * rows_b * kBlockBytes;
   const uint32_t recv = c > 1 ? static_cast<uint32_t>(c) * m * dec_rows_per_cta(c) * 8 : 0;
   s.bar_off = s.recv_off + ((recv + 15u) & ~15u);
-  // full[stages], empty[stages], planes, tfull, done, drain; then the TMEM address and an abort word
-  s.meta_off = s.bar_off + (2 * stages + 4) * 8 + 16;
+  // full[stages], empty[stages], planes, tfull, done, drain, recv; then the TMEM address and an abort word
+  s.meta_off = s.bar_off + (2 * stages + 5) * 8 + 16;
   // per token: max |x| bits, non-finite flag, exponent; then the scales of the rows this CTA finishes
   s.total = s.meta_off + 3 * kDecMaxTok * 4 + kTileRows * 4 + 1024;
   return s;
@@ -154,6 +154,18 @@ __device__ __forceinline__ float dec_nonfinite_dot(const DecParams& p, int t, in
                           __ldg(p.scale + n));
 }
 
+// Issue W stage `stage`: the ops index o covers k-blocks [kb0 + o * kps, +kps)
+// of the tile's 128 rows; the copy completes on the stage's full barrier.
+__device__ __forceinline__ void dec_issue_w(const DecParams& p, const CUtensorMap* map_w, uint8_t* smem,
+                                            uint64_t* full_bar, int stage, int o, uint32_t stage_bytes, int kb0,
+                                            int tile, uint64_t pol) {
+  mbar_arrive_expect_tx(full_bar + stage, stage_bytes);
+  if (p.kps == 1)
+    tma_load_2d(smem + stage * stage_bytes, map_w, full_bar + stage, (kb0 + o) * kBlockBytes, tile * kTileRows, pol);
+  else  // k-blocks past this CTA's range are loaded (zeros past K) but not multiplied
+    tma_load_3d(smem + stage * stage_bytes, map_w, full_bar + stage, tile * kTileRows, kb0 + o * p.kps, pol);
+}
+
 template <class G>
 __global__ void __launch_bounds__(kDecThreads, 1)
     q8_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmP,
@@ -170,7 +182,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint64_t* tfull_bar = planes_bar + 1;
   uint64_t* done_bar = tfull_bar + 1;
   uint64_t* drain_bar = done_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* recv_bar = drain_bar + 1;  // clusters: the partials of the rows this CTA finishes have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_max = reinterpret_cast<int*>(smem + L.meta_off);
   int* s_bad = s_max + kDecMaxTok;
@@ -238,9 +251,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     mbar_init(tfull_bar, 1);
     mbar_init(done_bar, kDecEpiWarps);
     mbar_init(drain_bar, 1);
+    mbar_init(recv_bar, 1);
+    if (c > 1) {
+      // every CTA of the cluster sends one f64 partial per token for each row this CTA finishes
+      const int rpc = dec_rows_per_cta(c);
+      const int r_cnt = kTileRows - rank * rpc < rpc ? kTileRows - rank * rpc : rpc;
+      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(c * p.m * (r_cnt > 0 ? r_cnt : 0) * 8));
+    }
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(map_w);
+  }
+  // The first W stages go out from this thread (the producer) right after it
+  // has initialised their barriers, ahead of the CTA barrier below: the
+  // weights are the bytes the call waits for, and their first stage no longer
+  // waits for the TMEM allocation and the other warps' set-up.
+  const int pre = nops < p.stages ? nops : p.stages;
+  if (threadIdx.x == 0) {
+    const uint64_t pol = policy_evict_first();
+    for (int o = 0; o < pre; ++o) dec_issue_w(p, map_w, smem, full_bar, o, o, stage_bytes, kb0, tile, pol);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + kDecMaxTok) {
     s_max[threadIdx.x - 64] = 0;
@@ -262,13 +290,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0, last_phase = 0;
       for (int o = 0; o < nops; ++o) {
-        if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(full_bar + stage, stage_bytes);
-        if (p.kps == 1)
-          tma_load_2d(smem + stage * stage_bytes, map_w, full_bar + stage, (kb0 + o) * kBlockBytes, tile * kTileRows,
-                      pol);
-        else  // k-blocks past this CTA's range are loaded (zeros past K) but not multiplied
-          tma_load_3d(smem + stage * stage_bytes, map_w, full_bar + stage, tile * kTileRows, kb0 + o * p.kps, pol);
+        if (o >= pre) {  // the first `pre` stages went out before the CTA barrier
+          if (!mbar_wait(empty_bar + stage, phase ^ 1, p.err, abort_flag, kDevTimeoutEmpty)) break;
+          dec_issue_w(p, map_w, smem, full_bar, stage, o, stage_bytes, kb0, tile, pol);
+        }
         issued_mask |= 1u << stage;
         last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
         if (++stage == p.stages) {
@@ -495,7 +520,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int owner = row / rpc;
       const int rl = row - owner * rpc;
       const uint32_t dst = mapa_shared(smem_u32(recv), static_cast<uint32_t>(owner));
-      cluster_wait_acquire();  // phase 1: the owner CTA is running
+      const uint32_t dst_bar = mapa_shared(smem_u32(recv_bar), static_cast<uint32_t>(owner));
+      cluster_wait_acquire();  // phase 1: the owner CTA is running and its barriers are initialised
       if (trace && et == 0) trace[9] = globaltimer() - t_acc;
       #pragma unroll
       for (int jt = 0; jt < 16; ++jt) {
@@ -509,11 +535,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                               256ll * static_cast<int>(v[3 * jt + 1]) + 65536ll * static_cast<int>(v[3 * jt + 2]);
           part = static_cast<double>(a) * pow2_f64(-s_exp[t]);
         }
-        st_cluster_f64(dst + static_cast<uint32_t>(((rank * p.m + t) * rpc + rl) * 8), part);
+        st_async_cluster_f64(dst + static_cast<uint32_t>(((rank * p.m + t) * rpc + rl) * 8), part, dst_bar);
       }
       if (trace && et == 0) trace[10] = globaltimer() - t_acc;
-      cluster_arrive_release();  // phase 2: partials delivered
-      cluster_wait_acquire();
+      // the partials of this CTA's rows from every CTA of the cluster (its own
+      // included) have landed: no CTA writes into this one after this point
+      const bool got = mbar_wait(recv_bar, 0, p.err, abort_flag, kDevTimeoutAccum, false);
       if (trace && et == 0) trace[11] = globaltimer() - t_acc;
       const int total = r_cnt > 0 ? p.m * r_cnt : 0;
       for (int idx = et; idx < total; idx += kDecEpiThreads) {
@@ -523,6 +550,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (nn >= p.n) continue;
         double sum = 0.0;
         for (int q = 0; q < c; ++q) sum += recv[(q * p.m + t) * rpc + rr];
+        if (!got) sum = __longlong_as_double(0x7ff8000000000000ll);
         float r;
         if (sum != sum)
           r = dec_nonfinite_dot(p, t, nn);
@@ -537,14 +565,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (trace && et == 0) trace[6] = globaltimer();
   }
 
-  // Warps 0 and 1 take the cluster steps the epilogue warps took.
+  // Warps 0 and 1 take the cluster step the epilogue warps took.
   if (warp < 2) {
     __syncwarp();
-    if (c > 1) {
-      cluster_wait_acquire();
-      cluster_arrive_release();
-      cluster_wait_acquire();
-    }
+    if (c > 1) cluster_wait_acquire();
   }
   if (warp == 1) {
     mbar_wait(done_bar, 0, p.err, abort_flag, kDevTimeoutDrain, false);
