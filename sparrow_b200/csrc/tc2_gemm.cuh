@@ -147,9 +147,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      // weights stream once (evict first), activations are re-read by every tile
+      // Swap mode: the weights (A) stream once (evict first), the digit planes
+      // (B) are re-read by every tile. Normal modes: both operands are re-read,
+      // the activations by every column tile and a weight tile by every row
+      // tile (C5: 16), so both are kept (evict last; C5 617-628 -> 603 us
+      // against weights marked evict-first).
       const uint64_t pol_a = kSwap ? policy_evict_first() : policy_evict_last();
-      const uint64_t pol_b = kSwap ? policy_evict_last() : policy_evict_first();
+      const uint64_t pol_b = policy_evict_last();
       uint32_t issued_mask = 0, last_phase = 0;
       unsigned long long wait_empty = 0;  // trace: time waiting for free stages
       // (issuing the weight half of the first stages before this wait, as the
