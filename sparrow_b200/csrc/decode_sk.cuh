@@ -587,40 +587,67 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         continue;
       }
-      // partial segment: add the f64 partials into the tile's slot, then
-      // count it. The barriers run whatever the waits returned (after a
-      // failed wait the results are invalid and the host clears slots and
-      // counters), so every epilogue thread takes the same barriers.
+      // partial segment. One thread first reads (acquire) how many of the
+      // tile's other parts are in its slot: when all are, this CTA finishes
+      // the tile from the slot and its own partials (still in registers),
+      // without publishing them. Otherwise it adds its f64 partials into the
+      // slot and counts them; the CTA whose count completes the tile
+      // finishes it. f64 sums of the partials are exact, so the order of the
+      // additions does not change the result. The barriers run whatever the
+      // waits returned (after a failed wait the results are invalid and the
+      // host clears slots and counters), so every epilogue thread takes the
+      // same barriers.
       const long long gt = pr.tile0 + tile;
       double* slot = p.slots + gt * p.m * kTileRows;
-      if (have && n < pr.n) {
-        #pragma unroll
-        for (int jt = 0; jt < 16; ++jt) {
-          if (jt >= mt) break;
-          const int t = t0 + jt;
-          double part;
-          if (sb[t]) {
-            part = __longlong_as_double(0x7ff8000000000000ll);  // NaN marks a recompute
-          } else {
-            const long long a = static_cast<long long>(static_cast<int>(v[3 * jt])) +
-                                256ll * static_cast<int>(v[3 * jt + 1]) + 65536ll * static_cast<int>(v[3 * jt + 2]);
-            part = static_cast<double>(a) * pow2_f64(-sx[t]);
+      const long long kb_first = pr.kbase + static_cast<long long>(tile) * pr.kb;
+      const int parts = dec_sk_cta_of(kb_first + pr.kb - 1, p.kb_total, p.grid) -
+                        dec_sk_cta_of(kb_first, p.kb_total, p.grid) + 1;
+      if (et == 0) s_fin[s] = ld_acquire_gpu(p.counters + gt) == parts - 1 ? 2 : 0;
+      named_bar_sync(1, kDecEpiThreads);
+      // this thread's partial of token t0 + jt (row `row`); NaN marks a recompute
+      auto own = [&](int jt) -> double {
+        const int t = t0 + jt;
+        if (!have || sb[t]) return __longlong_as_double(0x7ff8000000000000ll);
+        const long long a = static_cast<long long>(static_cast<int>(v[3 * jt])) +
+                            256ll * static_cast<int>(v[3 * jt + 1]) + 65536ll * static_cast<int>(v[3 * jt + 2]);
+        return static_cast<double>(a) * pow2_f64(-sx[t]);
+      };
+      if (s_fin[s] == 0) {
+        if (have && n < pr.n) {
+          #pragma unroll
+          for (int jt = 0; jt < 16; ++jt) {
+            if (jt >= mt) break;
+            atomicAdd(slot + (t0 + jt) * kTileRows + row, own(jt));
           }
-          atomicAdd(slot + t * kTileRows + row, part);
         }
+        // the CTA barrier, then one acq_rel RMW by one thread: it releases the
+        // whole CTA's adds (cumulative through the barrier) and, for the
+        // finishing CTA, acquires the other CTAs' adds for the reads below
+        named_bar_sync(1, kDecEpiThreads);
+        if (et == 0) s_fin[s] = atom_add_acq_rel_gpu(p.counters + gt, 1) == parts - 1 ? 1 : 0;
+        named_bar_sync(1, kDecEpiThreads);
       }
-      // the CTA barrier, then one acq_rel RMW by one thread: it releases the
-      // whole CTA's adds (cumulative through the barrier) and, for the
-      // finishing CTA, acquires the other CTAs' adds for the reads below
-      named_bar_sync(1, kDecEpiThreads);
-      if (et == 0) {
-        const long long kb_first = pr.kbase + static_cast<long long>(tile) * pr.kb;
-        const int parts = dec_sk_cta_of(kb_first + pr.kb - 1, p.kb_total, p.grid) -
-                          dec_sk_cta_of(kb_first, p.kb_total, p.grid) + 1;
-        s_fin[s] = atom_add_acq_rel_gpu(p.counters + gt, 1) == parts - 1 ? 1 : 0;
-      }
-      named_bar_sync(1, kDecEpiThreads);
-      if (s_fin[s]) {
+      if (s_fin[s] == 2) {
+        // the last part: each thread finishes its own row's tokens
+        if (n < pr.n) {
+          #pragma unroll
+          for (int jt = 0; jt < 16; ++jt) {
+            if (jt >= mt) break;
+            const int t = t0 + jt;
+            const int idx = t * kTileRows + row;
+            const double sum = __ldcg(slot + idx) + own(jt);
+            float r;
+            if (sum != sum)
+              r = nonfinite_dot_q8(pr.x + static_cast<long long>(t) * pr.ldx, pr.w + static_cast<long long>(n) * pr.k,
+                                   pr.k, sc_row);
+            else
+              r = __fmul_rn(__double2float_rn(sum), sc_row);
+            pr.out[static_cast<long long>(t) * pr.ldo + n] = r;
+            slot[idx] = 0.0;
+          }
+        }
+        if (et == 0) p.counters[gt] = 0;
+      } else if (s_fin[s] == 1) {
         for (int idx = et; idx < p.m * kTileRows; idx += kDecEpiThreads) {
           const int t = idx / kTileRows;
           const int nn = tile * kTileRows + (idx - t * kTileRows);

@@ -341,6 +341,12 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
   return old;
 }
 
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
