@@ -110,7 +110,8 @@ CASES = {"c1": ("q8", 1, 5760, 2304), "c2": ("bf16", M2, N2, K2), "c2f32": ("bf1
          "c4m64small": ("q8", 64, 16384, 2304), "c3q_m32": ("q8", 32, 2304, 2304), "c3d_m32": ("q8", 32, 2304, 5760),
          "c3g_m32": ("q8", 32, 5760, 2304), "c3b_m1": ("q8batch", 1, 0, 0), "c3b_m2": ("q8batch", 2, 0, 0),
          "c3b_m8": ("q8batch", 8, 0, 0), "c3b_m32": ("q8batch", 32, 0, 0),
-         "f32nt": ("f32nt", M2, N2, K2), "f32nn": ("f32nn", M2, N2, K2)}
+         "f32nt": ("f32nt", M2, N2, K2), "f32nn": ("f32nn", M2, N2, K2),
+         "i4_m1": ("int4", 1, 5760, 2304), "i4lm": ("int4", 1, 122753, 2304)}
 
 
 def run_case(args):
@@ -145,6 +146,15 @@ def run_case(args):
                 x = x.to(torch.bfloat16).float().contiguous()
             w = gen((n, k), 1 + 1000 * r, 0.02).to(torch.bfloat16)
             return (lambda: K.gemm_nt_bf16_dev(x, w, c, m, n, k, stream=st)), 4 * m * k + 2 * n * k
+        if kind == "int4":
+            # int4 with a scale per 32 columns (tests/src/quant.rs), weights with outlier channels
+            x = gen((m, k), 12, 0.5)
+            w = gen((n, k), 11 + 1000 * r, 1.0 / float(np.sqrt(k)))
+            w[:, ::64] *= 12.0
+            packed, s4 = quantise_int4_groups(w, 32)
+            del w
+            return ((lambda: K.gemm_nt_int4_gs_dev(x, packed, s4, c, m, n, k, 32, 0, stream=st)),
+                    packed.numel() + 4 * s4.numel())
         if kind in ("f32nt", "f32nn"):
             x = gen((m, k), 0 + 1000 * r, 1.0)
             w = gen((k, n) if kind == "f32nn" else (n, k), 1 + 1000 * r, 0.02)
@@ -946,6 +956,18 @@ def bench_variants(K, dist, rank, world, flush, pk):
             entry["cpu_oracle"] = {"value": 2 * m * n * k / best / 1e9, "unit": "GFLOP/s", "cores": 1, "kind": "port",
                                    "sample": "best of 20 runs of the restated AVX2 gemm_nt_int4_gs "
                                              "(tests/src/quant.rs:298-362), single thread as shipped"}
+        if n * k >= (1 << 20):
+            # steps back to back over rotating weight copies (larger than twice L2), captured in a graph
+            steps = [step]
+            for r in range(1, copies_for(nbytes)):
+                wr = gen((n, k), 11 + 100 * r, 1.0 / float(np.sqrt(k)))
+                wr[:, ::64] *= 12.0
+                pr, sr = quantise_int4_groups(wr, 32)
+                steps.append(lambda pr=pr, sr=sr: K.gemm_nt_int4_gs_dev(a, pr, sr, c, m, n, k, 32, 0, stream=st))
+                del wr
+            tr = time_rotating(steps, 60, 3, dist)
+            entry["rot"] = {"step_us": tr * 1e3, "frac_hbm": nbytes / tr / 1e6 / hbm, "copies": len(steps)}
+            del steps
         res[f"V_int4_g32_{m}x{n}x{k}"] = entry
         q, s, idx = quantise_int8_outliers(w, 3.0)
         wo = torch.empty((n, idx.numel()), dtype=torch.float32, device="cuda")
@@ -964,6 +986,20 @@ def bench_variants(K, dist, rank, world, flush, pk):
             entry["cpu_oracle"] = {"value": 2 * m * n * k / best / 1e9, "unit": "GFLOP/s", "cores": 1, "kind": "port",
                                    "sample": "best of 20 runs of the restated gemm_nt_int8_outlier "
                                              "(tests/src/quant.rs:524-565), single thread as shipped"}
+        if n * k >= (1 << 20):
+            steps = [step]
+            for r in range(1, copies_for(nbytes)):
+                wr = gen((n, k), 11 + 100 * r, 1.0 / float(np.sqrt(k)))
+                wr[:, ::64] *= 12.0
+                qr, sr, ir = quantise_int8_outliers(wr, 3.0)
+                wor = torch.empty((n, ir.numel()), dtype=torch.float32, device="cuda")
+                K.gather_columns_dev(wr, ir, ir.numel(), n, k, wor, stream=st)
+                steps.append(lambda qr=qr, sr=sr, ir=ir, wor=wor: K.gemm_nt_int8_outlier_dev(
+                    a, qr, sr, wor, ir, ir.numel(), c, m, n, k, compact=True, stream=st))
+                del wr
+            tr = time_rotating(steps, 60, 3, dist)
+            entry["rot"] = {"step_us": tr * 1e3, "frac_hbm": nbytes / tr / 1e6 / hbm, "copies": len(steps)}
+            del steps
         res[f"V_int8_outlier_{m}x{n}x{k}"] = entry
         del w, a, c, packed, s4, q, s, idx, wo
     return res
@@ -1061,6 +1097,13 @@ def make_summary(value, ms_per_step, eager_ms, flushed_ms, roofline, e2e, config
                   "ingress_GBps_over_call": r4(4.0 * 4096 * 28672 * (1 - 1 / world) / e["rot"]["fused_allgather_us"]
                                                / 1e3)})
     s["C5"] = d
+    var = {}
+    for name, e in configs.items():
+        if name.startswith("V_") and "rot" in e:
+            var[name[2:]] = {"us": r4(e["rot"]["step_us"]), "frac_hbm": r4(e["rot"]["frac_hbm"]),
+                             "flushed_us": r4(e["step_us"])}
+    if var:
+        s["variants"] = var
     if check:
         s["sharded_check"] = dict(check, all_ok=all(v["ok"] for v in check.values()))
     return s
