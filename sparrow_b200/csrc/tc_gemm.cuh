@@ -1097,6 +1097,55 @@ __global__ void peer_signal_kernel(unsigned* inbox) {
   }
 }
 
+// Row-sharded calls on more than two GPUs: push rows [0, rows) x columns
+// [0, cols) of this rank's slice of C (src, row pitch ld floats) into the same
+// place of every other rank's C (dst.p[q], q != self) with plain stores over
+// NVLink, a grid-stride loop over 16-byte vectors (vec) or single floats. It
+// runs beside the GEMM's next row chunk (a few registers, no shared memory, so
+// its CTAs fit next to the GEMM's). Then every rank's inbox gets one count from
+// peer_signal_all_kernel.
+struct PeerDst {
+  float* p[kMaxPeers];
+  unsigned* inbox[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(256) peer_push_kernel(const float* __restrict__ src, long long ld, int rows, int cols,
+                                                        const __grid_constant__ PeerDst dst, int npeers, int self,
+                                                        int vec) {
+  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int c4 = cols / 4;
+    const long long total = static_cast<long long>(rows) * c4;
+    for (long long i = tid; i < total; i += nth) {
+      const long long r = i / c4;
+      const long long off = r * ld + (i - r * c4) * 4;
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + off));
+      for (int q = 0; q < npeers; ++q)
+        if (q != self) *reinterpret_cast<float4*>(dst.p[q] + off) = v;
+    }
+  } else {
+    const long long total = static_cast<long long>(rows) * cols;
+    for (long long i = tid; i < total; i += nth) {
+      const long long r = i / cols;
+      const long long off = r * ld + (i - r * cols);
+      const float v = __ldcg(src + off);
+      for (int q = 0; q < npeers; ++q)
+        if (q != self) dst.p[q][off] = v;
+    }
+  }
+}
+
+// One count in every other rank's inbox, after all of this rank's stores into
+// their C (the kernels before it in the stream) are visible to them.
+__global__ void peer_signal_all_kernel(const __grid_constant__ PeerDst dst, int npeers, int self) {
+  const int q = static_cast<int>(threadIdx.x);
+  if (q < npeers && q != self) {
+    fence_sc_sys();
+    red_add_release_sys(dst.inbox[q], 1u);
+  }
+}
+
 __global__ void peer_wait_kernel(const unsigned* inbox, unsigned target, int* err) {
   if (threadIdx.x != 0) return;
   const unsigned long long t0 = globaltimer();
