@@ -209,3 +209,59 @@ def test_missing_rank_makes_the_bounded_wait_run_out_and_the_next_call_is_correc
         assert rc == 0
         kernels.sync(st)
         assert oracle.max_rel_err(c[0].cpu().numpy(), ref) <= TIGHT_Q8
+
+
+@pytest.mark.parametrize("kind,m,n,k", [("i8i8", 512, 12288, 1024), ("q8", 64, 98304, 1024)])
+def test_four_rank_forms_push_one_rank_slice_to_every_peer(kernels, oracle, kind, m, n, k):
+    """The forms used on more than two GPUs (int8 x int8 with a large output:
+    row chunks pushed to every peer by peer_push_kernel; Q8: the fused
+    epilogue), run on one GPU for rank 1 of a four-rank group whose C buffers
+    and inboxes are local. The other ranks' counts are added to rank 1's inbox
+    before each call, on the call's stream, so the call's bounded wait ends
+    without waiting on any other launch. Every rank's C must then hold rank 1's
+    column slice: bit for bit for int8 x int8, within the Q8 bound for Q8; the
+    rest of each C is untouched. Two calls in a row (the inbox count advances)."""
+    import ctypes
+    import torch
+    from sparrow_b200._lib import lib
+    from sparrow_b200.sharded import shard_rows
+    world, rank = 4, 1
+    r0, r1 = shard_rows(n, world, rank)
+    if kind == "i8i8":
+        x = oracle.fill_int8(m * k, 90).reshape(m, k)
+        w = oracle.fill_int8((r1 - r0) * k, 91).reshape(r1 - r0, k)
+        s = np.abs(oracle.fill_normal(r1 - r0, 92, 0.02)) + np.float32(1e-3)
+        ref, _ = oracle.gemm_i8i8(x, w, s, nt=os.cpu_count() or 1)
+    else:
+        x = oracle.fill_normal(m * k, 93, 1.0).reshape(m, k)
+        w, s = oracle.quant_int8(oracle.fill_normal((r1 - r0) * k, 94, 0.02).reshape(r1 - r0, k))
+        ref = oracle.gemm_nt_int8(x, w, s, nt=os.cpu_count() or 1)
+    dx, dw, ds = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda()
+    c = [torch.zeros((m, n), dtype=torch.float32, device="cuda") for _ in range(world)]
+    inbox = [torch.zeros(4, dtype=torch.int32, device="cuda") for _ in range(world)]
+    for b in inbox:
+        assert lib().vmlm_sharded_reset(ctypes.c_void_p(b.data_ptr())) == 0
+    c_ptrs = (ctypes.c_void_p * world)(*[t.data_ptr() for t in c])
+    in_ptrs = (ctypes.c_void_p * world)(*[t.data_ptr() for t in inbox])
+    st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream or 1)
+    fn = lib().vmlm_sharded_gemm_i8i8_dev if kind == "i8i8" else lib().vmlm_sharded_gemm_nt_int8_dev
+    try:
+        for _ in range(2):
+            for t in c:
+                t.zero_()
+            inbox[rank][0] += world - 1  # the other ranks' counts for this call
+            rc = fn(ctypes.c_void_p(dx.data_ptr()), ctypes.c_void_p(dw.data_ptr()), ctypes.c_void_p(ds.data_ptr()),
+                    c_ptrs, in_ptrs, rank, world, m, n, k, sp)
+            assert rc == 0
+            kernels.sync(st)
+            for q in range(world):
+                got = c[q].cpu().numpy()
+                if kind == "i8i8":
+                    assert np.array_equal(got[:, r0:r1].view(np.uint32), ref.view(np.uint32)), q
+                else:
+                    assert oracle.max_rel_err(got[:, r0:r1], ref) <= TIGHT_Q8, q
+                assert np.all(got[:, :r0] == 0) and np.all(got[:, r1:] == 0), q
+    finally:
+        for b in inbox:
+            lib().vmlm_sharded_reset(ctypes.c_void_p(b.data_ptr()))
