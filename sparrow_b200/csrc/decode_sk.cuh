@@ -547,6 +547,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const float sc_row = dec_sk_pick(sc_w, s);
       const float sc_fin = dec_sk_pick(sc_f, s);
       uint32_t v[48];
+      // Split tile: one thread reads (acquire) how many of the tile's other
+      // parts are in its slot, before this segment's accumulator is ready.
+      // When all are (usually this CTA's last segment, whose other parts sit
+      // at the start of the next CTAs' ranges), their sum is final and each
+      // thread loads its row's slot values while the MMAs finish.
+      const long long gt = pr.tile0 + tile;
+      double* slot = p.slots + gt * p.m * kTileRows;
+      const long long kb_first = pr.kbase + static_cast<long long>(tile) * pr.kb;
+      const int parts = dec_sk_cta_of(kb_first + pr.kb - 1, p.kb_total, p.grid) -
+                        dec_sk_cta_of(kb_first, p.kb_total, p.grid) + 1;
+      double pre[16];
+      if (!whole) {
+        if (et == 0) s_fin[s] = ld_acquire_gpu(p.counters + gt) == parts - 1 ? 2 : 0;
+        named_bar_sync(1, kDecEpiThreads);
+        #pragma unroll
+        for (int jt = 0; jt < 16; ++jt)
+          pre[jt] = (s_fin[s] == 2 && jt < mt && n < pr.n) ? __ldcg(slot + (t0 + jt) * kTileRows + row) : 0.0;
+      }
       const bool have = all && mbar_wait(tfull_bar + s, 0, p.err, abort_flag, kDevTimeoutAccum, false);
       all = have;
       tc_fence_after();
@@ -587,23 +605,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         continue;
       }
-      // partial segment. One thread first reads (acquire) how many of the
-      // tile's other parts are in its slot: when all are, this CTA finishes
-      // the tile from the slot and its own partials (still in registers),
-      // without publishing them. Otherwise it adds its f64 partials into the
-      // slot and counts them; the CTA whose count completes the tile
-      // finishes it. f64 sums of the partials are exact, so the order of the
-      // additions does not change the result. The barriers run whatever the
-      // waits returned (after a failed wait the results are invalid and the
-      // host clears slots and counters), so every epilogue thread takes the
-      // same barriers.
-      const long long gt = pr.tile0 + tile;
-      double* slot = p.slots + gt * p.m * kTileRows;
-      const long long kb_first = pr.kbase + static_cast<long long>(tile) * pr.kb;
-      const int parts = dec_sk_cta_of(kb_first + pr.kb - 1, p.kb_total, p.grid) -
-                        dec_sk_cta_of(kb_first, p.kb_total, p.grid) + 1;
-      if (et == 0) s_fin[s] = ld_acquire_gpu(p.counters + gt) == parts - 1 ? 2 : 0;
-      named_bar_sync(1, kDecEpiThreads);
+      // partial segment. When every other part was counted (s_fin 2), this
+      // CTA finishes the tile from the slot values loaded above and its own
+      // partials (in registers), without publishing them. Otherwise it adds
+      // its f64 partials into the slot and counts them; the CTA whose count
+      // completes the tile finishes it. f64 sums of the partials are exact,
+      // so the order of the additions does not change the result. The
+      // barriers run whatever the waits returned (after a failed wait the
+      // results are invalid and the host clears slots and counters), so every
+      // epilogue thread takes the same barriers.
       // this thread's partial of token t0 + jt (row `row`); NaN marks a recompute
       auto own = [&](int jt) -> double {
         const int t = t0 + jt;
@@ -635,7 +645,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (jt >= mt) break;
             const int t = t0 + jt;
             const int idx = t * kTileRows + row;
-            const double sum = __ldcg(slot + idx) + own(jt);
+            const double sum = pre[jt] + own(jt);
             float r;
             if (sum != sum)
               r = nonfinite_dot_q8(pr.x + static_cast<long long>(t) * pr.ldx, pr.w + static_cast<long long>(n) * pr.k,
