@@ -438,12 +438,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           const int kk = (qi - t * qpt) * 4;  // offset in this CTA's range
           const float4 v = s_bad[t] ? make_float4(0.f, 0.f, 0.f, 0.f) : g[i];
           const int e = s_exp[t];
-          int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
-          q8_digits(v.x, e, a0, a1, a2);
-          q8_digits(v.y, e, b0, b1, b2);
-          q8_digits(v.z, e, c0, c1, c2);
-          q8_digits(v.w, e, f0, f1, f2);
-          const uint32_t w3[3] = {pack4(a0, b0, c0, f0), pack4(a1, b1, c1, f1), pack4(a2, b2, c2, f2)};
+          uint32_t w3[3];
+          q8_digits4(v, e, w3[0], w3[1], w3[2]);
           const int j = kk >> 7, b = kk & 127;
           uint8_t* blk = planes + j * p.rows_b * kBlockBytes;
           #pragma unroll

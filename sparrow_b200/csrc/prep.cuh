@@ -83,6 +83,27 @@ __device__ __forceinline__ void q8_digits(float x, int e, int& d0, int& d1, int&
   d2 = (X1 - d1) >> 8;
 }
 
+// The three digit planes of four values at once, packed (byte j of plane p =
+// digit p of element j, as pack4 of q8_digits). With X = rint(x * 2^e),
+// |X| <= 2^22, Y = X + 0x808080 is positive and its bytes 0, 1, 2 are the
+// balanced digits d0, d1, d2 plus 128 each (the carries of the balanced form
+// are those of adding 128 to each byte), so each plane byte is a byte of Y
+// with its top bit flipped: three byte permutes per plane pair instead of
+// the digit arithmetic per element.
+__device__ __forceinline__ void q8_digits4(float4 v, int e, uint32_t& p0, uint32_t& p1, uint32_t& p2) {
+  const uint32_t ya = static_cast<uint32_t>(__float2int_rn(scale_pow2(v.x, e)) + 0x808080);
+  const uint32_t yb = static_cast<uint32_t>(__float2int_rn(scale_pow2(v.y, e)) + 0x808080);
+  const uint32_t yc = static_cast<uint32_t>(__float2int_rn(scale_pow2(v.z, e)) + 0x808080);
+  const uint32_t yd = static_cast<uint32_t>(__float2int_rn(scale_pow2(v.w, e)) + 0x808080);
+  const uint32_t ab01 = __byte_perm(ya, yb, 0x5140);  // a0 b0 a1 b1
+  const uint32_t cd01 = __byte_perm(yc, yd, 0x5140);  // c0 d0 c1 d1
+  const uint32_t ab2 = __byte_perm(ya, yb, 0x0062);   // a2 b2 . .
+  const uint32_t cd2 = __byte_perm(yc, yd, 0x0062);   // c2 d2 . .
+  p0 = __byte_perm(ab01, cd01, 0x5410) ^ 0x80808080u;
+  p1 = __byte_perm(ab01, cd01, 0x7632) ^ 0x80808080u;
+  p2 = __byte_perm(ab2, cd2, 0x5410) ^ 0x80808080u;
+}
+
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return (static_cast<uint32_t>(a) & 255u) | ((static_cast<uint32_t>(b) & 255u) << 8) |
          ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
@@ -141,15 +162,8 @@ __device__ __forceinline__ void q8_planes_row(const float* __restrict__ x, long 
   for (int i = 0; i < kPrepVec / 4; ++i) {
     const int ch = threadIdx.x + i * blockDim.x;
     if (ch < nchunk) {
-      int a0, a1, a2, b0, b1, b2, c0, c1, c2, f0, f1, f2;
       const float4 v = bad ? make_float4(0.f, 0.f, 0.f, 0.f) : reg[i];
-      q8_digits(v.x, e, a0, a1, a2);
-      q8_digits(v.y, e, b0, b1, b2);
-      q8_digits(v.z, e, c0, c1, c2);
-      q8_digits(v.w, e, f0, f1, f2);
-      p0[ch] = pack4(a0, b0, c0, f0);
-      p1[ch] = pack4(a1, b1, c1, f1);
-      p2[ch] = pack4(a2, b2, c2, f2);
+      q8_digits4(v, e, p0[ch], p1[ch], p2[ch]);
     }
   }
   for (int ch = threadIdx.x + kPrepVec / 4 * blockDim.x; ch < nchunk; ch += blockDim.x) {
